@@ -1,0 +1,105 @@
+// sym_b200 -- one device's execution context: two non-blocking streams (copy
+// engine and compute), the HBM ring, a parameter buffer, events, and the
+// sticky error state of the reference's CopyBackend contract
+// (libreloc/include/reloc/Backend.h:34-89: failed()/error(), quiesce(),
+// waitStream()). All CUDA work goes through the thin C-ABI layer
+// (include/sb_cuda.h); this header pulls in no CUDA headers.
+#ifndef SYM_B200_RELOC_CUDABACKEND_H
+#define SYM_B200_RELOC_CUDABACKEND_H
+
+#include <cstddef>
+#include <cstdint>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+namespace reloc {
+
+enum class QueueCompletion { Complete, Unknown };
+
+class CudaBackend {
+public:
+  /// Create a context on `device` (made current for the calling thread).
+  static std::unique_ptr<CudaBackend> create(int device, std::string &error);
+  ~CudaBackend();
+  CudaBackend(const CudaBackend &) = delete;
+  CudaBackend &operator=(const CudaBackend &) = delete;
+
+  int device() const { return device_; }
+  bool failed() const { return failed_; }
+  const std::string &error() const { return error_; }
+  /// Record a failure (first one wins). Returns false for call chaining.
+  bool fail(const std::string &what, int status);
+  /// Make this backend's device current on the calling thread.
+  bool activate();
+
+  void *copyStream() const { return copy_; }
+  void *computeStream() const { return compute_; }
+
+  /// Order both private streams after the work already on `external`.
+  bool waitStream(const void *external);
+  /// Order `external` after everything enqueued so far on the private streams.
+  bool signalStream(const void *external);
+  /// Block until all enqueued work completed.
+  QueueCompletion quiesce();
+
+  /// HBM ring of `slots` buffers of `slotBytes` (grown, never shrunk).
+  bool ensureRing(int slots, size_t slotBytes);
+  void *slot(int i) const { return ring_[static_cast<size_t>(i)]; }
+  void *slotReady(int i) const { return ready_[static_cast<size_t>(i)]; }
+  void *slotFree(int i) const { return free_[static_cast<size_t>(i)]; }
+  int slots() const { return static_cast<int>(ring_.size()); }
+  size_t slotBytes() const { return slotBytes_; }
+
+  /// Device scratch for staged sources (whole-source route), grown on demand.
+  void *staging(size_t bytes);
+  /// Device parameter buffer (grown on demand).
+  void *params(size_t bytes);
+  /// A device status word (channel range errors) and its pinned readback.
+  int32_t *statusWord() const { return status_; }
+  int32_t *statusHost() const { return statusHost_; }
+
+  void *stagingReady() const { return stagingReady_; }
+  void *stagingFree() const { return stagingFree_; }
+  void *doneEvent() const { return done_; }
+  void *startEvent() const { return start_; }
+  void *stopEvent() const { return stop_; }
+
+  size_t deviceBytes() const;
+  uint64_t copyCalls = 0;
+  uint64_t eventRecords = 0;
+  uint64_t eventWaits = 0;
+  uint64_t callerWaits = 0;
+  uint64_t kernelLaunches = 0;
+
+  /// Measured route choice per plan class: key -> seconds per byte of each
+  /// route (negative = not yet measured).
+  struct RouteStats {
+    double dmaSecondsPerByte = -1, zeroCopySecondsPerByte = -1;
+  };
+  std::map<std::string, RouteStats> routeStats;
+  std::mutex mutex; // one request at a time per context
+
+private:
+  CudaBackend() = default;
+  int device_ = -1;
+  bool failed_ = false;
+  std::string error_;
+  void *copy_ = nullptr, *compute_ = nullptr;
+  void *done_ = nullptr, *start_ = nullptr, *stop_ = nullptr, *fence_ = nullptr;
+  void *stagingReady_ = nullptr, *stagingFree_ = nullptr;
+  std::vector<void *> ring_, ready_, free_;
+  size_t slotBytes_ = 0;
+  void *staging_ = nullptr;
+  size_t stagingBytes_ = 0;
+  void *params_ = nullptr;
+  size_t paramBytes_ = 0;
+  int32_t *status_ = nullptr;
+  int32_t *statusHost_ = nullptr;
+};
+
+} // namespace reloc
+
+#endif

@@ -1,0 +1,160 @@
+// sym_b200 -- plan-driven typed dispatch onto the B200 rows.
+//
+// Same entry points, request/template/report types and policy vocabulary as
+// the reference's libreloc/include/reloc/Dispatch.h:100-271
+// (queryCapability :100, prepareDispatchTemplate/prepareDispatch :170-175,
+// executeDispatch :269). The capability table is new: every supported typed
+// plan is eligible for the B200 rows, which do all value work on the GPU and
+// fuse it into the host->device transfer:
+//   b200_fused_h2d            route chosen per plan (Route::Auto or options)
+//   b200_fused_h2d@dma_ring   raw source chunks DMA'd into an HBM ring, then
+//                             the fused transform kernel per chunk
+//   b200_fused_h2d@zero_copy  the fused kernel reads pinned host memory
+// The reference's CPU rows (cpu_reference, cpu_stages_cuda_stages@k) and its
+// legacy CUDA rows are listed as excluded with a reason: no supported plan
+// executes on the CPU here.
+#ifndef SYM_B200_RELOC_DISPATCH_H
+#define SYM_B200_RELOC_DISPATCH_H
+
+#include "reloc/Transfer.h"
+#include "reloc/TypedExecute.h"
+
+#include <cstdint>
+#include <memory>
+#include <optional>
+#include <string>
+#include <variant>
+#include <vector>
+
+namespace reloc {
+
+class CudaBackend;
+namespace b200 {
+struct Lowered;
+}
+
+namespace dispatch {
+
+enum class Policy { OriginalCpu, Auto };
+
+inline constexpr const char *kB200FusedH2D = "b200_fused_h2d";
+inline constexpr const char *kCpuReference = "cpu_reference";
+inline constexpr const char *kCpuStagesCudaStages = "cpu_stages_cuda_stages";
+inline constexpr const char *kCudaStagesThenCpu = "cuda_stages_then_cpu";
+inline constexpr const char *kCudaDequantRelocate = "cuda_dequant_relocate";
+inline constexpr const char *kCudaRelocateF32 = "cuda_relocate_f32";
+
+struct Implementation {
+  std::string id;
+  std::string variant; // "", "dma_ring" or "zero_copy"
+  uint32_t wireBoundary = 0;
+  bool wireResultLayout = false;
+  int64_t wireBytes = 0;
+  int64_t deviceTempBytes = 0;
+  std::string method;
+  std::string label() const { return variant.empty() ? id : id + "@" + variant; }
+};
+
+struct Exclusion {
+  std::string id;
+  std::string reason;
+};
+
+struct Capability {
+  std::vector<Implementation> eligible;
+  std::vector<Exclusion> excluded;
+};
+
+/// Pure: which rows can run `program` in `direction` with a CUDA device end.
+Capability queryCapability(const typed::Program &program, TransferDirection direction, bool cuda);
+
+struct Report {
+  std::string implementation;
+  std::string policy;
+  std::string placementReason;
+  std::string method;
+  uint32_t wireBoundary = 0;
+  int64_t sourceBytes = 0;
+  int64_t wireBytes = 0;
+  int64_t destinationBytes = 0;
+  int64_t parameterBytes = 0;
+  int64_t payloadBytesTransferred = 0;
+  int64_t deviceTempBytes = 0;
+  uint32_t artifactVersion = 1;
+  bool executed = false;
+  std::string hostPipeline = "not_applicable";
+  std::string hostKernel = "not_applicable";
+  size_t hostChunks = 0, hostChunkBytes = 0, hostBuffers = 0;
+  // B200 additions
+  std::string route;        // "dma_ring", "zero_copy" or "staged"
+  std::string deviceKernel; // "contiguous", "transpose" or "generic"
+  uint64_t kernelLaunches = 0;
+  uint64_t copyCalls = 0;
+};
+
+struct Options {
+  Policy policy = Policy::Auto;
+  int threads = 8;
+  bool cuda = false;
+  std::string implementation; // explicit row label
+};
+
+struct DispatchRequest {
+  typed::Program program;
+  BufferView source;
+  BufferView destination;
+  TransferDirection direction = TransferDirection::HostToDevice;
+  Implementation selected;
+  Report report;
+  bool consumed = false;
+  bool executing = false;
+  /// The program lowered to device kernels (shared with the template).
+  std::shared_ptr<const b200::Lowered> lowered;
+};
+
+struct Selection {
+  Implementation row;
+  std::string policy;
+  std::string reason;
+};
+
+struct DispatchTemplate {
+  typed::Program program;
+  Capability capability;
+  Selection selection;
+  TransferDirection direction = TransferDirection::HostToDevice;
+  bool cuda = false;
+  std::shared_ptr<const b200::Lowered> lowered;
+};
+
+std::variant<Selection, TransferError> selectImplementation(const typed::Program &, TransferDirection,
+                                                            const Options &);
+std::variant<DispatchTemplate, TransferError> prepareDispatchTemplate(const TypedBoundPlan &, TransferDirection,
+                                                                      const Options &);
+std::variant<DispatchRequest, TransferError> prepareDispatch(const DispatchTemplate &, const BufferView &source,
+                                                             const BufferView &destination);
+std::variant<DispatchRequest, TransferError> prepareDispatch(const TypedBoundPlan &plan, const BufferView &source,
+                                                             const BufferView &destination,
+                                                             TransferDirection direction, const Options &options);
+
+/// Run the selected row on `backend` (one device's streams, HBM ring and
+/// parameter buffers). Blocks until this request's work completed unless
+/// options.asyncCompletion. Marks the request consumed before launching.
+std::optional<TransferError> executeDispatch(DispatchRequest &request, CudaBackend &backend,
+                                             const TransferOptions &options);
+
+/// Execute the physical row window [rowBegin, rowEnd) of axis 0 of the
+/// padded result (a shard of the result, e.g. one GPU's rows of a sharded
+/// weight fetch). `dst` is the window's own storage; channels keep their
+/// global coordinates (the reference's executeHostChunk contract,
+/// libreloc/include/reloc/TypedExecute.h:160-170). `hostSource` selects the
+/// H2D routes; otherwise `src` is already in this device's memory and only
+/// the transform runs.
+std::optional<TransferError> executeWindow(const DispatchTemplate &tmpl, CudaBackend &backend, const void *src,
+                                           bool hostSource, void *dst, int64_t rowBegin, int64_t rowEnd,
+                                           const TransferOptions &options, Report &report);
+
+} // namespace dispatch
+} // namespace reloc
+
+#endif

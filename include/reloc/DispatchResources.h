@@ -1,0 +1,71 @@
+// sym_b200 -- typed contexts: a bounded, thread-safe pool of per-device
+// execution contexts (streams, HBM ring, parameter buffers).
+//
+// Interface of the reference's dispatch::Resources
+// (libreloc/include/reloc/DispatchResources.h:9-103; execute :74-86): leases
+// by device, FIFO admission per device, sticky quarantine after a failure
+// whose completion is unknown, stats(), clear(), close(). A context here is a
+// CudaBackend; there are no host worker pools because no plan runs on the CPU.
+#ifndef SYM_B200_RELOC_DISPATCHRESOURCES_H
+#define SYM_B200_RELOC_DISPATCHRESOURCES_H
+
+#include "reloc/CudaBackend.h"
+#include "reloc/Dispatch.h"
+
+#include <cstddef>
+#include <cstdint>
+#include <functional>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <optional>
+
+namespace reloc {
+namespace dispatch {
+
+struct ResourceStats {
+  uint64_t requests = 0, hits = 0, contexts = 0;
+  uint64_t deviceAllocations = 0, frees = 0;
+  size_t retainedBytes = 0, deviceBytes = 0;
+  uint64_t copyCalls = 0, eventRecords = 0, eventWaits = 0, callerWaits = 0, kernelLaunches = 0;
+  bool closed = false, quarantined = false;
+  size_t retainedLimit = 0, liveLimit = 0;
+  unsigned contextLimit = 0;
+};
+
+class Resources {
+public:
+  explicit Resources(size_t maxRetainedBytes = size_t(256) << 20, size_t maxLiveBytes = 0, unsigned maxContexts = 8);
+  ~Resources();
+  Resources(const Resources &) = delete;
+  Resources &operator=(const Resources &) = delete;
+
+  /// Lease the context of `device` and run the request on it.
+  TransferOutcome execute(DispatchRequest &request, int device, int streams, const TransferOptions &options,
+                          std::shared_ptr<void> owners);
+  /// Run `fn` with the leased context of `device` (window/device executions).
+  TransferOutcome withContext(int device, const std::function<std::optional<TransferError>(CudaBackend &)> &fn);
+
+  ResourceStats stats() const;
+  std::optional<TransferError> clear();
+  std::optional<TransferError> close();
+
+private:
+  struct Slot {
+    std::unique_ptr<CudaBackend> backend;
+    std::mutex lease;
+  };
+  std::optional<TransferError> acquire(int device, Slot *&slot);
+  mutable std::mutex mutex_;
+  std::map<int, std::unique_ptr<Slot>> slots_;
+  size_t maxRetained_, maxLive_;
+  unsigned maxContexts_;
+  bool closed_ = false, quarantined_ = false;
+  uint64_t requests_ = 0, hits_ = 0, created_ = 0;
+  std::vector<std::shared_ptr<void>> quarantinedOwners_;
+};
+
+} // namespace dispatch
+} // namespace reloc
+
+#endif

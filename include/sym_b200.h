@@ -1,0 +1,141 @@
+/* sym_b200 -- the drop-in C-ABI of the B200 typed relocation executor
+ * (libsb_runtime.so).
+ *
+ * Plain pointers, sizes, POD structs and opaque handles; no CUDA, C++ or
+ * torch type crosses it. Each entry point replaces one call of the
+ * reference's Python binding `pyreloc` (libreloc/python/Py*.cpp), which is
+ * what the reference's FFI binds for this path; the Python mirror in
+ * sym_b200/pyreloc.py binds these through ctypes. Status: 0 = success,
+ * otherwise non-zero with `err` filled (a stable code from the reference's
+ * vocabulary, a message and, for decode errors, the byte offset).
+ *
+ * Ownership: handles are released with their *_free function. Parameter
+ * bytes are copied at bind time. Buffers passed to the execute calls are
+ * borrowed for the call (or, with async completion, until the caller's
+ * stream passes the recorded completion).
+ */
+#ifndef SYM_B200_H
+#define SYM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct sb_plan sb_plan;           /* a decoded wire v0 or v1 plan */
+typedef struct sb_bound sb_bound;         /* a bound plan (typed: also its checked program) */
+typedef struct sb_template sb_template;   /* a prepared dispatch template (no buffers) */
+typedef struct sb_request sb_request;     /* a single-use prepared request */
+typedef struct sb_resources sb_resources; /* typed contexts (per-device streams, HBM ring) */
+
+typedef struct {
+  char code[48];     /* e.g. "decode_error", "bind_error", "plan_mismatch" */
+  char message[456];
+  int64_t offset;    /* byte offset of a decode error, else -1 */
+} sb_error;
+
+/* A caller buffer (reference BufferView, libreloc/include/reloc/Transfer.h:47-56). */
+typedef struct {
+  uint64_t base;           /* allocation base address */
+  uint64_t capacity_bytes;
+  uint64_t offset_bytes;   /* logical element 0 */
+  int32_t kind;            /* 0 host, 1 cuda */
+  int32_t device;          /* CUDA ordinal, -1 for host */
+  int32_t rank;            /* <= 8 */
+  uint32_t element_size;
+  int64_t extents[8];
+  int64_t strides[8];      /* elements */
+} sb_view;
+
+/* Execution options (reference TransferOptions, Transfer.h:121-155, plus the route). */
+typedef struct {
+  int32_t n_buffers;          /* HBM ring slots; <= 0 = 4 */
+  int32_t route;              /* 0 auto, 1 dma_ring, 2 zero_copy, 3 staged */
+  uint64_t chunk_bytes;       /* ring slot bytes; 0 = heuristic */
+  const void *caller_stream;  /* cudaStream_t of the caller, or NULL */
+  int32_t has_caller_stream;  /* order after / signal caller_stream */
+  int32_t async_completion;   /* return once enqueued; the caller stream carries completion */
+} sb_options;
+
+/* Version string of this library. */
+const char *sb_version(void);
+/* Kernels launched by this process through the library (instrumentation). */
+uint64_t sb_kernel_launches(void);
+
+/* pyreloc.wire_version (PyReloc.cpp:799): the blob's version or -1. */
+int sb_wire_version(const uint8_t *data, size_t size);
+/* pyreloc.load_plan (PyReloc.cpp:596): wire v0 -> decodePlan. */
+int sb_load_plan(const uint8_t *data, size_t size, sb_plan **out, sb_error *err);
+/* pyreloc.load_typed_plan (PyReloc.cpp:921): wire v1 -> decodeTypedPlan. */
+int sb_load_typed_plan(const uint8_t *data, size_t size, sb_plan **out, sb_error *err);
+/* TypedPlanHandle / PlanHandle properties as JSON (PyReloc.cpp:577-594, 812-862).
+ * Returns the JSON length; writes at most cap-1 bytes plus NUL. */
+int sb_plan_describe(const sb_plan *plan, char *json, size_t cap);
+void sb_plan_free(sb_plan *plan);
+
+/* pyreloc.bind (PyReloc.cpp:674): a v0 plan against {symbol: value}. */
+int sb_bind(const sb_plan *plan, int32_t nsym, const char *const *names, const int64_t *values, sb_bound **out,
+            sb_error *err);
+/* pyreloc.bind_typed (PyReloc.cpp:987): a v1 plan against symbols and runtime
+ * parameters (per parameter: name, dtype name, rank 0/1, extent, LE bytes). */
+int sb_bind_typed(const sb_plan *plan, int32_t nsym, const char *const *names, const int64_t *values, int32_t nparam,
+                  const char *const *pnames, const char *const *pdtypes, const int32_t *pranks,
+                  const int64_t *pextents, const void *const *pbytes, const size_t *plens, sb_bound **out,
+                  sb_error *err);
+/* BoundPlan / TypedBoundPlan properties as JSON (layout, cuts, footprints,
+ * stages with their checked arithmetic). */
+int sb_bound_describe(const sb_bound *bound, char *json, size_t cap);
+void sb_bound_free(sb_bound *bound);
+
+/* pyreloc.query_capability (PyDispatch.cpp:831): JSON {eligible, excluded}.
+ * direction: 0 h2d, 1 d2h. */
+int sb_query_capability(const sb_bound *bound, int32_t direction, int32_t cuda, char *json, size_t cap,
+                        sb_error *err);
+/* pyreloc.prepare_dispatch_template (PyDispatch.cpp:612). policy: 0 auto,
+ * 1 original_cpu; implementation: explicit row label or NULL/"". */
+int sb_prepare_dispatch_template(const sb_bound *bound, int32_t direction, int32_t policy, const char *implementation,
+                                 sb_template **out, sb_error *err);
+/* pyreloc.make_transfer (PyTransfer.cpp:440) for wire v0 layout plans: a
+ * template whose source is the dense 1-D span the plan reads and whose
+ * result is the dense padded destination; executed like a typed template. */
+int sb_prepare_transfer_template(const sb_bound *bound, sb_template **out, sb_error *err);
+/* capability + selection as JSON. */
+int sb_template_describe(const sb_template *tmpl, char *json, size_t cap);
+void sb_template_free(sb_template *tmpl);
+
+/* pyreloc.prepare_dispatch_from_template (PyDispatch.cpp:620): validate the
+ * caller's views against the template. */
+int sb_prepare_dispatch(const sb_template *tmpl, const sb_view *source, const sb_view *destination, sb_request **out,
+                        sb_error *err);
+/* pyreloc.execute_dispatch (PyDispatch.cpp:889): run the request on the
+ * context of the destination's device (resources may be NULL: a private
+ * context for this call). report: JSON of the reference Report fields. */
+int sb_execute_dispatch(sb_request *request, sb_resources *resources, const sb_options *options, char *report,
+                        size_t cap, sb_error *err);
+void sb_request_free(sb_request *request);
+
+/* Shard execution (reference typed::executeHostChunk contract,
+ * TypedExecute.h:160-170, on the device): produce the physical rows
+ * [row_begin, row_end) of axis 0 of the padded result into `dst` (the
+ * window's own device storage, (row_end-row_begin) rows). host_source != 0:
+ * `src` is the whole host source and only the rows' source bytes cross PCIe;
+ * host_source == 0: `src` is the whole source in this device's memory. */
+int sb_execute_rows(const sb_template *tmpl, sb_resources *resources, int32_t device, const void *src,
+                    int32_t host_source, void *dst, int64_t row_begin, int64_t row_end, const sb_options *options,
+                    char *report, size_t cap, sb_error *err);
+
+/* pyreloc.DispatchResources (PyDispatch.cpp:700-801) / dispatch::Resources. */
+int sb_resources_create(uint64_t max_retained_bytes, uint64_t max_live_bytes, uint32_t max_contexts,
+                        sb_resources **out, sb_error *err);
+int sb_resources_stats(const sb_resources *resources, char *json, size_t cap);
+int sb_resources_clear(sb_resources *resources, sb_error *err);
+int sb_resources_close(sb_resources *resources, sb_error *err);
+void sb_resources_free(sb_resources *resources);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

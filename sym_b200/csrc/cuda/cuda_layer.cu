@@ -1,0 +1,121 @@
+// sym_b200 -- the CUDA runtime half of the thin C-ABI layer (include/sb_cuda.h):
+// devices, pinned/device memory, async copies, streams and events. Each
+// function is one checked CUDA runtime call; status codes are cudaError_t
+// values. Counterpart of the reference's CudaBackend
+// (libreloc/cuda/CudaBackend.cu:55-282).
+#include "sb_cuda.h"
+
+#include <cuda_runtime.h>
+
+namespace {
+cudaStream_t S(void *s) { return static_cast<cudaStream_t>(s); }
+cudaEvent_t E(void *e) { return static_cast<cudaEvent_t>(e); }
+} // namespace
+
+extern "C" {
+
+int sbc_device_count(int *count) { return cudaGetDeviceCount(count); }
+int sbc_set_device(int device) { return cudaSetDevice(device); }
+int sbc_get_device(int *device) { return cudaGetDevice(device); }
+
+int sbc_device_info(int device, int *major, int *minor, int *sms, size_t *hbm_bytes) {
+  cudaDeviceProp p;
+  cudaError_t e = cudaGetDeviceProperties(&p, device);
+  if (e != cudaSuccess)
+    return e;
+  *major = p.major;
+  *minor = p.minor;
+  *sms = p.multiProcessorCount;
+  *hbm_bytes = p.totalGlobalMem;
+  return 0;
+}
+
+int sbc_malloc_device(void **ptr, size_t bytes) { return cudaMalloc(ptr, bytes); }
+int sbc_free_device(void *ptr) { return cudaFree(ptr); }
+
+int sbc_malloc_host(void **ptr, size_t bytes, int mapped) {
+  return cudaHostAlloc(ptr, bytes, mapped ? (cudaHostAllocMapped | cudaHostAllocPortable) : cudaHostAllocPortable);
+}
+int sbc_free_host(void *ptr) { return cudaFreeHost(ptr); }
+
+int sbc_host_register(void *ptr, size_t bytes, int mapped) {
+  return cudaHostRegister(ptr, bytes, mapped ? (cudaHostRegisterMapped | cudaHostRegisterPortable)
+                                             : cudaHostRegisterPortable);
+}
+int sbc_host_unregister(void *ptr) { return cudaHostUnregister(ptr); }
+
+int sbc_host_device_pointer(void *host, void **device) {
+  const cudaError_t e = cudaHostGetDevicePointer(device, host, 0);
+  if (e != cudaSuccess)
+    cudaGetLastError(); // an expected probe failure must not poison later launch checks
+  return e;
+}
+
+int sbc_pointer_info(const void *ptr, int *kind, int *device) {
+  cudaPointerAttributes a;
+  cudaError_t e = cudaPointerGetAttributes(&a, ptr);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return e;
+  }
+  switch (a.type) {
+  case cudaMemoryTypeHost: *kind = 1; break;
+  case cudaMemoryTypeDevice: *kind = 2; break;
+  case cudaMemoryTypeManaged: *kind = 3; break;
+  default: *kind = 0; break;
+  }
+  *device = (a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged) ? a.device : -1;
+  return 0;
+}
+
+int sbc_memcpy_h2d_async(void *dst, const void *src, size_t bytes, void *stream) {
+  return cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, S(stream));
+}
+int sbc_memcpy_d2h_async(void *dst, const void *src, size_t bytes, void *stream) {
+  return cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, S(stream));
+}
+int sbc_memcpy_d2d_async(void *dst, const void *src, size_t bytes, void *stream) {
+  return cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, S(stream));
+}
+int sbc_memcpy_h2d_2d_async(void *dst, size_t dpitch, const void *src, size_t spitch, size_t width, size_t rows,
+                            void *stream) {
+  return cudaMemcpy2DAsync(dst, dpitch, src, spitch, width, rows, cudaMemcpyHostToDevice, S(stream));
+}
+
+int sbc_stream_create(void **stream) {
+  cudaStream_t s = nullptr;
+  cudaError_t e = cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking);
+  *stream = s;
+  return e;
+}
+int sbc_stream_destroy(void *stream) { return cudaStreamDestroy(S(stream)); }
+int sbc_stream_synchronize(void *stream) { return cudaStreamSynchronize(S(stream)); }
+
+int sbc_event_create(void **event, int timing) {
+  cudaEvent_t ev = nullptr;
+  cudaError_t e = cudaEventCreateWithFlags(&ev, timing ? cudaEventDefault : cudaEventDisableTiming);
+  *event = ev;
+  return e;
+}
+int sbc_event_destroy(void *event) { return cudaEventDestroy(E(event)); }
+int sbc_event_record(void *event, void *stream) { return cudaEventRecord(E(event), S(stream)); }
+int sbc_event_query(void *event) {
+  cudaError_t e = cudaEventQuery(E(event));
+  if (e == cudaErrorNotReady) {
+    return 1;
+  }
+  return e;
+}
+int sbc_event_synchronize(void *event) { return cudaEventSynchronize(E(event)); }
+int sbc_stream_wait_event(void *stream, void *event) { return cudaStreamWaitEvent(S(stream), E(event), 0); }
+int sbc_event_elapsed_ms(void *start, void *stop, float *ms) { return cudaEventElapsedTime(ms, E(start), E(stop)); }
+
+const char *sbc_error_string(int status) {
+  if (status == SBC_EINVAL)
+    return "descriptor violates the launcher's preconditions";
+  if (status == SBC_EUNSUPPORTED)
+    return "layout is not of this kernel family";
+  return cudaGetErrorString(static_cast<cudaError_t>(status));
+}
+
+} // extern "C"

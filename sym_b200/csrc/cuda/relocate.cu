@@ -1,0 +1,666 @@
+// sym_b200 -- fused relocation kernels for sm_100a.
+//
+// Every kernel here performs the whole typed plan in one pass over HBM (or
+// over mapped pinned host memory on the zero-copy route): index remap with
+// pads, then the value-stage chain, then the store in the result layout. The
+// element arithmetic is libreloc's C1 contract
+// (docs/reloc-typed-semantics.md §3; reference kernels
+// libreloc/cuda/CudaKernels.cu:149-238):
+//   quantize   t = x * inv (one rounding), maxNum(t,-128), minNum(.,127), RNE
+//   dequantize (q - zp) exactly, then one multiply
+//   f32->f16 / f32->bf16 RNE narrowing, f16/bf16->f32 exact widening
+// Multiplies use __fmul_rn so no FMA contraction can arise; the build passes
+// neither --use_fast_math nor flush-to-zero. NaN inputs to the narrowing casts
+// produce the reference's CPU NaN encoding (quiet bit + top payload bits), so
+// outputs are bit-identical to the reference CPU executor for every input.
+#include "sb_cuda.h"
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdint>
+
+namespace {
+
+std::atomic<uint64_t> g_launches{0};
+
+// ---------------------------------------------------------------------------
+// Scalar stage arithmetic
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ uint32_t narrow_f16(uint32_t x) {
+  const uint32_t a = x & 0x7fffffffu;
+  if (a > 0x7f800000u)
+    return ((x >> 16) & 0x8000u) | 0x7e00u | ((a >> 13) & 0x3ffu);
+  return __half_as_ushort(__float2half_rn(__uint_as_float(x)));
+}
+
+__device__ __forceinline__ uint32_t narrow_bf16(uint32_t x) {
+  if ((x & 0x7fffffffu) > 0x7f800000u)
+    return (x >> 16) | 0x40u;
+  return __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(x)));
+}
+
+__device__ __forceinline__ uint32_t widen_f16(uint32_t h) {
+  if ((h & 0x7c00u) == 0x7c00u && (h & 0x3ffu)) // NaN: payload shifted up
+    return ((h & 0x8000u) << 16) | 0x7f800000u | ((h & 0x3ffu) << 13);
+  return __float_as_uint(__half2float(__ushort_as_half(static_cast<unsigned short>(h))));
+}
+
+__device__ __forceinline__ uint32_t widen_bf16(uint32_t b) { return b << 16; }
+
+__device__ __forceinline__ uint32_t quantize(uint32_t x, float inv) {
+  float t = __fmul_rn(__uint_as_float(x), inv);
+  t = fmaxf(t, -128.0f); // maxNum: NaN -> -128
+  t = fminf(t, 127.0f);
+  return static_cast<uint32_t>(__float2int_rn(t)) & 0xffu;
+}
+
+__device__ __forceinline__ uint32_t dequantize(uint32_t q, int32_t zp, float scale) {
+  const int32_t d = static_cast<int32_t>(static_cast<int8_t>(q & 0xffu)) - zp;
+  return __float_as_uint(__fmul_rn(static_cast<float>(d), scale));
+}
+
+// ---------------------------------------------------------------------------
+// Stage chains. Common chains are specialized at compile time; CH_ANY
+// interprets the descriptor's stage list.
+// ---------------------------------------------------------------------------
+
+enum Chain : int {
+  CH_COPY = 0,
+  CH_Q = 1,
+  CH_DQ = 2,
+  CH_F16 = 3,
+  CH_BF16 = 4,
+  CH_W16 = 5,
+  CH_WB16 = 6,
+  CH_DQ_F16 = 7,
+  CH_DQ_BF16 = 8,
+  CH_ANY = 9
+};
+
+__device__ __forceinline__ int32_t zp_of(const sbc_stage &s, int64_t c) {
+  return s.zp_mode == 0 ? 0 : (s.zp_mode == 1 ? s.zero_point[0] : s.zero_point[c]);
+}
+
+__device__ __forceinline__ uint32_t apply_one(const sbc_stage &s, uint32_t v, int64_t c) {
+  switch (s.op) {
+  case SBC_NARROW_F16: return narrow_f16(v);
+  case SBC_NARROW_BF16: return narrow_bf16(v);
+  case SBC_WIDEN_F16: return widen_f16(v);
+  case SBC_WIDEN_BF16: return widen_bf16(v);
+  case SBC_QUANTIZE: return quantize(v, s.param[c]);
+  default: return dequantize(v, zp_of(s, c), s.param[c]);
+  }
+}
+
+/// Channel of stage `s` from the padded coordinates (AXIS kind) or the
+/// global destination offset (OFFSET / EXPR kinds). Returns -1 when out of
+/// range (the caller records the error and skips the element).
+template <int R>
+__device__ __forceinline__ int64_t channel_of(const sbc_relocate &d, const sbc_stage &s, const int64_t *coords,
+                                              int64_t dglobal) {
+  int64_t c = 0;
+  if (s.channel == SBC_CH_NONE)
+    return 0;
+  if (s.channel == SBC_CH_AXIS) {
+    c = coords[s.ch_axis] / s.ch_div;
+    if (s.ch_mod)
+      c %= s.ch_mod;
+  } else if (s.channel == SBC_CH_OFFSET) {
+    c = (dglobal / d.result_strides[s.ch_dim]) % d.result_extents[s.ch_dim];
+  } else {
+    int64_t rc[SBC_MAX_RANK];
+    int64_t rest = dglobal;
+    for (int j = 0; j < d.result_rank; ++j) {
+      rc[j] = rest / d.result_strides[j];
+      rest -= rc[j] * d.result_strides[j];
+    }
+    int64_t st[SBC_MAX_TOKENS];
+    int sp = 0;
+    for (int i = 0; i < s.ntokens; ++i) {
+      const int op = s.token_op[i];
+      const int64_t v = s.token_value[i];
+      if (op == 0) st[sp++] = d.symbols[v];
+      else if (op == 1) st[sp++] = v;
+      else if (op == 7) st[sp++] = rc[v];
+      else {
+        const int64_t r = st[--sp], l = st[--sp];
+        int64_t o = 0;
+        if (op == 2) o = l + r;
+        else if (op == 3) o = l - r;
+        else if (op == 4) o = l * r;
+        else {
+          if (r == 0)
+            return -1;
+          int64_t q = l / r;
+          if ((l % r != 0) && ((l < 0) != (r < 0)))
+            --q;
+          o = op == 5 ? q : l - q * r;
+        }
+        st[sp++] = o;
+      }
+    }
+    c = sp == 1 ? st[0] : -1;
+  }
+  return (c < 0 || c >= s.channel_length) ? -1 : c;
+}
+
+/// Run the stage chain on one value. Returns false on a channel error.
+template <int CHAIN, int R>
+__device__ __forceinline__ bool run_chain(const sbc_relocate &d, uint32_t &v, const int64_t *coords, int64_t dglobal) {
+  if constexpr (CHAIN == CH_COPY) {
+    return true;
+  } else if constexpr (CHAIN == CH_F16) {
+    v = narrow_f16(v);
+    return true;
+  } else if constexpr (CHAIN == CH_BF16) {
+    v = narrow_bf16(v);
+    return true;
+  } else if constexpr (CHAIN == CH_W16) {
+    v = widen_f16(v);
+    return true;
+  } else if constexpr (CHAIN == CH_WB16) {
+    v = widen_bf16(v);
+    return true;
+  } else if constexpr (CHAIN == CH_Q || CHAIN == CH_DQ || CHAIN == CH_DQ_F16 || CHAIN == CH_DQ_BF16) {
+    const sbc_stage &s = d.stages[0];
+    const int64_t c = channel_of<R>(d, s, coords, dglobal);
+    if (c < 0)
+      return false;
+    if constexpr (CHAIN == CH_Q) {
+      v = quantize(v, s.param[c]);
+    } else {
+      v = dequantize(v, zp_of(s, c), s.param[c]);
+      if constexpr (CHAIN == CH_DQ_F16)
+        v = narrow_f16(v);
+      if constexpr (CHAIN == CH_DQ_BF16)
+        v = narrow_bf16(v);
+    }
+    return true;
+  } else {
+    for (int k = 0; k < d.nstages; ++k) {
+      const sbc_stage &s = d.stages[k];
+      const int64_t c = channel_of<R>(d, s, coords, dglobal);
+      if (c < 0)
+        return false;
+      v = apply_one(s, v, c);
+    }
+    return true;
+  }
+}
+
+template <int W> struct Word;
+template <> struct Word<1> { using T = uint8_t; };
+template <> struct Word<2> { using T = uint16_t; };
+template <> struct Word<4> { using T = uint32_t; };
+template <> struct Word<8> { using T = unsigned long long; };
+
+__device__ __forceinline__ void flag(const sbc_relocate &d) {
+  if (d.status)
+    atomicExch(d.status, 1);
+}
+
+// ---------------------------------------------------------------------------
+// Generic gather over the destination box: any rank, pads, any channel map.
+// ---------------------------------------------------------------------------
+
+template <int WS, int WD, int CHAIN>
+__global__ void __launch_bounds__(256) k_generic(const __grid_constant__ sbc_relocate d, int64_t total) {
+  using S = typename Word<WS>::T;
+  using D = typename Word<WD>::T;
+  const S *src = static_cast<const S *>(d.src);
+  D *dst = static_cast<D *>(d.dst);
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    int64_t coords[SBC_MAX_RANK];
+    int64_t rem = i, so = 0, dg = 0;
+    bool valid = true;
+#pragma unroll
+    for (int kk = 0; kk < SBC_MAX_RANK; ++kk) {
+      const int k = SBC_MAX_RANK - 1 - kk;
+      if (k >= d.rank)
+        continue;
+      const int64_t e = d.box_hi[k] - d.box_lo[k];
+      const int64_t q = rem / e;
+      const int64_t c = d.box_lo[k] + (rem - q * e);
+      rem = q;
+      coords[k] = c;
+      dg += c * d.dst_strides[k];
+      const int64_t v = c - d.pad_lo[k];
+      if (v < 0 || v >= d.extents[k])
+        valid = false;
+      else
+        so += v * d.src_strides[k];
+    }
+    if (!valid) {
+      dst[dg - d.dst_offset] = static_cast<D>(d.fill_bits);
+      continue;
+    }
+    if constexpr (WS == 8) {
+      dst[dg - d.dst_offset] = static_cast<D>(src[so - d.src_offset]);
+    } else {
+      uint32_t v = static_cast<uint32_t>(src[so - d.src_offset]);
+      if (!run_chain<CHAIN, SBC_MAX_RANK>(d, v, coords, dg)) {
+        flag(d);
+        continue;
+      }
+      dst[dg - d.dst_offset] = static_cast<D>(v);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Contiguous runs: rank 1, unit strides. 16-byte vector loads and stores on
+// the valid, aligned body; scalar head/tail and pad cells.
+// ---------------------------------------------------------------------------
+
+template <int WS, int WD>
+struct Vec {
+  static constexpr int MINW = WS < WD ? WS : WD;
+  static constexpr int V = 16 / MINW;                // elements per thread-step
+  static constexpr int LOADS = (V * WS) / 16;        // 16-byte loads
+  static constexpr int STORES = (V * WD) / 16;       // 16-byte stores
+};
+
+template <int WS, int WD, int CHAIN>
+__global__ void __launch_bounds__(256) k_contiguous(const __grid_constant__ sbc_relocate d, int64_t vbegin,
+                                                     int64_t nvec) {
+  using S = typename Word<WS>::T;
+  using D = typename Word<WD>::T;
+  constexpr int V = Vec<WS, WD>::V;
+  const S *src = static_cast<const S *>(d.src);
+  D *dst = static_cast<D *>(d.dst);
+  const int64_t lo = d.pad_lo[0];
+  for (int64_t g = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; g < nvec;
+       g += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t c0 = vbegin + g * V; // padded coordinate of the first element
+    const int64_t s0 = c0 - lo - d.src_offset;
+    const int64_t d0 = c0 - d.dst_offset;
+    union {
+      uint4 q[Vec<WS, WD>::LOADS];
+      S e[V];
+    } in;
+    union {
+      uint4 q[Vec<WS, WD>::STORES];
+      D e[V];
+    } out;
+    const uint4 *sp = reinterpret_cast<const uint4 *>(src + s0);
+#pragma unroll
+    for (int i = 0; i < Vec<WS, WD>::LOADS; ++i)
+      in.q[i] = __ldcs(sp + i); // streamed once: evict-first
+    bool ok = true;
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      int64_t c = c0 + i;
+      uint32_t v = static_cast<uint32_t>(in.e[i]);
+      ok &= run_chain<CHAIN, 1>(d, v, &c, c);
+      out.e[i] = static_cast<D>(v);
+    }
+    if (!ok) {
+      flag(d);
+      continue;
+    }
+    uint4 *dp = reinterpret_cast<uint4 *>(dst + d0);
+#pragma unroll
+    for (int i = 0; i < Vec<WS, WD>::STORES; ++i)
+      __stcs(dp + i, out.q[i]);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Tiled transpose. Layout (rank 2): axis A (src stride 1) then axis B (dst
+// stride 1); rank 3 adds a leading batch axis N. A tile of TA x TB padded
+// coordinates is read along A (coalesced in the source), converted, staged in
+// shared memory, and written along B (coalesced in the destination).
+// ---------------------------------------------------------------------------
+
+template <int WS, int WD, int CHAIN>
+__global__ void __launch_bounds__(256) k_transpose(const __grid_constant__ sbc_relocate d, int ta, int tb,
+                                                    int64_t tiles_a, int64_t tiles_b, int64_t nbatch) {
+  using S = typename Word<WS>::T;
+  using D = typename Word<WD>::T;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  D *tile = reinterpret_cast<D *>(smem_raw);
+  const int pitch = tb + 1;
+  const int r = d.rank;
+  const int ax_a = r - 2, ax_b = r - 1;
+  const S *src = static_cast<const S *>(d.src);
+  D *dst = static_cast<D *>(d.dst);
+  const int64_t tiles = tiles_a * tiles_b;
+  for (int64_t job = blockIdx.x; job < tiles * nbatch; job += gridDim.x) {
+    const int64_t n_idx = job / tiles;
+    const int64_t t = job - n_idx * tiles;
+    const int64_t ta_i = t % tiles_a, tb_i = t / tiles_a;
+    int64_t coords[3];
+    int64_t nsrc = 0, ndst = 0;
+    bool nvalid = true;
+    if (r == 3) {
+      const int64_t cn = d.box_lo[0] + n_idx;
+      coords[0] = cn;
+      ndst = cn * d.dst_strides[0];
+      const int64_t vn = cn - d.pad_lo[0];
+      nvalid = vn >= 0 && vn < d.extents[0];
+      nsrc = vn * d.src_strides[0];
+    }
+    const int64_t a0 = d.box_lo[ax_a] + ta_i * ta, b0 = d.box_lo[ax_b] + tb_i * tb;
+    const int64_t a_end = min(a0 + ta, d.box_hi[ax_a]), b_end = min(b0 + tb, d.box_hi[ax_b]);
+    const int na = static_cast<int>(a_end - a0), nb = static_cast<int>(b_end - b0);
+    // load + convert: consecutive threads take consecutive A (source-contiguous)
+    for (int e = threadIdx.x; e < na * nb; e += blockDim.x) {
+      const int al = e % na, bl = e / na;
+      const int64_t ca = a0 + al, cb = b0 + bl;
+      const int64_t va = ca - d.pad_lo[ax_a], vb = cb - d.pad_lo[ax_b];
+      D out;
+      if (!nvalid || va < 0 || va >= d.extents[ax_a] || vb < 0 || vb >= d.extents[ax_b]) {
+        out = static_cast<D>(d.fill_bits);
+      } else {
+        uint32_t v = static_cast<uint32_t>(src[nsrc + va + vb * d.src_strides[ax_b] - d.src_offset]);
+        coords[ax_a] = ca;
+        coords[ax_b] = cb;
+        const int64_t dg = ndst + ca * d.dst_strides[ax_a] + cb;
+        if (!run_chain<CHAIN, 3>(d, v, coords, dg)) {
+          flag(d);
+          v = 0;
+        }
+        out = static_cast<D>(v);
+      }
+      tile[al * pitch + bl] = out;
+    }
+    __syncthreads();
+    // store: consecutive threads take consecutive B (destination-contiguous)
+    for (int e = threadIdx.x; e < na * nb; e += blockDim.x) {
+      const int al = e / nb, bl = e % nb;
+      dst[ndst + (a0 + al) * d.dst_strides[ax_a] + b0 + bl - d.dst_offset] = tile[al * pitch + bl];
+    }
+    __syncthreads();
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Fill
+// ---------------------------------------------------------------------------
+
+template <int W>
+__global__ void __launch_bounds__(256) k_fill(void *dst, int64_t count, uint64_t bits) {
+  using D = typename Word<W>::T;
+  D *p = static_cast<D *>(dst);
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < count;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    p[i] = static_cast<D>(bits);
+}
+
+// ---------------------------------------------------------------------------
+// Host side: chain detection, dispatch over the instantiations, launch shape.
+// ---------------------------------------------------------------------------
+
+int chain_of(const sbc_relocate &d) {
+  if (d.nstages == 0)
+    return CH_COPY;
+  const int o0 = d.stages[0].op;
+  if (d.nstages == 1) {
+    switch (o0) {
+    case SBC_QUANTIZE: return CH_Q;
+    case SBC_DEQUANTIZE: return CH_DQ;
+    case SBC_NARROW_F16: return CH_F16;
+    case SBC_NARROW_BF16: return CH_BF16;
+    case SBC_WIDEN_F16: return CH_W16;
+    case SBC_WIDEN_BF16: return CH_WB16;
+    }
+  }
+  if (d.nstages == 2 && o0 == SBC_DEQUANTIZE && d.stages[1].channel == SBC_CH_NONE) {
+    if (d.stages[1].op == SBC_NARROW_F16)
+      return CH_DQ_F16;
+    if (d.stages[1].op == SBC_NARROW_BF16)
+      return CH_DQ_BF16;
+  }
+  return CH_ANY;
+}
+
+/// Channel kinds a specialized chain may use (it only reads stage 0).
+bool chain_channels_ok(const sbc_relocate &d, int chain, bool allow_offset) {
+  for (int k = 0; k < d.nstages; ++k) {
+    const int ch = d.stages[k].channel;
+    if (ch == SBC_CH_EXPR || (ch == SBC_CH_OFFSET && !allow_offset))
+      return false;
+  }
+  (void)chain;
+  return true;
+}
+
+int g_sms = 0;
+int sm_count() {
+  if (g_sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&g_sms, cudaDevAttrMultiProcessorCount, dev);
+    if (g_sms <= 0)
+      g_sms = 148;
+  }
+  return g_sms;
+}
+
+int64_t grid_for(int64_t work_items, int per_block, int blocks_per_sm) {
+  int64_t blocks = (work_items + per_block - 1) / per_block;
+  const int64_t cap = static_cast<int64_t>(sm_count()) * blocks_per_sm;
+  if (blocks > cap)
+    blocks = cap;
+  return blocks < 1 ? 1 : blocks;
+}
+
+int launched(cudaError_t e) {
+  if (e == cudaSuccess)
+    e = cudaGetLastError();
+  if (e == cudaSuccess)
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+  return static_cast<int>(e);
+}
+
+template <template <int, int, int> class F, typename... Args>
+int dispatch(int ws, int wd, int chain, Args &&...args) {
+#define SBC_CASE(WS_, WD_, CH_)                                                                                 \
+  if (ws == WS_ && wd == WD_ && chain == CH_)                                                                  \
+    return F<WS_, WD_, CH_>::run(args...);
+  SBC_CASE(1, 1, CH_COPY)
+  SBC_CASE(2, 2, CH_COPY)
+  SBC_CASE(4, 4, CH_COPY)
+  SBC_CASE(8, 8, CH_COPY)
+  SBC_CASE(4, 1, CH_Q)
+  SBC_CASE(1, 4, CH_DQ)
+  SBC_CASE(4, 2, CH_F16)
+  SBC_CASE(4, 2, CH_BF16)
+  SBC_CASE(2, 4, CH_W16)
+  SBC_CASE(2, 4, CH_WB16)
+  SBC_CASE(1, 2, CH_DQ_F16)
+  SBC_CASE(1, 2, CH_DQ_BF16)
+  SBC_CASE(1, 1, CH_ANY)
+  SBC_CASE(1, 2, CH_ANY)
+  SBC_CASE(1, 4, CH_ANY)
+  SBC_CASE(2, 1, CH_ANY)
+  SBC_CASE(2, 2, CH_ANY)
+  SBC_CASE(2, 4, CH_ANY)
+  SBC_CASE(4, 1, CH_ANY)
+  SBC_CASE(4, 2, CH_ANY)
+  SBC_CASE(4, 4, CH_ANY)
+#undef SBC_CASE
+  return SBC_EUNSUPPORTED;
+}
+
+template <int WS, int WD, int CH> struct GenericLaunch {
+  static int run(const sbc_relocate &d, int64_t total, cudaStream_t s) {
+    const int64_t blocks = grid_for(total, 256, 8);
+    k_generic<WS, WD, CH><<<static_cast<unsigned>(blocks), 256, 0, s>>>(d, total);
+    return launched(cudaSuccess);
+  }
+};
+
+template <int WS, int WD, int CH> struct ContiguousLaunch {
+  static int run(const sbc_relocate &d, int64_t vbegin, int64_t nvec, cudaStream_t s) {
+    if constexpr (WS == 8 || WD == 8) {
+      return SBC_EUNSUPPORTED;
+    } else {
+      const int64_t blocks = grid_for(nvec, 256, 8);
+      k_contiguous<WS, WD, CH><<<static_cast<unsigned>(blocks), 256, 0, s>>>(d, vbegin, nvec);
+      return launched(cudaSuccess);
+    }
+  }
+};
+
+template <int WS, int WD, int CH> struct TransposeLaunch {
+  static int run(const sbc_relocate &d, int ta, int tb, int64_t tiles_a, int64_t tiles_b, int64_t nbatch,
+                 cudaStream_t s) {
+    if constexpr (WS == 8) {
+      return SBC_EUNSUPPORTED;
+    } else {
+      const size_t smem = static_cast<size_t>(ta) * (tb + 1) * WD;
+      const int64_t jobs = tiles_a * tiles_b * nbatch;
+      int64_t blocks = jobs;
+      const int64_t cap = static_cast<int64_t>(sm_count()) * 16;
+      if (blocks > cap)
+        blocks = cap;
+      k_transpose<WS, WD, CH><<<static_cast<unsigned>(blocks), 256, smem, s>>>(d, ta, tb, tiles_a, tiles_b, nbatch);
+      return launched(cudaSuccess);
+    }
+  }
+};
+
+bool basic_ok(const sbc_relocate &d) {
+  if (d.rank < 1 || d.rank > SBC_MAX_RANK || d.nstages < 0 || d.nstages > SBC_MAX_STAGES || !d.dst)
+    return false;
+  for (int k = 0; k < d.rank; ++k)
+    if (d.box_hi[k] < d.box_lo[k] || d.box_lo[k] < 0 || d.extents[k] < 1)
+      return false;
+  return true;
+}
+
+int64_t box_count(const sbc_relocate &d) {
+  int64_t n = 1;
+  for (int k = 0; k < d.rank; ++k)
+    n *= d.box_hi[k] - d.box_lo[k];
+  return n;
+}
+
+} // namespace
+
+extern "C" {
+
+int sbc_relocate_generic(const sbc_relocate *desc, void *stream) {
+  if (!desc || !basic_ok(*desc))
+    return SBC_EINVAL;
+  const int64_t total = box_count(*desc);
+  if (total == 0)
+    return 0;
+  int chain = chain_of(*desc);
+  if (!chain_channels_ok(*desc, chain, true))
+    chain = CH_ANY;
+  if (desc->src_width == 8 || desc->dst_width == 8)
+    chain = desc->nstages == 0 && desc->src_width == desc->dst_width ? CH_COPY : -1;
+  return dispatch<GenericLaunch>(desc->src_width, desc->dst_width, chain, *desc, total,
+                                 static_cast<cudaStream_t>(stream));
+}
+
+int sbc_relocate_contiguous(const sbc_relocate *desc, void *stream) {
+  if (!desc || !basic_ok(*desc))
+    return SBC_EINVAL;
+  const sbc_relocate &d = *desc;
+  if (d.rank != 1 || d.src_strides[0] != 1 || d.dst_strides[0] != 1)
+    return SBC_EUNSUPPORTED;
+  int chain = chain_of(d);
+  if (!chain_channels_ok(d, chain, false))
+    return SBC_EUNSUPPORTED;
+  const int ws = d.src_width, wd = d.dst_width;
+  if (ws == 8 || wd == 8)
+    return SBC_EUNSUPPORTED;
+  const int minw = ws < wd ? ws : wd;
+  const int V = 16 / minw;
+  // Valid part of the box, then its 16-byte aligned vector body.
+  const int64_t lo = d.box_lo[0], hi = d.box_hi[0];
+  const int64_t v0 = lo > d.pad_lo[0] ? lo : d.pad_lo[0];
+  const int64_t vend = d.pad_lo[0] + d.extents[0];
+  const int64_t v1 = hi < vend ? hi : vend;
+  int64_t body0 = v0, nvec = 0;
+  if (v1 > v0) {
+    const uintptr_t sa = reinterpret_cast<uintptr_t>(d.src) + (v0 - d.pad_lo[0] - d.src_offset) * ws;
+    const uintptr_t da = reinterpret_cast<uintptr_t>(d.dst) + (v0 - d.dst_offset) * wd;
+    // advance to the first element where both addresses are 16-byte aligned
+    int64_t skip = -1;
+    for (int64_t i = 0; i < V && v0 + i < v1; ++i)
+      if ((sa + i * ws) % 16 == 0 && (da + i * wd) % 16 == 0) {
+        skip = i;
+        break;
+      }
+    if (skip >= 0) {
+      body0 = v0 + skip;
+      nvec = (v1 - body0) / V;
+    }
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // Scalar remainder (head, tail, pads) through the generic kernel.
+  auto generic_range = [&](int64_t a, int64_t b) -> int {
+    if (b <= a)
+      return 0;
+    sbc_relocate part = d;
+    part.box_lo[0] = a;
+    part.box_hi[0] = b;
+    return sbc_relocate_generic(&part, stream);
+  };
+  if (nvec == 0)
+    return generic_range(lo, hi);
+  int rc = dispatch<ContiguousLaunch>(ws, wd, chain, d, body0, nvec, s);
+  if (rc)
+    return rc;
+  if ((rc = generic_range(lo, body0)))
+    return rc;
+  return generic_range(body0 + nvec * V, hi);
+}
+
+int sbc_relocate_transpose(const sbc_relocate *desc, void *stream) {
+  if (!desc || !basic_ok(*desc))
+    return SBC_EINVAL;
+  const sbc_relocate &d = *desc;
+  if (d.rank != 2 && d.rank != 3)
+    return SBC_EUNSUPPORTED;
+  const int ax_a = d.rank - 2, ax_b = d.rank - 1;
+  if (d.src_strides[ax_a] != 1 || d.dst_strides[ax_b] != 1)
+    return SBC_EUNSUPPORTED;
+  int chain = chain_of(d);
+  if (!chain_channels_ok(d, chain, true))
+    return SBC_EUNSUPPORTED;
+  if (d.src_width == 8 || d.dst_width == 8)
+    return SBC_EUNSUPPORTED;
+  const int64_t ext_a = d.box_hi[ax_a] - d.box_lo[ax_a], ext_b = d.box_hi[ax_b] - d.box_lo[ax_b];
+  const int64_t nbatch = d.rank == 3 ? d.box_hi[0] - d.box_lo[0] : 1;
+  if (ext_a == 0 || ext_b == 0 || nbatch == 0)
+    return 0;
+  // Tile shape: a short destination row (B) takes the whole row so the tile
+  // is one contiguous destination block; otherwise 64 x 64.
+  int tb = 64, ta = 64;
+  if (ext_b <= 16) {
+    tb = static_cast<int>(ext_b);
+    ta = 2048 / tb;
+  }
+  const int64_t tiles_a = (ext_a + ta - 1) / ta, tiles_b = (ext_b + tb - 1) / tb;
+  return dispatch<TransposeLaunch>(d.src_width, d.dst_width, chain, d, ta, tb, tiles_a, tiles_b, nbatch,
+                                   static_cast<cudaStream_t>(stream));
+}
+
+int sbc_fill(void *dst, int64_t count, int32_t width, uint64_t bits, void *stream) {
+  if (count <= 0)
+    return 0;
+  const int64_t blocks = grid_for(count, 256, 8);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (width) {
+  case 1: k_fill<1><<<static_cast<unsigned>(blocks), 256, 0, s>>>(dst, count, bits); break;
+  case 2: k_fill<2><<<static_cast<unsigned>(blocks), 256, 0, s>>>(dst, count, bits); break;
+  case 4: k_fill<4><<<static_cast<unsigned>(blocks), 256, 0, s>>>(dst, count, bits); break;
+  case 8: k_fill<8><<<static_cast<unsigned>(blocks), 256, 0, s>>>(dst, count, bits); break;
+  default: return SBC_EINVAL;
+  }
+  return launched(cudaSuccess);
+}
+
+uint64_t sbc_launch_count(void) { return g_launches.load(); }
+
+} // extern "C"

@@ -1,0 +1,510 @@
+// Lowering of typed programs to the fused sm_100a kernels and the H2D data
+// paths. See device_plan.hpp.
+//
+// Data paths (routes a/b):
+//  * DmaRing: the raw source is cut into chunks of whole source rows (the
+//    coalesced axis with the largest source stride), each chunk DMA'd by the
+//    copy engine into a slot of an HBM ring on the copy stream, and the fused
+//    kernel for that chunk's destination box runs on the compute stream as
+//    soon as the chunk lands. Slot reuse is gated by events, so PCIe DMA of
+//    chunk i+1.. overlaps the kernel of chunk i. A row window on the
+//    destination (multi-GPU shards) whose source is a column range of every
+//    source row is gathered with one 2-D DMA per chunk.
+//  * ZeroCopy: the fused kernel reads mapped pinned host memory directly.
+//  * Staged: one DMA of the (windowed) source, then one kernel.
+// No route transforms data on the CPU.
+#include "device_plan.hpp"
+
+#include <algorithm>
+#include <climits>
+#include <cstring>
+
+namespace reloc {
+namespace b200 {
+namespace {
+
+TransferError terr(const char *code, std::string msg) { return TransferError{code, std::move(msg)}; }
+
+bool isF32(ElementType t) { return t.kind == ElementTypeKind::Float && t.bitwidth == 32; }
+bool isBF16(ElementType t) { return t.kind == ElementTypeKind::BFloat && t.bitwidth == 16; }
+
+int stageOp(const typed::StageArithmetic &s) {
+  switch (s.transform) {
+  case ValueTransformKind::Cast:
+    if (isF32(s.input))
+      return isBF16(s.output) ? SBC_NARROW_BF16 : SBC_NARROW_F16;
+    return isBF16(s.input) ? SBC_WIDEN_BF16 : SBC_WIDEN_F16;
+  case ValueTransformKind::Quantize:
+    return SBC_QUANTIZE;
+  case ValueTransformKind::Dequantize:
+    return SBC_DEQUANTIZE;
+  }
+  return SBC_NARROW_F16;
+}
+
+constexpr size_t kNone = SIZE_MAX;
+constexpr size_t kDefaultChunkBytes = size_t(8) << 20;
+
+} // namespace
+
+const char *familyName(Family f) {
+  switch (f) {
+  case Family::Contiguous: return "contiguous";
+  case Family::Transpose: return "transpose";
+  default: return "generic";
+  }
+}
+
+std::variant<Lowered, TransferError> lower(const typed::Program &p) {
+  Lowered l;
+  sbc_relocate &d = l.desc;
+  std::memset(&d, 0, sizeof d);
+  const BoundPlan &lay = p.plan.layout;
+  const int r = static_cast<int>(lay.extents.size());
+  if (r < 1 || r > SBC_MAX_RANK)
+    return terr("unsupported_layout", "coalesced rank " + std::to_string(r) + " exceeds the device limit of 8");
+  const uint32_t nst = static_cast<uint32_t>(p.stages.size());
+  if (nst > SBC_MAX_STAGES)
+    return terr("unsupported_stage", "more than 4 value stages");
+  auto fill = typed::fillAt(p, nst);
+  if (auto *e = std::get_if<typed::ExecutionError>(&fill))
+    return terr(e->code.c_str(), e->message);
+  const auto &fb = std::get<std::optional<uint64_t>>(fill);
+  d.has_fill = fb.has_value();
+  d.fill_bits = fb.value_or(0);
+  d.rank = r;
+  d.src_width = static_cast<int32_t>(typed::widthAt(p, 0));
+  d.dst_width = static_cast<int32_t>(typed::widthAt(p, nst));
+  for (int k = 0; k < r; ++k) {
+    d.extents[k] = lay.extents[k];
+    d.src_strides[k] = lay.srcStrides[k];
+    d.dst_strides[k] = lay.dstStrides[k];
+  }
+  for (const PadRegion &pr : lay.padRegions)
+    d.pad_lo[pr.axis] = pr.lo;
+  int64_t hiPad[SBC_MAX_RANK] = {};
+  for (const PadRegion &pr : lay.padRegions)
+    hiPad[pr.axis] = pr.hi;
+  l.dstElements = 1;
+  for (int k = 0; k < r; ++k) {
+    l.padded[k] = lay.extents[k] + d.pad_lo[k] + hiPad[k];
+    d.box_lo[k] = 0;
+    d.box_hi[k] = l.padded[k];
+    l.dstElements *= l.padded[k];
+  }
+  l.srcElements = p.sourceElements;
+  // dense row-major destination over the padded box
+  {
+    int64_t expect = 1;
+    l.denseCover = true;
+    for (int k = r - 1; k >= 0; --k) {
+      if (l.padded[k] != 1 && d.dst_strides[k] != expect)
+        l.denseCover = false;
+      expect *= l.padded[k];
+    }
+  }
+  const size_t rr = p.plan.resultExtents.size();
+  if (rr > SBC_MAX_RANK)
+    return terr("unsupported_layout", "result rank exceeds the device limit of 8");
+  d.result_rank = static_cast<int32_t>(rr);
+  for (size_t j = 0; j < rr; ++j) {
+    d.result_extents[j] = p.plan.resultExtents[j];
+    d.result_strides[j] = p.resultStrides[j];
+  }
+  d.nsymbols = static_cast<int32_t>(std::min<size_t>(p.plan.symbols.size(), SBC_MAX_SYMBOLS));
+  for (int i = 0; i < d.nsymbols; ++i)
+    d.symbols[i] = p.plan.symbols[static_cast<size_t>(i)];
+
+  // Stages and the packed parameter blob (reciprocals for quantize).
+  d.nstages = static_cast<int32_t>(nst);
+  bool anyExpr = false, anyOffset = false;
+  for (uint32_t k = 0; k < nst; ++k) {
+    const typed::StageArithmetic &s = p.stages[k];
+    sbc_stage &g = d.stages[k];
+    g.op = stageOp(s);
+    g.channel = SBC_CH_NONE;
+    g.channel_length = s.channelLength;
+    size_t po = kNone, zo = kNone;
+    if (s.transform != ValueTransformKind::Cast) {
+      const std::vector<float> &vals = s.transform == ValueTransformKind::Quantize ? s.invScale : s.scale;
+      po = l.paramBlob.size();
+      l.paramBlob.resize(po + vals.size() * 4);
+      std::memcpy(l.paramBlob.data() + po, vals.data(), vals.size() * 4);
+      if (s.transform == ValueTransformKind::Dequantize && !s.zeroPoint.empty()) {
+        while (l.paramBlob.size() % 4)
+          l.paramBlob.push_back(0);
+        zo = l.paramBlob.size();
+        l.paramBlob.resize(zo + s.zeroPoint.size() * 4);
+        std::memcpy(l.paramBlob.data() + zo, s.zeroPoint.data(), s.zeroPoint.size() * 4);
+        g.zp_mode = s.zeroPoint.size() == 1 ? 1 : 2;
+      }
+    }
+    l.paramOffset.push_back(po);
+    l.zpOffset.push_back(zo);
+    if (!s.perChannel)
+      continue;
+    const ExprStream &ch = p.plan.stages[k].channel;
+    if (s.channelIsDim) {
+      const uint32_t dim = s.channelDim;
+      const int64_t rs = p.resultStrides[dim], re = p.plan.resultExtents[dim];
+      bool placed = false;
+      if (re == 1) {
+        g.channel = SBC_CH_AXIS;
+        g.ch_axis = 0;
+        g.ch_div = 1;
+        g.ch_mod = 1;
+        placed = true;
+      } else if (l.denseCover) {
+        for (int a = 0; a < r && !placed; ++a) {
+          const int64_t ds = d.dst_strides[a];
+          if (l.padded[a] == 1 || ds > rs || rs % ds != 0 || rs >= ds * l.padded[a])
+            continue;
+          const int64_t div = rs / ds;
+          g.channel = SBC_CH_AXIS;
+          g.ch_axis = a;
+          g.ch_div = div;
+          g.ch_mod = (div * re == l.padded[a]) ? 0 : re;
+          placed = true;
+        }
+      }
+      if (!placed) {
+        g.channel = SBC_CH_OFFSET;
+        g.ch_dim = static_cast<int32_t>(dim);
+        anyOffset = true;
+      }
+      // static range proof: the coordinate never exceeds its extent
+      if (re > s.channelLength)
+        l.needsStatus = true;
+    } else {
+      if (ch.size() > SBC_MAX_TOKENS)
+        return terr("implementation_unavailable", "channel expression longer than 16 tokens");
+      for (const ExprToken &t : ch)
+        if (t.op == ExprOp::PushSym && t.value >= SBC_MAX_SYMBOLS)
+          return terr("implementation_unavailable", "channel expression uses more than 8 symbols");
+      g.channel = SBC_CH_EXPR;
+      g.ntokens = static_cast<int32_t>(ch.size());
+      for (size_t i = 0; i < ch.size(); ++i) {
+        g.token_op[i] = static_cast<int32_t>(ch[i].op);
+        g.token_value[i] = ch[i].value;
+      }
+      anyExpr = true;
+      l.needsStatus = true;
+    }
+  }
+
+  // Kernel family.
+  l.family = Family::Generic;
+  if (!anyExpr) {
+    if (r == 1 && d.src_strides[0] == 1 && d.dst_strides[0] == 1 && !anyOffset)
+      l.family = Family::Contiguous;
+    else if ((r == 2 || r == 3) && d.src_strides[r - 2] == 1 && d.dst_strides[r - 1] == 1 && l.padded[r - 1] > 1 &&
+             l.padded[r - 2] > 1)
+      l.family = Family::Transpose;
+  }
+  if (d.src_width == 8 || d.dst_width == 8)
+    l.family = Family::Generic;
+
+  // Source rows: the axis with the largest source stride, if the source is
+  // dense and that axis is outermost (each row is one contiguous block).
+  int64_t best = -1;
+  for (int k = 0; k < r; ++k)
+    if (lay.extents[k] > 1 && d.src_strides[k] > best) {
+      best = d.src_strides[k];
+      l.srcOuter = k;
+    }
+  if (l.srcOuter >= 0) {
+    const int o = l.srcOuter;
+    int64_t span = 0;
+    for (int k = 0; k < r; ++k)
+      if (k != o)
+        span += (lay.extents[k] - 1) * d.src_strides[k];
+    l.rowsChunkable = d.src_strides[o] * lay.extents[o] == l.srcElements && span < d.src_strides[o];
+  }
+  l.classKey = std::string(familyName(l.family)) + ":" + std::to_string(d.src_width) + ">" +
+               std::to_string(d.dst_width) + ":" + std::to_string(nst) + ":" +
+               std::to_string(64 - __builtin_clzll(static_cast<unsigned long long>(l.srcElements * d.src_width) | 1));
+  return l;
+}
+
+std::optional<TransferError> uploadParams(const Lowered &l, CudaBackend &b, sbc_relocate &d) {
+  if (l.paramBlob.empty())
+    return std::nullopt;
+  auto *base = static_cast<uint8_t *>(b.params(l.paramBlob.size()));
+  if (!base)
+    return terr("backend_failure", b.error());
+  // Pageable source: the driver stages it before returning, and the copy is
+  // ordered on the compute stream after every earlier reader of the buffer.
+  const int rc = sbc_memcpy_h2d_async(base, l.paramBlob.data(), l.paramBlob.size(), b.computeStream());
+  if (rc) {
+    b.fail("parameter upload", rc);
+    return terr("backend_failure", b.error());
+  }
+  ++b.copyCalls;
+  for (int k = 0; k < d.nstages; ++k) {
+    if (l.paramOffset[static_cast<size_t>(k)] != kNone)
+      d.stages[k].param = reinterpret_cast<const float *>(base + l.paramOffset[static_cast<size_t>(k)]);
+    if (l.zpOffset[static_cast<size_t>(k)] != kNone)
+      d.stages[k].zero_point = reinterpret_cast<const int32_t *>(base + l.zpOffset[static_cast<size_t>(k)]);
+  }
+  return std::nullopt;
+}
+
+namespace {
+
+/// Launch the family kernel for `d` on the compute stream.
+std::optional<TransferError> launch(const Lowered &l, CudaBackend &b, const sbc_relocate &d, RunStats &st) {
+  int rc = SBC_EUNSUPPORTED;
+  if (l.family == Family::Contiguous)
+    rc = sbc_relocate_contiguous(&d, b.computeStream());
+  else if (l.family == Family::Transpose)
+    rc = sbc_relocate_transpose(&d, b.computeStream());
+  if (rc == SBC_EUNSUPPORTED)
+    rc = sbc_relocate_generic(&d, b.computeStream());
+  if (rc) {
+    b.fail("relocation kernel", rc);
+    return terr("backend_failure", b.error());
+  }
+  ++st.launches;
+  ++b.kernelLaunches;
+  return std::nullopt;
+}
+
+/// Apply the row window to the descriptor's axis-0 box and destination rebase.
+bool applyWindow(const Lowered &l, sbc_relocate &d, RowWindow w) {
+  const int64_t end = w.end < 0 ? l.padded[0] : w.end;
+  if (w.begin < 0 || end > l.padded[0] || end < w.begin)
+    return false;
+  d.box_lo[0] = w.begin;
+  d.box_hi[0] = end;
+  d.dst_offset = w.begin * d.dst_strides[0];
+  return true;
+}
+
+bool isWhole(const Lowered &l, RowWindow w) { return w.begin == 0 && (w.end < 0 || w.end == l.padded[0]); }
+
+std::optional<TransferError> prefill(const Lowered &l, CudaBackend &b, void *ddst, RowWindow w, RunStats &st) {
+  // Gather kernels write exactly the box; a destination the box does not
+  // cover densely gets the fill first (the reference fills, then walks).
+  if (!l.desc.has_fill || l.denseCover || !isWhole(l, w))
+    return std::nullopt;
+  const int rc = sbc_fill(ddst, l.dstElements, l.desc.dst_width, l.desc.fill_bits, b.computeStream());
+  if (rc) {
+    b.fail("fill kernel", rc);
+    return terr("backend_failure", b.error());
+  }
+  ++st.launches;
+  ++b.kernelLaunches;
+  return std::nullopt;
+}
+
+std::optional<TransferError> zeroStatus(const Lowered &l, CudaBackend &b, sbc_relocate &d) {
+  if (!l.needsStatus)
+    return std::nullopt;
+  d.status = b.statusWord();
+  const int rc = sbc_fill(b.statusWord(), 1, 4, 0, b.computeStream());
+  if (rc) {
+    b.fail("status reset", rc);
+    return terr("backend_failure", b.error());
+  }
+  return std::nullopt;
+}
+
+} // namespace
+
+std::optional<TransferError> runDevice(const Lowered &l, CudaBackend &b, const void *dsrc, void *ddst, RowWindow w,
+                                       RunStats &st) {
+  sbc_relocate d = l.desc;
+  if (!applyWindow(l, d, w))
+    return terr("invalid_options", "row window outside the padded result");
+  if (auto e = uploadParams(l, b, d))
+    return e;
+  if (auto e = zeroStatus(l, b, d))
+    return e;
+  if (auto e = prefill(l, b, ddst, w, st))
+    return e;
+  d.src = dsrc;
+  d.dst = ddst;
+  st.kernel = familyName(l.family);
+  return launch(l, b, d, st);
+}
+
+Route chooseRoute(const Lowered &l, CudaBackend &b, const void *hsrc, const TransferOptions &o) {
+  if (o.route != Route::Auto)
+    return o.route;
+  int kind = 0, dev = -1;
+  void *mapped = nullptr;
+  const bool pinned = sbc_pointer_info(hsrc, &kind, &dev) == 0 && kind == 1 &&
+                      sbc_host_device_pointer(const_cast<void *>(hsrc), &mapped) == 0;
+  if (!l.rowsChunkable)
+    return pinned ? Route::ZeroCopy : Route::Staged;
+  if (!pinned)
+    return Route::DmaRing;
+  auto &s = b.routeStats[l.classKey];
+  if (s.dmaSecondsPerByte < 0)
+    return Route::DmaRing;
+  if (s.zeroCopySecondsPerByte < 0)
+    return Route::ZeroCopy;
+  return s.zeroCopySecondsPerByte < s.dmaSecondsPerByte ? Route::ZeroCopy : Route::DmaRing;
+}
+
+std::optional<TransferError> runH2D(const Lowered &l, CudaBackend &b, const void *hsrc, void *ddst, Route route,
+                                    RowWindow w, const TransferOptions &o, RunStats &st) {
+  const int r = l.desc.rank;
+  const int ws = l.desc.src_width;
+  if (route == Route::ZeroCopy) {
+    void *mapped = nullptr;
+    const int rc = sbc_host_device_pointer(const_cast<void *>(hsrc), &mapped);
+    if (rc)
+      return terr("invalid_view", "zero_copy needs a mapped pinned host source");
+    st.route = "zero_copy";
+    st.payloadBytes += l.srcElements * ws; // upper bound: the window may read less
+    return runDevice(l, b, mapped, ddst, w, st);
+  }
+
+  sbc_relocate base = l.desc;
+  if (!applyWindow(l, base, w))
+    return terr("invalid_options", "row window outside the padded result");
+  if (auto e = uploadParams(l, b, base))
+    return e;
+  if (auto e = zeroStatus(l, b, base))
+    return e;
+  if (auto e = prefill(l, b, ddst, w, st))
+    return e;
+  base.dst = ddst;
+  st.kernel = familyName(l.family);
+
+  // Chunk axis and source compaction mode.
+  //  rows   : chunk = whole source rows along srcOuter (window on axis 0
+  //           allowed only when srcOuter == 0): one contiguous DMA
+  //  rows2d : rank-2 layout, window on axis 0 (source stride 1) and chunks
+  //           along axis 1: one 2-D DMA of the window's columns per chunk
+  //  whole  : one DMA of the entire source, one kernel
+  enum class Mode { Rows, Rows2D, Whole } mode = Mode::Whole;
+  const int o_ax = l.srcOuter;
+  if (route != Route::Staged && l.rowsChunkable && o_ax >= 0) {
+    if (isWhole(l, w) || o_ax == 0)
+      mode = Mode::Rows;
+    else if (r == 2 && o_ax == 1 && l.desc.src_strides[0] == 1)
+      mode = Mode::Rows2D;
+  }
+  if (route == Route::Staged && r == 2 && o_ax == 1 && l.rowsChunkable && !isWhole(l, w) &&
+      l.desc.src_strides[0] == 1)
+    mode = Mode::Rows2D; // one chunk of the window's columns
+
+  if (mode == Mode::Whole) {
+    const size_t bytes = static_cast<size_t>(l.srcElements) * ws;
+    void *stage = b.staging(bytes ? bytes : 16);
+    if (!stage)
+      return terr("backend_failure", b.error());
+    int rc;
+    if ((rc = sbc_stream_wait_event(b.copyStream(), b.stagingFree())) ||
+        (rc = sbc_memcpy_h2d_async(stage, hsrc, bytes, b.copyStream())) ||
+        (rc = sbc_event_record(b.stagingReady(), b.copyStream())) ||
+        (rc = sbc_stream_wait_event(b.computeStream(), b.stagingReady()))) {
+      b.fail("staged upload", rc);
+      return terr("backend_failure", b.error());
+    }
+    ++b.copyCalls;
+    ++st.copies;
+    st.route = "staged";
+    st.chunks = 1;
+    st.chunkBytes = bytes;
+    st.buffers = 1;
+    st.payloadBytes += static_cast<int64_t>(bytes);
+    sbc_relocate d = base;
+    d.src = stage;
+    if (auto e = launch(l, b, d, st))
+      return e;
+    if ((rc = sbc_event_record(b.stagingFree(), b.computeStream()))) {
+      b.fail("staging release", rc);
+      return terr("backend_failure", b.error());
+    }
+    return std::nullopt;
+  }
+
+  // Chunked ring.
+  const int ax = mode == Mode::Rows ? o_ax : 1;
+  const int64_t lo = l.desc.pad_lo[ax], E = l.desc.extents[ax];
+  const int64_t B0 = base.box_lo[ax], B1 = base.box_hi[ax];
+  const int64_t V0 = std::max(B0, lo), V1 = std::min(B1, lo + E); // valid padded rows in the box
+  // Window columns (rows2d): valid source coordinates of axis 0.
+  int64_t c0 = 0, c1 = 0;
+  if (mode == Mode::Rows2D) {
+    c0 = std::max<int64_t>(base.box_lo[0] - l.desc.pad_lo[0], 0);
+    c1 = std::min<int64_t>(base.box_hi[0] - l.desc.pad_lo[0], l.desc.extents[0]);
+    if (c1 < c0)
+      c1 = c0;
+  }
+  const int64_t rowElems = mode == Mode::Rows ? l.desc.src_strides[ax] : (c1 - c0);
+  const int64_t rowBytes = std::max<int64_t>(rowElems * ws, 1);
+  const size_t target = o.chunkSizeOverride ? o.chunkSizeOverride : kDefaultChunkBytes;
+  int64_t rowsPer = std::max<int64_t>(1, static_cast<int64_t>(target) / rowBytes);
+  const int slots = std::max(2, o.nBuffers);
+  if (mode == Mode::Whole || route == Route::Staged)
+    rowsPer = std::max<int64_t>(1, V1 - V0);
+  if (!b.ensureRing(slots, static_cast<size_t>(rowsPer * rowBytes)))
+    return terr("backend_failure", b.error());
+  st.route = route == Route::Staged ? "staged" : "dma_ring";
+  st.buffers = static_cast<size_t>(slots);
+  st.chunkBytes = static_cast<size_t>(rowsPer * rowBytes);
+
+  if (V1 <= V0) { // the box holds only pad rows: no source needed
+    sbc_relocate d = base;
+    d.src = nullptr;
+    st.chunks = 1;
+    return launch(l, b, d, st);
+  }
+  int64_t i = 0;
+  for (int64_t r0 = V0; r0 < V1; r0 += rowsPer, ++i) {
+    const int64_t r1 = std::min(r0 + rowsPer, V1);
+    const int s = static_cast<int>(i % slots);
+    void *slot = b.slot(s);
+    int rc;
+    if ((rc = sbc_stream_wait_event(b.copyStream(), b.slotFree(s)))) {
+      b.fail("ring wait", rc);
+      return terr("backend_failure", b.error());
+    }
+    const int64_t v0 = r0 - lo, v1 = r1 - lo; // source rows
+    if (mode == Mode::Rows) {
+      const auto *src = static_cast<const uint8_t *>(hsrc) + v0 * rowBytes;
+      rc = sbc_memcpy_h2d_async(slot, src, static_cast<size_t>((v1 - v0) * rowBytes), b.copyStream());
+    } else {
+      const int64_t S1 = l.desc.src_strides[1];
+      const auto *src = static_cast<const uint8_t *>(hsrc) + (v0 * S1 + c0) * ws;
+      rc = sbc_memcpy_h2d_2d_async(slot, static_cast<size_t>(rowBytes), src, static_cast<size_t>(S1 * ws),
+                                   static_cast<size_t>((c1 - c0) * ws), static_cast<size_t>(v1 - v0), b.copyStream());
+    }
+    if (rc || (rc = sbc_event_record(b.slotReady(s), b.copyStream())) ||
+        (rc = sbc_stream_wait_event(b.computeStream(), b.slotReady(s)))) {
+      b.fail("ring upload", rc);
+      return terr("backend_failure", b.error());
+    }
+    ++b.copyCalls;
+    ++st.copies;
+    b.eventRecords += 1;
+    b.eventWaits += 2;
+    st.payloadBytes += (v1 - v0) * rowBytes;
+    sbc_relocate d = base;
+    d.box_lo[ax] = (r0 == V0) ? B0 : r0;
+    d.box_hi[ax] = (r1 == V1) ? B1 : r1;
+    d.src = slot;
+    if (mode == Mode::Rows) {
+      d.src_offset = v0 * l.desc.src_strides[ax];
+    } else {
+      d.src_strides[1] = c1 - c0;
+      d.src_offset = v0 * (c1 - c0) + c0;
+    }
+    if (auto e = launch(l, b, d, st))
+      return e;
+    if ((rc = sbc_event_record(b.slotFree(s), b.computeStream()))) {
+      b.fail("ring release", rc);
+      return terr("backend_failure", b.error());
+    }
+    ++b.eventRecords;
+  }
+  st.chunks = static_cast<size_t>(i);
+  return std::nullopt;
+}
+
+} // namespace b200
+} // namespace reloc

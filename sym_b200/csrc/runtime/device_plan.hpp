@@ -1,0 +1,74 @@
+// Lowering of a checked typed program to the fused device kernels, and the
+// H2D execution engine (DMA ring, zero copy, staged) built on it.
+#ifndef SYM_B200_DEVICE_PLAN_HPP
+#define SYM_B200_DEVICE_PLAN_HPP
+
+#include "reloc/CudaBackend.h"
+#include "reloc/Dispatch.h"
+#include "reloc/TypedExecute.h"
+
+#include "sb_cuda.h"
+
+#include <optional>
+#include <string>
+#include <variant>
+#include <vector>
+
+namespace reloc {
+namespace b200 {
+
+enum class Family { Generic = 0, Contiguous = 1, Transpose = 2 };
+const char *familyName(Family f);
+
+/// A program in device-ready form. `desc` carries the full padded box and
+/// everything but pointers; parameter arrays are packed into `paramBlob`.
+struct Lowered {
+  sbc_relocate desc{};
+  Family family = Family::Generic;
+  int64_t padded[SBC_MAX_RANK] = {};
+  bool denseCover = false;  // dst strides are dense row-major over the padded box
+  int srcOuter = -1;        // axis whose source rows are contiguous blocks
+  bool rowsChunkable = false;
+  int64_t srcElements = 0;  // dense source elements
+  int64_t dstElements = 0;
+  bool needsStatus = false; // a channel map is checked on the device
+  std::vector<uint8_t> paramBlob;
+  std::vector<size_t> paramOffset, zpOffset; // per stage, SIZE_MAX = none
+  std::string classKey; // route-measurement class
+};
+
+std::variant<Lowered, TransferError> lower(const typed::Program &program);
+
+/// A window of physical (padded) rows of axis 0; {0, padded[0]} = whole.
+struct RowWindow {
+  int64_t begin = 0, end = -1;
+};
+
+struct RunStats {
+  std::string route, kernel;
+  uint64_t launches = 0, copies = 0;
+  size_t chunks = 0, chunkBytes = 0, buffers = 0;
+  int64_t payloadBytes = 0;
+};
+
+/// Device source: the transform alone (source already in HBM). Enqueued on
+/// the backend's compute stream.
+std::optional<TransferError> runDevice(const Lowered &l, CudaBackend &b, const void *dsrc, void *ddst,
+                                       RowWindow window, RunStats &stats);
+
+/// Host source -> device destination through `route` (Auto resolved by the
+/// caller). Enqueued on the backend's streams; the caller orders/blocks.
+std::optional<TransferError> runH2D(const Lowered &l, CudaBackend &b, const void *hsrc, void *ddst, Route route,
+                                    RowWindow window, const TransferOptions &options, RunStats &stats);
+
+/// Resolve Route::Auto for this plan class on this backend (measurement-
+/// driven; see dispatch.cpp).
+Route chooseRoute(const Lowered &l, CudaBackend &b, const void *hsrc, const TransferOptions &options);
+
+/// Upload the parameter blob and patch the stage pointers of `desc`.
+std::optional<TransferError> uploadParams(const Lowered &l, CudaBackend &b, sbc_relocate &desc);
+
+} // namespace b200
+} // namespace reloc
+
+#endif

@@ -1,0 +1,334 @@
+// Capability rows, selection, request validation and execution for the B200
+// rows; see include/reloc/Dispatch.h. Contracts follow the reference's
+// libreloc/src/Dispatch.cpp (queryCapability :1382-1533, select :1147,
+// prepareDispatch :1585-1620, executeDispatch :1983-2048): pure capability,
+// policy over eligible rows only, single-use requests, errors by value, no
+// second path after data dispatch.
+#include "reloc/Dispatch.h"
+#include "reloc/CudaBackend.h"
+
+#include "device_plan.hpp"
+#include "sb_cuda.h"
+
+#include <cstring>
+
+namespace reloc {
+namespace dispatch {
+namespace {
+
+TransferError terr(const char *code, std::string msg) { return TransferError{code, std::move(msg)}; }
+
+const char *const kCpuExcluded = "the B200 executor runs no supported plan on the CPU";
+
+Implementation b200Row(const typed::Program &p, const char *variant, const b200::Lowered *l) {
+  Implementation row;
+  row.id = kB200FusedH2D;
+  row.variant = variant;
+  row.wireBoundary = 0; // the raw source crosses the link
+  row.wireResultLayout = false;
+  row.wireBytes = p.plan.sourceBytes;
+  row.deviceTempBytes = 0;
+  row.method = "B";
+  (void)l;
+  return row;
+}
+
+} // namespace
+
+Capability queryCapability(const typed::Program &p, TransferDirection direction, bool cuda) {
+  Capability cap;
+  const uint32_t n = static_cast<uint32_t>(p.stages.size());
+  cap.excluded.push_back({kCpuReference, kCpuExcluded});
+  for (uint32_t k = 0; k <= n; ++k)
+    cap.excluded.push_back({std::string(kCpuStagesCudaStages) + "@" + std::to_string(k), kCpuExcluded});
+  cap.excluded.push_back({kCudaDequantRelocate, "superseded by b200_fused_h2d"});
+  cap.excluded.push_back({kCudaRelocateF32, "superseded by b200_fused_h2d"});
+  if (direction == TransferDirection::DeviceToHost) {
+    cap.excluded.push_back({kB200FusedH2D, "device-to-host transfers are outside this executor"});
+    return cap;
+  }
+  if (!cuda) {
+    cap.excluded.push_back({kB200FusedH2D, "no CUDA device end"});
+    return cap;
+  }
+  auto lowered = b200::lower(p);
+  if (auto *e = std::get_if<TransferError>(&lowered)) {
+    cap.excluded.push_back({kB200FusedH2D, e->code + ": " + e->message});
+    return cap;
+  }
+  const auto &l = std::get<b200::Lowered>(lowered);
+  cap.eligible.push_back(b200Row(p, "", &l));
+  cap.eligible.push_back(b200Row(p, "dma_ring", &l));
+  cap.eligible.push_back(b200Row(p, "zero_copy", &l));
+  return cap;
+}
+
+std::variant<Selection, TransferError> selectImplementation(const typed::Program &p, TransferDirection direction,
+                                                            const Options &o) {
+  const Capability cap = queryCapability(p, direction, o.cuda);
+  Selection sel;
+  if (!o.implementation.empty()) {
+    for (const Implementation &row : cap.eligible)
+      if (row.label() == o.implementation) {
+        sel.row = row;
+        sel.policy = "explicit";
+        sel.reason = "explicit";
+        return sel;
+      }
+    std::string why = "not an eligible row";
+    for (const Exclusion &e : cap.excluded)
+      if (e.id == o.implementation)
+        why = e.reason;
+    return terr("implementation_unavailable", o.implementation + ": " + why);
+  }
+  if (o.policy == Policy::OriginalCpu)
+    return terr("implementation_unavailable", std::string("original_cpu: ") + kCpuExcluded);
+  if (cap.eligible.empty()) {
+    std::string why;
+    for (const Exclusion &e : cap.excluded)
+      if (e.id == kB200FusedH2D)
+        why = e.reason;
+    return terr("implementation_unavailable", "no eligible row: " + why);
+  }
+  sel.row = cap.eligible.front();
+  sel.policy = "auto";
+  sel.reason = "b200_gpu_only";
+  return sel;
+}
+
+std::variant<DispatchTemplate, TransferError> prepareDispatchTemplate(const TypedBoundPlan &plan,
+                                                                      TransferDirection direction, const Options &o) {
+  auto prog = typed::prepareProgram(plan);
+  if (auto *e = std::get_if<typed::ExecutionError>(&prog))
+    return terr(e->code.c_str(), e->message);
+  DispatchTemplate t;
+  t.program = std::get<typed::Program>(std::move(prog));
+  t.direction = direction;
+  t.cuda = o.cuda;
+  t.capability = queryCapability(t.program, direction, o.cuda);
+  auto sel = selectImplementation(t.program, direction, o);
+  if (auto *e = std::get_if<TransferError>(&sel))
+    return *e;
+  t.selection = std::get<Selection>(std::move(sel));
+  auto lowered = b200::lower(t.program);
+  if (auto *e = std::get_if<TransferError>(&lowered))
+    return *e;
+  t.lowered = std::make_shared<const b200::Lowered>(std::get<b200::Lowered>(std::move(lowered)));
+  return t;
+}
+
+namespace {
+
+/// The views must be the plan's dense tensors: row-major, the bound extents,
+/// the boundary element width, enough capacity.
+std::optional<TransferError> checkView(const BufferView &v, const std::vector<int64_t> &extents, uint32_t width,
+                                       int64_t bytes, MemoryKind kind, const char *role) {
+  if (v.kind != kind)
+    return terr("direction_mismatch", std::string(role) + " memory kind does not match the transfer direction");
+  if (v.base == 0)
+    return terr("invalid_view", std::string(role) + " base is null");
+  if (v.elementSize != width)
+    return terr("plan_mismatch", std::string(role) + " element size " + std::to_string(v.elementSize) +
+                                     " differs from the plan's " + std::to_string(width));
+  if (v.extents != extents)
+    return terr("plan_mismatch", std::string(role) + " extents differ from the bound plan");
+  if (v.strides.size() != extents.size())
+    return terr("invalid_view", std::string(role) + " strides and extents differ in rank");
+  int64_t expect = 1;
+  for (size_t k = extents.size(); k-- > 0;) {
+    if (extents[k] != 1 && v.strides[k] != expect)
+      return terr("unsupported_layout", std::string(role) + " must be dense row-major");
+    expect *= extents[k];
+  }
+  if (v.offsetBytes > v.capacityBytes || static_cast<int64_t>(v.capacityBytes - v.offsetBytes) < bytes)
+    return terr("insufficient_capacity", std::string(role) + " allocation is smaller than the plan's " +
+                                             std::to_string(bytes) + " bytes");
+  return std::nullopt;
+}
+
+} // namespace
+
+std::variant<DispatchRequest, TransferError> prepareDispatch(const DispatchTemplate &t, const BufferView &src,
+                                                             const BufferView &dst) {
+  if (t.direction != TransferDirection::HostToDevice)
+    return terr("implementation_unavailable", "device-to-host transfers are outside this executor");
+  const typed::Program &p = t.program;
+  const uint32_t n = static_cast<uint32_t>(p.stages.size());
+  if (auto e = checkView(src, p.plan.sourceExtents, typed::widthAt(p, 0), p.plan.sourceBytes, MemoryKind::Host,
+                         "source"))
+    return *e;
+  if (auto e = checkView(dst, p.plan.resultExtents, typed::widthAt(p, n), p.plan.destinationBytes, MemoryKind::Cuda,
+                         "destination"))
+    return *e;
+  DispatchRequest r;
+  r.program = p;
+  r.source = src;
+  r.destination = dst;
+  r.direction = t.direction;
+  r.selected = t.selection.row;
+  r.lowered = t.lowered;
+  Report &rep = r.report;
+  rep.implementation = t.selection.row.label();
+  rep.policy = t.selection.policy;
+  rep.placementReason = t.selection.reason;
+  rep.method = t.selection.row.method;
+  rep.wireBoundary = t.selection.row.wireBoundary;
+  rep.sourceBytes = p.plan.sourceBytes;
+  rep.wireBytes = t.selection.row.wireBytes;
+  rep.destinationBytes = p.plan.destinationBytes;
+  rep.parameterBytes = p.plan.parameterBytes;
+  return r;
+}
+
+std::variant<DispatchRequest, TransferError> prepareDispatch(const TypedBoundPlan &plan, const BufferView &src,
+                                                             const BufferView &dst, TransferDirection direction,
+                                                             const Options &o) {
+  auto t = prepareDispatchTemplate(plan, direction, o);
+  if (auto *e = std::get_if<TransferError>(&t))
+    return *e;
+  return prepareDispatch(std::get<DispatchTemplate>(t), src, dst);
+}
+
+namespace {
+
+Route routeOf(const Implementation &row, const TransferOptions &o) {
+  if (row.variant == "dma_ring")
+    return Route::DmaRing;
+  if (row.variant == "zero_copy")
+    return Route::ZeroCopy;
+  return o.route;
+}
+
+/// Shared tail of a blocking execution: wait, read the status word, learn
+/// the route timing.
+std::optional<TransferError> finish(const b200::Lowered &l, CudaBackend &b, const TransferOptions &o, bool timed,
+                                    Route route, int64_t bytes) {
+  if (!b.signalStream(o.hasCallerStream ? o.callerStream : nullptr))
+    return terr("backend_failure", b.error());
+  if (o.asyncCompletion && !l.needsStatus && !timed)
+    return std::nullopt;
+  int rc = sbc_event_synchronize(b.doneEvent());
+  if (rc) {
+    b.fail("completion", rc);
+    return terr("backend_failure", b.error());
+  }
+  if (timed) {
+    float ms = 0;
+    if (sbc_event_elapsed_ms(b.startEvent(), b.stopEvent(), &ms) == 0 && bytes > 0) {
+      auto &s = b.routeStats[l.classKey];
+      const double spb = (ms * 1e-3) / static_cast<double>(bytes);
+      if (route == Route::DmaRing)
+        s.dmaSecondsPerByte = spb;
+      else if (route == Route::ZeroCopy)
+        s.zeroCopySecondsPerByte = spb;
+    }
+  }
+  if (l.needsStatus) {
+    if ((rc = sbc_memcpy_d2h_async(b.statusHost(), b.statusWord(), 4, b.computeStream())) ||
+        (rc = sbc_stream_synchronize(b.computeStream()))) {
+      b.fail("status readback", rc);
+      return terr("backend_failure", b.error());
+    }
+    if (*b.statusHost())
+      return terr("channel_out_of_range", "a channel index fell outside its parameter table");
+  }
+  return std::nullopt;
+}
+
+} // namespace
+
+std::optional<TransferError> executeDispatch(DispatchRequest &req, CudaBackend &b, const TransferOptions &o) {
+  if (req.consumed)
+    return terr("already_executed", "dispatch requests are single-use");
+  req.consumed = true;
+  if (!req.lowered)
+    return terr("implementation_unavailable", "request has no lowered program");
+  if (req.destination.device != b.device())
+    return terr("device_mismatch", "destination lives on cuda:" + std::to_string(req.destination.device) +
+                                       ", the context on cuda:" + std::to_string(b.device()));
+  if (b.failed())
+    return terr("backend_failure", b.error());
+  if (!b.activate())
+    return terr("backend_failure", b.error());
+  const b200::Lowered &l = *req.lowered;
+  const void *src = reinterpret_cast<const void *>(req.source.base + req.source.offsetBytes);
+  void *dst = reinterpret_cast<void *>(req.destination.base + req.destination.offsetBytes);
+  if (o.hasCallerStream && !b.waitStream(o.callerStream))
+    return terr("backend_failure", b.error());
+  TransferOptions ro = o;
+  ro.route = routeOf(req.selected, o);
+  const Route route = b200::chooseRoute(l, b, src, ro);
+  // Auto mode learns each route's cost per plan class from event timings.
+  const bool timed = ro.route == Route::Auto && !o.asyncCompletion;
+  if (timed)
+    sbc_event_record(b.startEvent(), b.copyStream());
+  b200::RunStats st;
+  const uint64_t copies0 = b.copyCalls, launches0 = b.kernelLaunches;
+  if (auto e = b200::runH2D(l, b, src, dst, route, b200::RowWindow{}, ro, st))
+    return e;
+  if (timed)
+    sbc_event_record(b.stopEvent(), b.computeStream());
+  Report &rep = req.report;
+  rep.executed = true;
+  rep.route = st.route;
+  rep.deviceKernel = st.kernel;
+  rep.hostPipeline = st.route;
+  rep.hostChunks = st.chunks;
+  rep.hostChunkBytes = st.chunkBytes;
+  rep.hostBuffers = st.buffers;
+  rep.payloadBytesTransferred = st.payloadBytes + static_cast<int64_t>(l.paramBlob.size());
+  rep.kernelLaunches = b.kernelLaunches - launches0;
+  rep.copyCalls = b.copyCalls - copies0;
+  rep.implementation = req.selected.variant.empty() ? std::string(kB200FusedH2D) + "@" + st.route
+                                                    : req.selected.label();
+  return finish(l, b, o, timed, route, req.program.plan.sourceBytes);
+}
+
+std::optional<TransferError> executeWindow(const DispatchTemplate &t, CudaBackend &b, const void *src, bool hostSource,
+                                           void *dst, int64_t rowBegin, int64_t rowEnd, const TransferOptions &o,
+                                           Report &rep) {
+  if (!t.lowered)
+    return terr("implementation_unavailable", "template has no lowered program");
+  if (b.failed())
+    return terr("backend_failure", b.error());
+  if (!b.activate())
+    return terr("backend_failure", b.error());
+  const b200::Lowered &l = *t.lowered;
+  if (rowBegin < 0 || rowEnd > l.padded[0] || rowEnd < rowBegin)
+    return terr("invalid_options", "row window outside the padded result rows [0, " + std::to_string(l.padded[0]) +
+                                       ")");
+  if (rowEnd == rowBegin)
+    return std::nullopt;
+  if (o.hasCallerStream && !b.waitStream(o.callerStream))
+    return terr("backend_failure", b.error());
+  b200::RunStats st;
+  const uint64_t copies0 = b.copyCalls, launches0 = b.kernelLaunches;
+  std::optional<TransferError> e;
+  if (hostSource) {
+    TransferOptions ro = o;
+    ro.route = routeOf(t.selection.row, o);
+    if (ro.route == Route::Auto)
+      ro.route = Route::DmaRing;
+    e = b200::runH2D(l, b, src, dst, ro.route, b200::RowWindow{rowBegin, rowEnd}, ro, st);
+  } else {
+    st.route = "device";
+    e = b200::runDevice(l, b, src, dst, b200::RowWindow{rowBegin, rowEnd}, st);
+  }
+  if (e)
+    return e;
+  rep.executed = true;
+  rep.route = st.route;
+  rep.deviceKernel = st.kernel;
+  rep.hostChunks = st.chunks;
+  rep.hostChunkBytes = st.chunkBytes;
+  rep.hostBuffers = st.buffers;
+  rep.payloadBytesTransferred = st.payloadBytes + static_cast<int64_t>(l.paramBlob.size());
+  rep.kernelLaunches = b.kernelLaunches - launches0;
+  rep.copyCalls = b.copyCalls - copies0;
+  rep.sourceBytes = t.program.plan.sourceBytes;
+  rep.destinationBytes = t.program.plan.destinationBytes;
+  return finish(l, b, o, false, Route::Auto, 0);
+}
+
+} // namespace dispatch
+} // namespace reloc

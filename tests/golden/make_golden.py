@@ -54,7 +54,8 @@ def typed_corpus(corpus: Path):
                 "footprints": b.get("footprints"),
             })
         cases.append({"name": meta["name"], "blob": blob.hex(), "parameters": params,
-                      "bindings": bindings, "stages": meta.get("stages")})
+                      "bindings": bindings, "stages": meta.get("stages"),
+                      "recipe": meta.get("recipe")})
     return cases
 
 
