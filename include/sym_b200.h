@@ -130,6 +130,10 @@ int sb_execute_rows(const sb_template *tmpl, sb_resources *resources, int32_t de
 int sb_resources_create(uint64_t max_retained_bytes, uint64_t max_live_bytes, uint32_t max_contexts,
                         sb_resources **out, sb_error *err);
 int sb_resources_stats(const sb_resources *resources, char *json, size_t cap);
+/* The copy-engine and compute streams (cudaStream_t) of the context of
+ * `device`, created on first use; for callers that time or order work on them. */
+int sb_resources_streams(sb_resources *resources, int32_t device, void **copy_stream, void **compute_stream,
+                         sb_error *err);
 int sb_resources_clear(sb_resources *resources, sb_error *err);
 int sb_resources_close(sb_resources *resources, sb_error *err);
 void sb_resources_free(sb_resources *resources);

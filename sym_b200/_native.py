@@ -83,6 +83,7 @@ def lib():
                                            ctypes.c_char_p, sz, ep]),
         "sb_resources_create": (ctypes.c_int, [u64, u64, ctypes.c_uint32, pp, ep]),
         "sb_resources_stats": (ctypes.c_int, [vp, ctypes.c_char_p, sz]),
+        "sb_resources_streams": (ctypes.c_int, [vp, i32, pp, pp, ep]),
         "sb_resources_clear": (ctypes.c_int, [vp, ep]),
         "sb_resources_close": (ctypes.c_int, [vp, ep]),
         "sb_resources_free": (None, [vp]),

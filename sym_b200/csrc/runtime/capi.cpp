@@ -569,6 +569,18 @@ int sb_resources_stats(const sb_resources *r, char *json, size_t cap) {
   return putJson(os.str(), json, cap);
 }
 
+int sb_resources_streams(sb_resources *r, int32_t device, void **copy_stream, void **compute_stream,
+                         sb_error *err) {
+  auto out = r->res.withContext(device, [&](CudaBackend &b) -> std::optional<TransferError> {
+    *copy_stream = b.copyStream();
+    *compute_stream = b.computeStream();
+    return std::nullopt;
+  });
+  if (out.error)
+    return setErr(err, out.error->code, out.error->message);
+  return 0;
+}
+
 int sb_resources_clear(sb_resources *r, sb_error *err) {
   if (auto e = r->res.clear())
     return setErr(err, e->code, e->message);

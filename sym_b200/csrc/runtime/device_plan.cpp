@@ -226,20 +226,45 @@ std::variant<Lowered, TransferError> lower(const typed::Program &p) {
   return l;
 }
 
+ParamCache::~ParamCache() {
+  int current = -1;
+  sbc_get_device(&current);
+  for (auto &kv : device) {
+    sbc_set_device(kv.first);
+    sbc_free_device(kv.second);
+  }
+  if (current >= 0)
+    sbc_set_device(current);
+}
+
 std::optional<TransferError> uploadParams(const Lowered &l, CudaBackend &b, sbc_relocate &d) {
   if (l.paramBlob.empty())
     return std::nullopt;
-  auto *base = static_cast<uint8_t *>(b.params(l.paramBlob.size()));
-  if (!base)
-    return terr("backend_failure", b.error());
-  // Pageable source: the driver stages it before returning, and the copy is
-  // ordered on the compute stream after every earlier reader of the buffer.
-  const int rc = sbc_memcpy_h2d_async(base, l.paramBlob.data(), l.paramBlob.size(), b.computeStream());
-  if (rc) {
-    b.fail("parameter upload", rc);
-    return terr("backend_failure", b.error());
+  uint8_t *base = nullptr;
+  {
+    std::lock_guard<std::mutex> g(l.params->mutex);
+    auto it = l.params->device.find(b.device());
+    if (it != l.params->device.end()) {
+      base = static_cast<uint8_t *>(it->second);
+    } else {
+      void *p = nullptr;
+      int rc = sbc_malloc_device(&p, l.paramBlob.size());
+      if (rc) {
+        b.fail("cudaMalloc(parameters)", rc);
+        return terr("backend_failure", b.error());
+      }
+      // First use on this device: one blocking upload, then reused.
+      if ((rc = sbc_memcpy_h2d_async(p, l.paramBlob.data(), l.paramBlob.size(), b.computeStream())) ||
+          (rc = sbc_stream_synchronize(b.computeStream()))) {
+        sbc_free_device(p);
+        b.fail("parameter upload", rc);
+        return terr("backend_failure", b.error());
+      }
+      ++b.copyCalls;
+      l.params->device[b.device()] = p;
+      base = static_cast<uint8_t *>(p);
+    }
   }
-  ++b.copyCalls;
   for (int k = 0; k < d.nstages; ++k) {
     if (l.paramOffset[static_cast<size_t>(k)] != kNone)
       d.stages[k].param = reinterpret_cast<const float *>(base + l.paramOffset[static_cast<size_t>(k)]);

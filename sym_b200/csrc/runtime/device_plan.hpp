@@ -9,6 +9,9 @@
 
 #include "sb_cuda.h"
 
+#include <map>
+#include <memory>
+#include <mutex>
 #include <optional>
 #include <string>
 #include <variant>
@@ -20,9 +23,20 @@ namespace b200 {
 enum class Family { Generic = 0, Contiguous = 1, Transpose = 2 };
 const char *familyName(Family f);
 
+/// Device copies of a lowered program's parameter blob, one per device,
+/// uploaded on first use and freed with the program. A bound program's
+/// parameters are an immutable snapshot, so every execution on a device
+/// reuses the same copy (no per-call upload, no host sync).
+struct ParamCache {
+  std::mutex mutex;
+  std::map<int, void *> device;
+  ~ParamCache();
+};
+
 /// A program in device-ready form. `desc` carries the full padded box and
 /// everything but pointers; parameter arrays are packed into `paramBlob`.
 struct Lowered {
+  std::shared_ptr<ParamCache> params = std::make_shared<ParamCache>();
   sbc_relocate desc{};
   Family family = Family::Generic;
   int64_t padded[SBC_MAX_RANK] = {};

@@ -440,6 +440,15 @@ class DispatchResources:
     def stats(self):
         return json_call(_native.lib().sb_resources_stats, self.handle)
 
+    def streams(self, device: int):
+        """(copy stream, compute stream) handles of ``device``'s context."""
+        a, b = ctypes.c_void_p(), ctypes.c_void_p()
+        err = SbError()
+        if _native.lib().sb_resources_streams(self.handle, int(device), ctypes.byref(a), ctypes.byref(b),
+                                              ctypes.byref(err)):
+            _raise_transfer(err)
+        return a.value or 0, b.value or 0
+
     def clear(self):
         err = SbError()
         if _native.lib().sb_resources_clear(self.handle, ctypes.byref(err)):
