@@ -402,8 +402,54 @@ def cpu_baseline():
                       "scaled to layers by element count"}
 
 
+def run_kernel_case(args):
+    """Profiling case: the fused dequant->f16->transpose kernel alone on one
+    Llama-70B gate matrix [28672, 8192] already in HBM (235 MB int8 in,
+    470 MB f16 out: larger than L2), `--warmup` untimed launches then
+    `--steps` launches. Prints the per-launch time and HBM GB/s."""
+    import torch
+
+    from helpers import encode, recipe_c4
+    from sym_b200 import pyreloc
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    res = pyreloc.DispatchResources()
+    _, compute_s = res.streams(0)
+    stream = torch.cuda.ExternalStream(compute_s, device=dev)
+    out_f, in_f = 28672, 8192
+    rng = np.random.default_rng(0)
+    q = torch.from_numpy(rng.integers(-127, 128, size=(out_f, in_f), dtype=np.int8)).to(dev)
+    scale = np.exp(rng.normal(-5.0, 0.5, out_f)).astype(np.float32)
+    bound = pyreloc.bind_typed(pyreloc.load_typed_plan(encode(recipe_c4())),
+                               {"out_features": out_f, "in_features": in_f},
+                               {"scale": ("float32", [out_f], scale.tobytes())})
+    tmpl = pyreloc.prepare_dispatch_template(bound)
+    out = torch.empty((in_f, out_f), dtype=torch.float16, device=dev)
+
+    def launch():
+        pyreloc.execute_rows(tmpl, q.data_ptr(), out.data_ptr(), 0, in_f, device=0, host_source=False,
+                             resources=res, async_completion=True)
+
+    for _ in range(args.warmup):
+        launch()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(args.steps):
+        launch()
+    b.record(stream)
+    torch.cuda.synchronize()
+    dt = a.elapsed_time(b) * 1e-3 / args.steps
+    nbytes = out_f * in_f * 3 + out_f * 4
+    print(json.dumps({"case": "gate[28672,8192] s8->f16 transpose", "ms_per_launch": dt * 1e3,
+                      "hbm_gbs": nbytes / dt / 1e9, "bytes_per_launch": nbytes}))
+    return 0
+
+
 def main():
     parser = argparse.ArgumentParser()
+    parser.add_argument("--kernel-case", action="store_true",
+                        help="profiling case: the hot kernel alone on one device-resident matrix")
     parser.add_argument("--gpus", type=int, default=1)
     parser.add_argument("--steps", type=int, default=5)
     parser.add_argument("--warmup", type=int, default=3)
@@ -414,6 +460,8 @@ def main():
     args = parser.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.kernel_case:
+        return run_kernel_case(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)

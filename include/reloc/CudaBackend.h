@@ -40,8 +40,10 @@ public:
 
   /// Order both private streams after the work already on `external`.
   bool waitStream(const void *external);
-  /// Order `external` after everything enqueued so far on the private streams.
-  bool signalStream(const void *external);
+  /// Record completion of everything enqueued so far on the private streams;
+  /// with `hasExternal`, order `external` (a null handle = the legacy default
+  /// stream) after it.
+  bool signalStream(const void *external, bool hasExternal);
   /// Block until all enqueued work completed.
   QueueCompletion quiesce();
 

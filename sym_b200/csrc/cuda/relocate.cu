@@ -380,6 +380,195 @@ __global__ void __launch_bounds__(256) k_transpose(const __grid_constant__ sbc_r
 }
 
 // ---------------------------------------------------------------------------
+// Vectorized tiled transpose for unpadded, 16-byte aligned (batched) 2-D
+// transposes -- the hot kernel of the int8 weight fetch.
+//
+// A tile is 128 source bytes along A by 128 destination bytes along B
+// (s8 -> f16: 128 x 64 elements). Load: each thread moves one 16-byte
+// chunk of a source row into shared memory (8 threads per 128-byte row,
+// fully coalesced). Shared rows are 128 bytes with the 16-byte chunk index
+// XOR-swizzled by (row / VD) so that the transposed reads below hit eight
+// distinct chunks per quarter-warp. Store: each thread gathers VD = 16/WD
+// elements of one destination row from VD shared rows, runs the stage chain
+// with the per-channel parameter of its coordinate, and writes one 16-byte
+// chunk (8 threads per 128-byte destination row segment). Edge tiles take a
+// guarded element path. CH_ON: 0 = no per-channel stage, 1 = channel is the
+// A coordinate, 2 = channel is the B coordinate (divisor 1, no modulus).
+// ---------------------------------------------------------------------------
+
+template <int CHAIN>
+__device__ __forceinline__ bool chain_at(const sbc_relocate &d, uint32_t &v, int64_t ch) {
+  if constexpr (CHAIN == CH_COPY) {
+    return true;
+  } else if constexpr (CHAIN == CH_F16) {
+    v = narrow_f16(v);
+    return true;
+  } else if constexpr (CHAIN == CH_BF16) {
+    v = narrow_bf16(v);
+    return true;
+  } else if constexpr (CHAIN == CH_W16) {
+    v = widen_f16(v);
+    return true;
+  } else if constexpr (CHAIN == CH_WB16) {
+    v = widen_bf16(v);
+    return true;
+  } else if constexpr (CHAIN == CH_Q || CHAIN == CH_DQ || CHAIN == CH_DQ_F16 || CHAIN == CH_DQ_BF16) {
+    const sbc_stage &s = d.stages[0];
+    const int64_t c = s.channel == SBC_CH_NONE ? 0 : ch;
+    if (c >= s.channel_length)
+      return false;
+    if constexpr (CHAIN == CH_Q) {
+      v = quantize(v, s.param[c]);
+    } else {
+      v = dequantize(v, zp_of(s, c), s.param[c]);
+      if constexpr (CHAIN == CH_DQ_F16)
+        v = __half_as_ushort(__float2half_rn(__uint_as_float(v))); // finite: no NaN path
+      if constexpr (CHAIN == CH_DQ_BF16)
+        v = __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(v)));
+    }
+    return true;
+  } else {
+    for (int k = 0; k < d.nstages; ++k) {
+      const sbc_stage &s = d.stages[k];
+      const int64_t c = s.channel == SBC_CH_NONE ? 0 : ch;
+      if (c >= s.channel_length)
+        return false;
+      v = apply_one(s, v, c);
+    }
+    return true;
+  }
+}
+
+template <int W>
+__device__ __forceinline__ uint32_t load_elem(const uint8_t *p) {
+  if constexpr (W == 1)
+    return *p;
+  else if constexpr (W == 2)
+    return *reinterpret_cast<const uint16_t *>(p);
+  else
+    return *reinterpret_cast<const uint32_t *>(p);
+}
+
+template <int WS, int WD, int CHAIN, int CH_ON>
+__global__ void __launch_bounds__(256) k_tile(const __grid_constant__ sbc_relocate d, int64_t tiles_b,
+                                              int64_t tiles, int64_t nbatch) {
+  using D = typename Word<WD>::T;
+  constexpr int TA = 128 / WS, TB = 128 / WD, VD = 16 / WD, VS = 16 / WS;
+  __shared__ __align__(16) uint8_t sm[TB * 128];
+  const int t = threadIdx.x;
+  const int r = d.rank, ax_a = r - 2, ax_b = r - 1;
+  const int64_t Sb = d.src_strides[ax_b], Da = d.dst_strides[ax_a];
+  for (int64_t job = blockIdx.x; job < tiles * nbatch; job += gridDim.x) {
+    const int64_t n_idx = job / tiles, tile = job - n_idx * tiles;
+    const int64_t tb_i = tile % tiles_b, ta_i = tile / tiles_b;
+    int64_t nsrc = 0, ndst = 0;
+    if (r == 3) {
+      const int64_t cn = d.box_lo[0] + n_idx;
+      nsrc = cn * d.src_strides[0];
+      ndst = cn * d.dst_strides[0];
+    }
+    const int64_t a0 = d.box_lo[ax_a] + ta_i * TA, b0 = d.box_lo[ax_b] + tb_i * TB;
+    const int na = static_cast<int>(min(static_cast<int64_t>(TA), d.box_hi[ax_a] - a0));
+    const int nb = static_cast<int>(min(static_cast<int64_t>(TB), d.box_hi[ax_b] - b0));
+    const bool full = na == TA && nb == TB;
+    const uint8_t *srcb = static_cast<const uint8_t *>(d.src) + (nsrc + a0 + b0 * Sb - d.src_offset) * WS;
+    uint8_t *dstb = static_cast<uint8_t *>(d.dst) + (ndst + a0 * Da + b0 - d.dst_offset) * WD;
+    // ---- load: 16-byte chunks of TB source rows
+#pragma unroll
+    for (int p = 0; p < TB / 32; ++p) {
+      const int row = p * 32 + (t >> 3), c = t & 7;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (full) {
+        v = __ldcs(reinterpret_cast<const uint4 *>(srcb + row * Sb * WS + c * 16));
+      } else if (row < nb) {
+        uint8_t *vb = reinterpret_cast<uint8_t *>(&v);
+        for (int e = 0; e < VS; ++e)
+          if (c * VS + e < na)
+            for (int k = 0; k < WS; ++k)
+              vb[e * WS + k] = srcb[row * Sb * WS + (c * VS + e) * WS + k];
+      }
+      *reinterpret_cast<uint4 *>(sm + row * 128 + ((c ^ ((row / VD) & 7)) << 4)) = v;
+    }
+    __syncthreads();
+    // ---- store: one 16-byte destination chunk per thread per pass
+    const int c = t & 7;
+    // Quantize/dequantize parameters of this thread's VD columns, loaded once
+    // per tile when the channel is the B coordinate.
+    constexpr bool QDQ = CHAIN == CH_Q || CHAIN == CH_DQ || CHAIN == CH_DQ_F16 || CHAIN == CH_DQ_BF16;
+    float pscale[VD];
+    int32_t pzp[VD];
+    bool pok = true;
+    if constexpr (QDQ) {
+      const sbc_stage &s = d.stages[0];
+#pragma unroll
+      for (int j = 0; j < VD; ++j) {
+        int64_t ch = (CH_ON == 2 && c * VD + j < nb) ? b0 + c * VD + j : 0;
+        if (ch >= s.channel_length) {
+          pok = false;
+          ch = 0;
+        }
+        pscale[j] = s.param[ch];
+        pzp[j] = zp_of(s, ch);
+      }
+    }
+#pragma unroll
+    for (int p = 0; p < TA / 32; ++p) {
+      const int arow = p * 32 + (t >> 3);
+      if (arow < na) {
+        union {
+          uint4 q;
+          D e[VD];
+        } out;
+        const int xb = arow * WS; // byte column in the shared rows
+        bool ok = pok;
+        if constexpr (QDQ && CH_ON == 1) {
+          const sbc_stage &s = d.stages[0];
+          int64_t ch = a0 + arow;
+          if (ch >= s.channel_length) {
+            ok = false;
+            ch = 0;
+          }
+#pragma unroll
+          for (int j = 0; j < VD; ++j) {
+            pscale[j] = s.param[ch];
+            pzp[j] = zp_of(s, ch);
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < VD; ++j) {
+          const int brow = c * VD + j;
+          uint32_t v = load_elem<WS>(sm + brow * 128 + (((xb >> 4) ^ (c & 7)) << 4) + (xb & 15));
+          if constexpr (CHAIN == CH_Q) {
+            v = quantize(v, pscale[j]);
+          } else if constexpr (CHAIN == CH_DQ) {
+            v = dequantize(v, pzp[j], pscale[j]);
+          } else if constexpr (CHAIN == CH_DQ_F16) {
+            v = __half_as_ushort(__float2half_rn(__uint_as_float(dequantize(v, pzp[j], pscale[j]))));
+          } else if constexpr (CHAIN == CH_DQ_BF16) {
+            v = __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(dequantize(v, pzp[j], pscale[j]))));
+          } else {
+            const int64_t ch = CH_ON == 2 ? b0 + brow : (CH_ON == 1 ? a0 + arow : 0);
+            ok &= chain_at<CHAIN>(d, v, ch);
+          }
+          out.e[j] = static_cast<D>(v);
+        }
+        if (!ok)
+          flag(d);
+        uint8_t *dp = dstb + static_cast<int64_t>(arow) * Da * WD + c * 16;
+        if (full) {
+          __stcs(reinterpret_cast<uint4 *>(dp), out.q);
+        } else {
+          for (int j = 0; j < VD; ++j)
+            if (c * VD + j < nb)
+              reinterpret_cast<D *>(dp)[j] = out.e[j];
+        }
+      }
+    }
+    __syncthreads();
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Fill
 // ---------------------------------------------------------------------------
 
@@ -526,6 +715,68 @@ template <int WS, int WD, int CH> struct TransposeLaunch {
   }
 };
 
+template <int WS, int WD, int CH> struct TileLaunch {
+  static int run(const sbc_relocate &d, int ch_on, int64_t tiles_b, int64_t tiles, int64_t nbatch, cudaStream_t s) {
+    if constexpr (WS == 8 || WD == 8) {
+      return SBC_EUNSUPPORTED;
+    } else {
+      const int64_t jobs = tiles * nbatch;
+      const int64_t cap = static_cast<int64_t>(sm_count()) * 64;
+      const unsigned blocks = static_cast<unsigned>(jobs < cap ? jobs : cap);
+      constexpr bool PER_CHANNEL = !(CH == CH_COPY || CH == CH_F16 || CH == CH_BF16 || CH == CH_W16 || CH == CH_WB16);
+      if (ch_on == 0 || !PER_CHANNEL)
+        k_tile<WS, WD, CH, 0><<<blocks, 256, 0, s>>>(d, tiles_b, tiles, nbatch);
+      else if constexpr (PER_CHANNEL) {
+        if (ch_on == 1)
+          k_tile<WS, WD, CH, 1><<<blocks, 256, 0, s>>>(d, tiles_b, tiles, nbatch);
+        else
+          k_tile<WS, WD, CH, 2><<<blocks, 256, 0, s>>>(d, tiles_b, tiles, nbatch);
+      }
+      return launched(cudaSuccess);
+    }
+  }
+};
+
+/// The vectorized tile kernel applies when no axis is padded, every
+/// per-channel stage reads one of the two transposed coordinates directly,
+/// and both ends keep 16-byte alignment for every tile. Returns the channel
+/// axis code (0 none, 1 A, 2 B) or -1.
+int tile_eligible(const sbc_relocate &d) {
+  const int r = d.rank, ax_a = r - 2, ax_b = r - 1;
+  const int ws = d.src_width, wd = d.dst_width;
+  if (!((ws == 1 || ws == 2 || ws == 4) && (wd == 1 || wd == 2 || wd == 4)))
+    return -1;
+  for (int k = 0; k < r; ++k)
+    if (d.pad_lo[k] != 0 || d.box_hi[k] > d.extents[k])
+      return -1;
+  int ch_on = 0;
+  for (int k = 0; k < d.nstages; ++k) {
+    const sbc_stage &s = d.stages[k];
+    if (s.channel == SBC_CH_NONE)
+      continue;
+    if (s.channel != SBC_CH_AXIS || s.ch_div != 1 || s.ch_mod != 0 || (s.ch_axis != ax_a && s.ch_axis != ax_b))
+      return -1;
+    const int on = s.ch_axis == ax_a ? 1 : 2;
+    if (ch_on && ch_on != on)
+      return -1;
+    ch_on = on;
+  }
+  const int64_t Sb = d.src_strides[ax_b], Da = d.dst_strides[ax_a];
+  if ((Sb * ws) % 16 || (Da * wd) % 16)
+    return -1;
+  int64_t si = d.box_lo[ax_a] + d.box_lo[ax_b] * Sb - d.src_offset;
+  int64_t di = d.box_lo[ax_a] * Da + d.box_lo[ax_b] - d.dst_offset;
+  if (r == 3) {
+    if ((d.src_strides[0] * ws) % 16 || (d.dst_strides[0] * wd) % 16)
+      return -1;
+    si += d.box_lo[0] * d.src_strides[0];
+    di += d.box_lo[0] * d.dst_strides[0];
+  }
+  if ((reinterpret_cast<uintptr_t>(d.src) + si * ws) % 16 || (reinterpret_cast<uintptr_t>(d.dst) + di * wd) % 16)
+    return -1;
+  return ch_on;
+}
+
 bool basic_ok(const sbc_relocate &d) {
   if (d.rank < 1 || d.rank > SBC_MAX_RANK || d.nstages < 0 || d.nstages > SBC_MAX_STAGES || !d.dst)
     return false;
@@ -634,6 +885,15 @@ int sbc_relocate_transpose(const sbc_relocate *desc, void *stream) {
   const int64_t nbatch = d.rank == 3 ? d.box_hi[0] - d.box_lo[0] : 1;
   if (ext_a == 0 || ext_b == 0 || nbatch == 0)
     return 0;
+  const int ch_on = tile_eligible(d);
+  if (ch_on >= 0 && ext_a * d.src_width >= 128 && ext_b * d.dst_width >= 128) {
+    const int64_t ta = 128 / d.src_width, tbn = 128 / d.dst_width;
+    const int64_t tiles_b = (ext_b + tbn - 1) / tbn, tiles = ((ext_a + ta - 1) / ta) * tiles_b;
+    const int rc = dispatch<TileLaunch>(d.src_width, d.dst_width, chain, d, ch_on, tiles_b, tiles, nbatch,
+                                        static_cast<cudaStream_t>(stream));
+    if (rc != SBC_EUNSUPPORTED)
+      return rc;
+  }
   // Tile shape: a short destination row (B) takes the whole row so the tile
   // is one contiguous destination block; otherwise 64 x 64.
   int tb = 64, ta = 64;

@@ -80,13 +80,14 @@ bool CudaBackend::waitStream(const void *external) {
   return true;
 }
 
-bool CudaBackend::signalStream(const void *external) {
+bool CudaBackend::signalStream(const void *external, bool hasExternal) {
   int rc;
   if ((rc = sbc_event_record(fence_, copy_)) || (rc = sbc_stream_wait_event(compute_, fence_)) ||
       (rc = sbc_event_record(done_, compute_)))
     return fail("cudaEventRecord", rc);
   eventRecords += 2;
-  if (external && (rc = sbc_stream_wait_event(const_cast<void *>(external), done_)))
+  // A null handle is the legacy default stream, a real caller stream.
+  if (hasExternal && (rc = sbc_stream_wait_event(const_cast<void *>(external), done_)))
     return fail("cudaStreamWaitEvent(caller stream)", rc);
   return true;
 }

@@ -203,7 +203,7 @@ Route routeOf(const Implementation &row, const TransferOptions &o) {
 /// the route timing.
 std::optional<TransferError> finish(const b200::Lowered &l, CudaBackend &b, const TransferOptions &o, bool timed,
                                     Route route, int64_t bytes) {
-  if (!b.signalStream(o.hasCallerStream ? o.callerStream : nullptr))
+  if (!b.signalStream(o.callerStream, o.hasCallerStream))
     return terr("backend_failure", b.error());
   if (o.asyncCompletion && !l.needsStatus && !timed)
     return std::nullopt;

@@ -101,7 +101,8 @@ def _c4_inputs(out_f, in_f, seed=3):
     return q, scale
 
 
-@pytest.mark.parametrize("out_f,in_f", [(3, 5), (96, 200), (257, 131), (1024, 4096), (4096, 11008)])
+@pytest.mark.parametrize("out_f,in_f", [(3, 5), (96, 200), (257, 131), (100, 272), (72, 400), (1024, 4096),
+                                         (4096, 11008)])
 @pytest.mark.parametrize("route", ROUTES)
 def test_c4_dequant_f16_transpose(out_f, in_f, route):
     blob = encode(recipe_c4())
@@ -152,7 +153,8 @@ def expected_rows(blob, symbols, params, src, begin, end):
 
 @pytest.mark.parametrize("shards", [1, 2, 3, 8])
 @pytest.mark.parametrize("host_source", [True, False])
-def test_c4_row_windows(shards, host_source):
+@pytest.mark.parametrize("out_f,in_f", [(320, 1000), (192, 2048)])
+def test_c4_row_windows(shards, host_source, out_f, in_f):
     """Each shard produces result rows [k*in/N, (k+1)*in/N) -- the per-GPU
     window of the sharded weight fetch -- bit-identical to the reference's
     executeHostChunk of the same window."""
@@ -160,7 +162,6 @@ def test_c4_row_windows(shards, host_source):
     from helpers import resources
     from sym_b200 import pyreloc
 
-    out_f, in_f = 320, 1000
     blob = encode(recipe_c4())
     q, scale = _c4_inputs(out_f, in_f, seed=11)
     sym = {"out_features": out_f, "in_features": in_f}
