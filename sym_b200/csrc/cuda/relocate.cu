@@ -569,6 +569,170 @@ __global__ void __launch_bounds__(256) k_tile(const __grid_constant__ sbc_reloca
 }
 
 // ---------------------------------------------------------------------------
+// int8-source tile transpose (dequantize -> f16/bf16/f32): the hot kernel.
+//
+// Same tile and swizzle as k_tile, but each thread owns a 4 x VD block of
+// the output (4 destination rows A, VD = 16/WD destination columns B): it
+// reads VD 32-bit shared words, each holding the 4 A-consecutive int8 values
+// of one source row, so one shared load feeds 4 outputs. The block loops over
+// tiles with the next tile's 16-byte global loads issued before the current
+// tile's conversion and stores (register prefetch), keeping HBM reads in
+// flight while the SM converts. Per-channel parameters along B are loaded once
+// per tile.
+// ---------------------------------------------------------------------------
+
+template <int WD, int CHAIN, int CH_ON>
+__global__ void __launch_bounds__(256, 4) k_tile_s8(const __grid_constant__ sbc_relocate d, int64_t tiles_b,
+                                                 int64_t tiles, int64_t nbatch) {
+  constexpr int TA = 128, TB = 128 / WD, VD = 16 / WD, LP = TB / 32;
+  using D = typename Word<WD>::T;
+  __shared__ __align__(16) uint8_t sm[TB * 128];
+  const int t = threadIdx.x;
+  const int r = d.rank, ax_a = r - 2, ax_b = r - 1;
+  const int64_t Sb = d.src_strides[ax_b], Da = d.dst_strides[ax_a];
+  const int64_t total = tiles * nbatch;
+  const int ag = t >> 3, c = t & 7; // store-phase block: rows 4*ag.., columns c*VD..
+
+  struct Tile {
+    int64_t a0, b0, nsrc, ndst;
+    int na, nb;
+  };
+  auto tile_of = [&](int64_t job) {
+    Tile T;
+    const int64_t n_idx = job / tiles, tile = job - n_idx * tiles;
+    const int64_t tb_i = tile % tiles_b, ta_i = tile / tiles_b;
+    T.nsrc = T.ndst = 0;
+    if (r == 3) {
+      const int64_t cn = d.box_lo[0] + n_idx;
+      T.nsrc = cn * d.src_strides[0];
+      T.ndst = cn * d.dst_strides[0];
+    }
+    T.a0 = d.box_lo[ax_a] + ta_i * TA;
+    T.b0 = d.box_lo[ax_b] + tb_i * TB;
+    T.na = static_cast<int>(min(static_cast<int64_t>(TA), d.box_hi[ax_a] - T.a0));
+    T.nb = static_cast<int>(min(static_cast<int64_t>(TB), d.box_hi[ax_b] - T.b0));
+    return T;
+  };
+  auto load = [&](const Tile &T, uint4 (&v)[LP]) {
+    const uint8_t *srcb = static_cast<const uint8_t *>(d.src) + (T.nsrc + T.a0 + T.b0 * Sb - d.src_offset);
+    const bool full = T.na == TA && T.nb == TB;
+#pragma unroll
+    for (int p = 0; p < LP; ++p) {
+      const int row = p * 32 + (t >> 3);
+      v[p] = make_uint4(0, 0, 0, 0);
+      if (full) {
+        v[p] = __ldcs(reinterpret_cast<const uint4 *>(srcb + row * Sb + c * 16));
+      } else if (row < T.nb) {
+        uint8_t *vb = reinterpret_cast<uint8_t *>(&v[p]);
+        for (int e = 0; e < 16; ++e)
+          if (c * 16 + e < T.na)
+            vb[e] = srcb[row * Sb + c * 16 + e];
+      }
+    }
+  };
+
+  int64_t job = blockIdx.x;
+  uint4 pre[LP];
+  if (job < total)
+    load(tile_of(job), pre);
+  for (; job < total; job += gridDim.x) {
+    const Tile T = tile_of(job);
+#pragma unroll
+    for (int p = 0; p < LP; ++p) {
+      const int row = p * 32 + (t >> 3);
+      *reinterpret_cast<uint4 *>(sm + row * 128 + ((c ^ ((row / VD) & 7)) << 4)) = pre[p];
+    }
+    __syncthreads();
+    const int64_t next = job + gridDim.x;
+    if (next < total)
+      load(tile_of(next), pre); // in flight during the conversion below
+
+    // parameters of this thread's VD columns
+    float ps[VD];
+    int32_t pz[VD];
+    bool ok = true;
+    const sbc_stage &s = d.stages[0];
+#pragma unroll
+    for (int j = 0; j < VD; ++j) {
+      int64_t ch = 0;
+      if constexpr (CH_ON == 2)
+        ch = (c * VD + j < T.nb) ? T.b0 + c * VD + j : 0;
+      if (ch >= s.channel_length) {
+        ok = false;
+        ch = 0;
+      }
+      ps[j] = s.param[ch];
+      pz[j] = zp_of(s, ch);
+    }
+    uint32_t w[VD];
+#pragma unroll
+    for (int j = 0; j < VD; ++j) {
+      const int row = c * VD + j;
+      w[j] = *reinterpret_cast<const uint32_t *>(sm + row * 128 + ((((4 * ag) >> 4) ^ c) << 4) + ((4 * ag) & 15));
+    }
+    const bool full = T.na == TA && T.nb == TB;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int arow = 4 * ag + i;
+      if (arow >= T.na)
+        break;
+      if constexpr (CH_ON == 1) {
+        int64_t ch = T.a0 + arow;
+        if (ch >= s.channel_length) {
+          ok = false;
+          ch = 0;
+        }
+#pragma unroll
+        for (int j = 0; j < VD; ++j) {
+          ps[j] = s.param[ch];
+          pz[j] = zp_of(s, ch);
+        }
+      }
+      float f[VD];
+#pragma unroll
+      for (int j = 0; j < VD; ++j) {
+        const int32_t q = static_cast<int32_t>(static_cast<int8_t>((w[j] >> (8 * i)) & 0xffu));
+        f[j] = __fmul_rn(static_cast<float>(q - pz[j]), ps[j]);
+      }
+      union {
+        uint4 q;
+        D e[VD];
+        uint32_t u[4];
+      } out;
+      if constexpr (CHAIN == CH_DQ_F16) {
+#pragma unroll
+        for (int j = 0; j < VD; j += 2) {
+          const __half2 h = __floats2half2_rn(f[j], f[j + 1]);
+          out.u[j / 2] = *reinterpret_cast<const uint32_t *>(&h);
+        }
+      } else if constexpr (CHAIN == CH_DQ_BF16) {
+#pragma unroll
+        for (int j = 0; j < VD; j += 2) {
+          const __nv_bfloat162 h = __floats2bfloat162_rn(f[j], f[j + 1]);
+          out.u[j / 2] = *reinterpret_cast<const uint32_t *>(&h);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < VD; ++j)
+          out.e[j] = static_cast<D>(__float_as_uint(f[j]));
+      }
+      uint8_t *dp = static_cast<uint8_t *>(d.dst) +
+                    (T.ndst + (T.a0 + arow) * Da + T.b0 + c * VD - d.dst_offset) * WD;
+      if (full) {
+        __stcs(reinterpret_cast<uint4 *>(dp), out.q);
+      } else {
+        for (int j = 0; j < VD; ++j)
+          if (c * VD + j < T.nb)
+            reinterpret_cast<D *>(dp)[j] = out.e[j];
+      }
+    }
+    if (!ok)
+      flag(d);
+    __syncthreads();
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Fill
 // ---------------------------------------------------------------------------
 
@@ -886,6 +1050,33 @@ int sbc_relocate_transpose(const sbc_relocate *desc, void *stream) {
   if (ext_a == 0 || ext_b == 0 || nbatch == 0)
     return 0;
   const int ch_on = tile_eligible(d);
+  const bool dq = chain == CH_DQ || chain == CH_DQ_F16 || chain == CH_DQ_BF16;
+  if (ch_on >= 0 && dq && d.src_width == 1 && ext_a >= 128 && ext_b * d.dst_width >= 128) {
+    const int64_t tbn = 128 / d.dst_width;
+    const int64_t tiles_b = (ext_b + tbn - 1) / tbn, tiles = ((ext_a + 127) / 128) * tiles_b;
+    const int64_t jobs = tiles * nbatch, cap = static_cast<int64_t>(sm_count()) * 8;
+    const unsigned blocks = static_cast<unsigned>(jobs < cap ? jobs : cap);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+#define SBC_S8(WD_, CH_, ON_) k_tile_s8<WD_, CH_, ON_><<<blocks, 256, 0, s>>>(d, tiles_b, tiles, nbatch)
+#define SBC_S8_ON(WD_, CH_)                                                                                     \
+  do {                                                                                                         \
+    if (ch_on == 0)                                                                                            \
+      SBC_S8(WD_, CH_, 0);                                                                                     \
+    else if (ch_on == 1)                                                                                       \
+      SBC_S8(WD_, CH_, 1);                                                                                     \
+    else                                                                                                       \
+      SBC_S8(WD_, CH_, 2);                                                                                     \
+  } while (0)
+    if (chain == CH_DQ_F16 && d.dst_width == 2)
+      SBC_S8_ON(2, CH_DQ_F16);
+    else if (chain == CH_DQ_BF16 && d.dst_width == 2)
+      SBC_S8_ON(2, CH_DQ_BF16);
+    else if (chain == CH_DQ && d.dst_width == 4)
+      SBC_S8_ON(4, CH_DQ);
+#undef SBC_S8_ON
+#undef SBC_S8
+    return launched(cudaSuccess);
+  }
   if (ch_on >= 0 && ext_a * d.src_width >= 128 && ext_b * d.dst_width >= 128) {
     const int64_t ta = 128 / d.src_width, tbn = 128 / d.dst_width;
     const int64_t tiles_b = (ext_b + tbn - 1) / tbn, tiles = ((ext_a + ta - 1) / ta) * tiles_b;

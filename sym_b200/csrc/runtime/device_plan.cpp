@@ -464,6 +464,10 @@ std::optional<TransferError> runH2D(const Lowered &l, CudaBackend &b, const void
   const int64_t rowBytes = std::max<int64_t>(rowElems * ws, 1);
   const size_t target = o.chunkSizeOverride ? o.chunkSizeOverride : kDefaultChunkBytes;
   int64_t rowsPer = std::max<int64_t>(1, static_cast<int64_t>(target) / rowBytes);
+  // Chunk boundaries on a multiple of 64 rows keep every chunk's destination
+  // box 16-byte aligned and made of whole kernel tiles.
+  if (rowsPer >= 64)
+    rowsPer -= rowsPer % 64;
   const int slots = std::max(2, o.nBuffers);
   if (mode == Mode::Whole || route == Route::Staged)
     rowsPer = std::max<int64_t>(1, V1 - V0);
