@@ -581,57 +581,73 @@ __global__ void __launch_bounds__(256) k_tile(const __grid_constant__ sbc_reloca
 // per tile.
 // ---------------------------------------------------------------------------
 
+/// Division by a runtime divisor d for numerators below 2^31:
+/// n / d == (n * m) >> s with s = 31 + ceil(log2 d), m = ceil(2^s / d)
+/// (exact because n * (m * d - 2^s) < 2^31 * d <= 2^s).
+struct FastDiv {
+  unsigned long long m;
+  uint32_t s, d;
+};
+
+__device__ __forceinline__ uint32_t fdiv(uint32_t n, const FastDiv &f) {
+  return static_cast<uint32_t>((static_cast<unsigned long long>(n) * f.m) >> f.s);
+}
+
 template <int WD, int CHAIN, int CH_ON>
-__global__ void __launch_bounds__(256, 4) k_tile_s8(const __grid_constant__ sbc_relocate d, int64_t tiles_b,
-                                                 int64_t tiles, int64_t nbatch) {
+__global__ void __launch_bounds__(256, 4) k_tile_s8(const __grid_constant__ sbc_relocate d, FastDiv div_b,
+                                                    FastDiv div_t, uint32_t total) {
   constexpr int TA = 128, TB = 128 / WD, VD = 16 / WD, LP = TB / 32;
   using D = typename Word<WD>::T;
   __shared__ __align__(16) uint8_t sm[TB * 128];
-  const int t = threadIdx.x;
+  const int t = threadIdx.x, ag = t >> 3, c = t & 7; // store block: rows 4*ag.., columns c*VD..
   const int r = d.rank, ax_a = r - 2, ax_b = r - 1;
-  const int64_t Sb = d.src_strides[ax_b], Da = d.dst_strides[ax_a];
-  const int64_t total = tiles * nbatch;
-  const int ag = t >> 3, c = t & 7; // store-phase block: rows 4*ag.., columns c*VD..
+  const int64_t Sb = d.src_strides[ax_b], Da = d.dst_strides[ax_a], DaB = Da * WD;
+  const uint8_t *const src0 = static_cast<const uint8_t *>(d.src) - d.src_offset;
+  uint8_t *const dst0 = static_cast<uint8_t *>(d.dst) - d.dst_offset * WD;
+  const sbc_stage &s = d.stages[0];
 
   struct Tile {
-    int64_t a0, b0, nsrc, ndst;
+    const uint8_t *src;
+    uint8_t *dst;
+    int64_t a0, b0;
     int na, nb;
   };
-  auto tile_of = [&](int64_t job) {
+  auto tile_of = [&](uint32_t job) {
     Tile T;
-    const int64_t n_idx = job / tiles, tile = job - n_idx * tiles;
-    const int64_t tb_i = tile % tiles_b, ta_i = tile / tiles_b;
-    T.nsrc = T.ndst = 0;
+    const uint32_t n_idx = fdiv(job, div_t), tile = job - n_idx * div_t.d;
+    const uint32_t ta_i = fdiv(tile, div_b), tb_i = tile - ta_i * div_b.d;
+    int64_t ns = 0, nd = 0;
     if (r == 3) {
       const int64_t cn = d.box_lo[0] + n_idx;
-      T.nsrc = cn * d.src_strides[0];
-      T.ndst = cn * d.dst_strides[0];
+      ns = cn * d.src_strides[0];
+      nd = cn * d.dst_strides[0];
     }
-    T.a0 = d.box_lo[ax_a] + ta_i * TA;
-    T.b0 = d.box_lo[ax_b] + tb_i * TB;
+    T.a0 = d.box_lo[ax_a] + static_cast<int64_t>(ta_i) * TA;
+    T.b0 = d.box_lo[ax_b] + static_cast<int64_t>(tb_i) * TB;
     T.na = static_cast<int>(min(static_cast<int64_t>(TA), d.box_hi[ax_a] - T.a0));
     T.nb = static_cast<int>(min(static_cast<int64_t>(TB), d.box_hi[ax_b] - T.b0));
+    T.src = src0 + ns + T.a0 + T.b0 * Sb;
+    T.dst = dst0 + (nd + T.a0 * Da + T.b0) * WD;
     return T;
   };
   auto load = [&](const Tile &T, uint4 (&v)[LP]) {
-    const uint8_t *srcb = static_cast<const uint8_t *>(d.src) + (T.nsrc + T.a0 + T.b0 * Sb - d.src_offset);
     const bool full = T.na == TA && T.nb == TB;
 #pragma unroll
     for (int p = 0; p < LP; ++p) {
       const int row = p * 32 + (t >> 3);
       v[p] = make_uint4(0, 0, 0, 0);
       if (full) {
-        v[p] = __ldcs(reinterpret_cast<const uint4 *>(srcb + row * Sb + c * 16));
+        v[p] = __ldcs(reinterpret_cast<const uint4 *>(T.src + row * Sb + c * 16));
       } else if (row < T.nb) {
         uint8_t *vb = reinterpret_cast<uint8_t *>(&v[p]);
         for (int e = 0; e < 16; ++e)
           if (c * 16 + e < T.na)
-            vb[e] = srcb[row * Sb + c * 16 + e];
+            vb[e] = T.src[row * Sb + c * 16 + e];
       }
     }
   };
 
-  int64_t job = blockIdx.x;
+  uint32_t job = blockIdx.x;
   uint4 pre[LP];
   if (job < total)
     load(tile_of(job), pre);
@@ -643,15 +659,15 @@ __global__ void __launch_bounds__(256, 4) k_tile_s8(const __grid_constant__ sbc_
       *reinterpret_cast<uint4 *>(sm + row * 128 + ((c ^ ((row / VD) & 7)) << 4)) = pre[p];
     }
     __syncthreads();
-    const int64_t next = job + gridDim.x;
-    if (next < total)
-      load(tile_of(next), pre); // in flight during the conversion below
+    if (job + gridDim.x < total)
+      load(tile_of(job + gridDim.x), pre); // in flight during the conversion below
 
-    // parameters of this thread's VD columns
-    float ps[VD];
-    int32_t pz[VD];
+    // Parameters of this thread's VD columns. The int8 -> f32 conversion is
+    // exact and uses the FP32 pipe: the biased byte (q + 128) is placed in
+    // the mantissa of 2^23, and one subtraction of 2^23 + 128 + zp leaves the
+    // integer q - zp exactly; one multiply by the scale follows (C1 affine).
+    float ps[VD], bias[VD];
     bool ok = true;
-    const sbc_stage &s = d.stages[0];
 #pragma unroll
     for (int j = 0; j < VD; ++j) {
       int64_t ch = 0;
@@ -662,17 +678,19 @@ __global__ void __launch_bounds__(256, 4) k_tile_s8(const __grid_constant__ sbc_
         ch = 0;
       }
       ps[j] = s.param[ch];
-      pz[j] = zp_of(s, ch);
+      bias[j] = 8388736.0f + static_cast<float>(zp_of(s, ch));
     }
     uint32_t w[VD];
 #pragma unroll
     for (int j = 0; j < VD; ++j) {
       const int row = c * VD + j;
-      w[j] = *reinterpret_cast<const uint32_t *>(sm + row * 128 + ((((4 * ag) >> 4) ^ c) << 4) + ((4 * ag) & 15));
+      w[j] = *reinterpret_cast<const uint32_t *>(sm + row * 128 + ((((4 * ag) >> 4) ^ c) << 4) + ((4 * ag) & 15)) ^
+             0x80808080u;
     }
     const bool full = T.na == TA && T.nb == TB;
+    uint8_t *dp = T.dst + static_cast<int64_t>(4 * ag) * DaB + c * 16;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < 4; ++i, dp += DaB) {
       const int arow = 4 * ag + i;
       if (arow >= T.na)
         break;
@@ -682,18 +700,17 @@ __global__ void __launch_bounds__(256, 4) k_tile_s8(const __grid_constant__ sbc_
           ok = false;
           ch = 0;
         }
+        const float sc = s.param[ch], bi = 8388736.0f + static_cast<float>(zp_of(s, ch));
 #pragma unroll
         for (int j = 0; j < VD; ++j) {
-          ps[j] = s.param[ch];
-          pz[j] = zp_of(s, ch);
+          ps[j] = sc;
+          bias[j] = bi;
         }
       }
       float f[VD];
 #pragma unroll
-      for (int j = 0; j < VD; ++j) {
-        const int32_t q = static_cast<int32_t>(static_cast<int8_t>((w[j] >> (8 * i)) & 0xffu));
-        f[j] = __fmul_rn(static_cast<float>(q - pz[j]), ps[j]);
-      }
+      for (int j = 0; j < VD; ++j)
+        f[j] = __fmul_rn(__fsub_rn(__int_as_float(__byte_perm(w[j], 0x4B000000u, 0x7650 + i)), bias[j]), ps[j]);
       union {
         uint4 q;
         D e[VD];
@@ -716,8 +733,6 @@ __global__ void __launch_bounds__(256, 4) k_tile_s8(const __grid_constant__ sbc_
         for (int j = 0; j < VD; ++j)
           out.e[j] = static_cast<D>(__float_as_uint(f[j]));
       }
-      uint8_t *dp = static_cast<uint8_t *>(d.dst) +
-                    (T.ndst + (T.a0 + arow) * Da + T.b0 + c * VD - d.dst_offset) * WD;
       if (full) {
         __stcs(reinterpret_cast<uint4 *>(dp), out.q);
       } else {
@@ -1051,13 +1066,26 @@ int sbc_relocate_transpose(const sbc_relocate *desc, void *stream) {
     return 0;
   const int ch_on = tile_eligible(d);
   const bool dq = chain == CH_DQ || chain == CH_DQ_F16 || chain == CH_DQ_BF16;
-  if (ch_on >= 0 && dq && d.src_width == 1 && ext_a >= 128 && ext_b * d.dst_width >= 128) {
+  if (ch_on >= 0 && dq && d.src_width == 1 && ext_a >= 128 && ext_b * d.dst_width >= 128 &&
+      ((ext_a + 127) / 128) * ((ext_b * d.dst_width + 127) / 128) * nbatch < (int64_t(1) << 31)) {
     const int64_t tbn = 128 / d.dst_width;
     const int64_t tiles_b = (ext_b + tbn - 1) / tbn, tiles = ((ext_a + 127) / 128) * tiles_b;
     const int64_t jobs = tiles * nbatch, cap = static_cast<int64_t>(sm_count()) * 8;
     const unsigned blocks = static_cast<unsigned>(jobs < cap ? jobs : cap);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-#define SBC_S8(WD_, CH_, ON_) k_tile_s8<WD_, CH_, ON_><<<blocks, 256, 0, s>>>(d, tiles_b, tiles, nbatch)
+    auto fast = [](uint32_t dv) {
+      FastDiv f;
+      uint32_t l = 0;
+      while ((1ull << l) < dv)
+        ++l;
+      f.s = 31 + l;
+      f.d = dv;
+      f.m = ((1ull << f.s) + dv - 1) / dv;
+      return f;
+    };
+    const FastDiv div_b = fast(static_cast<uint32_t>(tiles_b)), div_t = fast(static_cast<uint32_t>(tiles));
+#define SBC_S8(WD_, CH_, ON_)                                                                                  \
+  k_tile_s8<WD_, CH_, ON_><<<blocks, 256, 0, s>>>(d, div_b, div_t, static_cast<uint32_t>(jobs))
 #define SBC_S8_ON(WD_, CH_)                                                                                     \
   do {                                                                                                         \
     if (ch_on == 0)                                                                                            \
