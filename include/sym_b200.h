@@ -126,6 +126,26 @@ int sb_execute_rows(const sb_template *tmpl, sb_resources *resources, int32_t de
                     int32_t host_source, void *dst, int64_t row_begin, int64_t row_end, const sb_options *options,
                     char *report, size_t cap, sb_error *err);
 
+/* No reference counterpart: a host->device execution of a prepared template
+ * that allocates nothing, for callers that cannot call cudaMalloc (code under
+ * a caching allocator that owns the device heap, hosts with a fixed device
+ * memory budget, code that must not allocate between graph captures). Instead
+ * of a context's HBM ring and parameter buffers it uses one statically
+ * allocated 32 MiB __device__ array (1 MiB of parameters, the rest one staging
+ * slot for source rows) that every GPU loading libsb_cuda.so holds until exit.
+ * `source` is host memory (pinned for full speed), `destination` device memory
+ * of the template's destination size; all work is ordered on `stream` (NULL =
+ * the legacy default stream) with no copy/compute overlap. Plans whose
+ * parameters exceed 1 MiB, or whose single source row (or whole source, when
+ * rows cannot be split) exceeds the staging slot, are rejected with
+ * invalid_options. The first call on a device resolves the array's device
+ * address (cudaGetSymbolAddress) with that device current: make that first
+ * call outside any stream capture. All calls share the array, so calls that
+ * overlap on the GPU (other streams, other threads) race; plans whose channel
+ * map is checked on the device synchronize `stream` before returning. */
+int sb_execute_h2d_static(const sb_template *tmpl, const void *source, void *destination, void *stream,
+                          sb_error *err);
+
 /* pyreloc.DispatchResources (PyDispatch.cpp:700-801) / dispatch::Resources. */
 int sb_resources_create(uint64_t max_retained_bytes, uint64_t max_live_bytes, uint32_t max_contexts,
                         sb_resources **out, sb_error *err);

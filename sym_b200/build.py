@@ -23,7 +23,8 @@ ROOT = PKG.parent
 LIB_DIR = PKG / "_lib"
 CUDA_SOURCES = sorted((PKG / "csrc" / "cuda").glob("*.cu"))
 RUNTIME_SOURCES = sorted((PKG / "csrc" / "runtime").glob("*.cpp"))
-HEADERS = sorted((ROOT / "include").rglob("*.h")) + sorted((PKG / "csrc").rglob("*.hpp"))
+HEADERS = (sorted((ROOT / "include").rglob("*.h")) + sorted((PKG / "csrc").rglob("*.hpp"))
+           + sorted((PKG / "csrc").rglob("*.h")))
 CUDA_LIB = LIB_DIR / "libsb_cuda.so"
 RUNTIME_LIB = LIB_DIR / "libsb_runtime.so"
 
@@ -69,6 +70,7 @@ def build(force: bool = False, verbose: bool = False) -> None:
     if force or _stale(RUNTIME_LIB, RUNTIME_SOURCES + HEADERS + [CUDA_LIB]):
         cmd = [_cxx(), "-O2", "-std=c++17", "-fPIC", "-shared", "-ffp-contract=off", "-fno-fast-math",
                "-Wall", "-Wextra", "-Wno-unused-parameter", *inc, "-I", PKG / "csrc" / "runtime",
+               "-I", PKG / "csrc" / "cuda",
                *RUNTIME_SOURCES, "-L", LIB_DIR, "-lsb_cuda", "-Wl,-rpath,$ORIGIN", "-pthread",
                "-o", RUNTIME_LIB]
         _run(cmd, verbose)

@@ -10,6 +10,7 @@
 
 #include "device_plan.hpp"
 #include "sb_cuda.h"
+#include "static_scratch.h"
 
 #include <cstdio>
 #include <cstring>
@@ -544,6 +545,23 @@ int sb_execute_rows(const sb_template *t, sb_resources *res, int32_t device, con
   putJson(reportJson(rep), report, cap);
   if (out.error)
     return setErr(err, out.error->code, out.error->message);
+  return 0;
+}
+
+int sb_execute_h2d_static(const sb_template *t, const void *source, void *destination, void *stream,
+                          sb_error *err) {
+  if (!t->t.lowered)
+    return setErr(err, "implementation_unavailable", "template has no lowered program");
+  if (!source || !destination)
+    return setErr(err, "invalid_view", "source and destination must be non-null");
+  void *scratch = nullptr;
+  size_t bytes = 0;
+  const int rc = sbc_static_scratch(&scratch, &bytes);
+  if (rc)
+    return setErr(err, "backend_failure", std::string("static scratch: ") + sbc_error_string(rc));
+  auto e = b200::runH2DStatic(*t->t.lowered, source, destination, stream, static_cast<uint8_t *>(scratch), bytes);
+  if (e)
+    return setErr(err, e->code, e->message);
   return 0;
 }
 

@@ -535,5 +535,99 @@ std::optional<TransferError> runH2D(const Lowered &l, CudaBackend &b, const void
   return std::nullopt;
 }
 
+std::optional<TransferError> runH2DStatic(const Lowered &l, const void *hsrc, void *ddst, void *stream,
+                                          uint8_t *scratch, size_t scratchBytes) {
+  // Scratch layout: [0, 256) status word | [256, 256 + kParams) parameters |
+  // the rest one staging slot for source rows.
+  constexpr size_t kStatus = 256, kParams = size_t(1) << 20;
+  if (l.paramBlob.size() > kParams)
+    return terr("invalid_options", "parameters exceed the static scratch's 1 MiB parameter area (" +
+                                       std::to_string(l.paramBlob.size()) + " bytes)");
+  uint8_t *slot = scratch + kStatus + kParams;
+  const size_t slotBytes = scratchBytes - kStatus - kParams;
+  sbc_relocate base = l.desc;
+  int rc = 0;
+  if (!l.paramBlob.empty()) {
+    uint8_t *pdev = scratch + kStatus;
+    if ((rc = sbc_memcpy_h2d_async(pdev, l.paramBlob.data(), l.paramBlob.size(), stream)))
+      return terr("backend_failure", std::string("parameter copy: ") + sbc_error_string(rc));
+    for (int k = 0; k < base.nstages; ++k) {
+      if (l.paramOffset[static_cast<size_t>(k)] != kNone)
+        base.stages[k].param = reinterpret_cast<const float *>(pdev + l.paramOffset[static_cast<size_t>(k)]);
+      if (l.zpOffset[static_cast<size_t>(k)] != kNone)
+        base.stages[k].zero_point = reinterpret_cast<const int32_t *>(pdev + l.zpOffset[static_cast<size_t>(k)]);
+    }
+  }
+  // The scratch keeps the previous call's contents: the status word must start at 0.
+  if (l.needsStatus) {
+    base.status = reinterpret_cast<int32_t *>(scratch);
+    if ((rc = sbc_fill(scratch, 1, 4, 0, stream)))
+      return terr("backend_failure", std::string("status reset: ") + sbc_error_string(rc));
+  }
+  if (l.desc.has_fill && !l.denseCover &&
+      (rc = sbc_fill(ddst, l.dstElements, l.desc.dst_width, l.desc.fill_bits, stream)))
+    return terr("backend_failure", std::string("fill kernel: ") + sbc_error_string(rc));
+  base.dst = ddst;
+  const int ws = l.desc.src_width;
+  auto launchOn = [&](const sbc_relocate &d) -> int {
+    int r2 = SBC_EUNSUPPORTED;
+    if (l.family == Family::Contiguous)
+      r2 = sbc_relocate_contiguous(&d, stream);
+    else if (l.family == Family::Transpose)
+      r2 = sbc_relocate_transpose(&d, stream);
+    if (r2 == SBC_EUNSUPPORTED)
+      r2 = sbc_relocate_generic(&d, stream);
+    return r2;
+  };
+  if (!l.rowsChunkable || l.srcOuter < 0) {
+    const size_t bytes = static_cast<size_t>(l.srcElements) * ws;
+    if (bytes > slotBytes)
+      return terr("invalid_options", "source of " + std::to_string(bytes) +
+                                         " bytes is not row-chunkable and exceeds the static scratch's " +
+                                         std::to_string(slotBytes) + "-byte staging slot");
+    if ((rc = sbc_memcpy_h2d_async(slot, hsrc, bytes, stream)))
+      return terr("backend_failure", std::string("source copy: ") + sbc_error_string(rc));
+    sbc_relocate d = base;
+    d.src = slot;
+    if ((rc = launchOn(d)))
+      return terr("backend_failure", std::string("relocation kernel: ") + sbc_error_string(rc));
+  } else {
+    const int ax = l.srcOuter;
+    const int64_t lo = l.desc.pad_lo[ax], E = l.desc.extents[ax];
+    const int64_t B1 = l.padded[ax];
+    const int64_t rowBytes = l.desc.src_strides[ax] * ws;
+    int64_t rowsPer = static_cast<int64_t>(slotBytes) / rowBytes;
+    if (rowsPer < 1)
+      return terr("invalid_options", "one source row of " + std::to_string(rowBytes) +
+                                         " bytes exceeds the static scratch's " + std::to_string(slotBytes) +
+                                         "-byte staging slot");
+    if (rowsPer >= 64)
+      rowsPer -= rowsPer % 64;
+    for (int64_t r0 = lo; r0 < lo + E; r0 += rowsPer) {
+      const int64_t r1 = std::min(r0 + rowsPer, lo + E);
+      const int64_t v0 = r0 - lo, v1 = r1 - lo;
+      // Same stream: this copy starts only after the previous chunk's kernel.
+      if ((rc = sbc_memcpy_h2d_async(slot, static_cast<const uint8_t *>(hsrc) + v0 * rowBytes,
+                                     static_cast<size_t>((v1 - v0) * rowBytes), stream)))
+        return terr("backend_failure", std::string("source copy: ") + sbc_error_string(rc));
+      sbc_relocate d = base;
+      d.box_lo[ax] = r0 == lo ? 0 : r0;
+      d.box_hi[ax] = r1 == lo + E ? B1 : r1;
+      d.src = slot;
+      d.src_offset = v0 * l.desc.src_strides[ax];
+      if ((rc = launchOn(d)))
+        return terr("backend_failure", std::string("relocation kernel: ") + sbc_error_string(rc));
+    }
+  }
+  if (l.needsStatus) {
+    int32_t status = 0;
+    if ((rc = sbc_memcpy_d2h_async(&status, scratch, 4, stream)) || (rc = sbc_stream_synchronize(stream)))
+      return terr("backend_failure", std::string("status readback: ") + sbc_error_string(rc));
+    if (status)
+      return terr("channel_out_of_range", "a channel index fell outside its parameter table");
+  }
+  return std::nullopt;
+}
+
 } // namespace b200
 } // namespace reloc

@@ -75,6 +75,13 @@ std::optional<TransferError> runDevice(const Lowered &l, CudaBackend &b, const v
 std::optional<TransferError> runH2D(const Lowered &l, CudaBackend &b, const void *hsrc, void *ddst, Route route,
                                     RowWindow window, const TransferOptions &options, RunStats &stats);
 
+/// Host source -> device destination on the caller's `stream` through the
+/// statically allocated scratch `scratch` (`scratchBytes`), allocating
+/// nothing: parameters and one staging slot live in the scratch, chunks of
+/// source rows are copied and transformed in stream order.
+std::optional<TransferError> runH2DStatic(const Lowered &l, const void *hsrc, void *ddst, void *stream,
+                                          uint8_t *scratch, size_t scratchBytes);
+
 /// Resolve Route::Auto for this plan class on this backend (measurement-
 /// driven; see dispatch.cpp).
 Route chooseRoute(const Lowered &l, CudaBackend &b, const void *hsrc, const TransferOptions &options);

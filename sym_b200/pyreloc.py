@@ -424,6 +424,19 @@ def execute_rows(prepared: DispatchTemplate, source_ptr: int, destination_ptr: i
     return MappingProxyType(report)
 
 
+def execute_h2d_static(prepared: DispatchTemplate, source_ptr: int, destination_ptr: int, stream=None):
+    """Host -> device execution that allocates nothing, for callers that cannot
+    allocate device memory: staging and parameters live in a statically
+    allocated 32 MiB device array (see include/sym_b200.h). Work is ordered on
+    ``stream`` (a cudaStream_t handle; None/0 = the legacy default stream).
+    Calls that overlap on the GPU share that array and race."""
+    err = SbError()
+    if _native.lib().sb_execute_h2d_static(prepared.ptr, ctypes.c_void_p(int(source_ptr)),
+                                           ctypes.c_void_p(int(destination_ptr)),
+                                           ctypes.c_void_p(int(stream or 0)), ctypes.byref(err)):
+        _raise_transfer(err)
+
+
 class DispatchResources:
     """Typed contexts: per-device streams, HBM ring and parameter buffers,
     retained across calls (reference ``pyreloc.DispatchResources``)."""
