@@ -238,26 +238,14 @@ def run_ours(args):
         distinct.append(mats)
     outs = [[torch.empty((m["in"], m["out"]), dtype=torch.float16, device=dev) for m in distinct[0]]
             for _ in range(2)]
-    rows = []
-    for m in distinct[0]:
-        b, e = m["in"] * rank // world, m["in"] * (rank + 1) // world
-        rows.append((b, e))
+    from sym_b200.workloads import ShardedLayerFetch, shard_bounds
+
+    rows = [shard_bounds(m["in"], world, rank) for m in distinct[0]]
     sample = torch.empty(32, dtype=torch.float16).pin_memory()
+    fetcher = ShardedLayerFetch(res, local, world, rank, chunk_bytes=args.chunk_bytes, ring_slots=args.ring_slots)
 
     def layer(l, host_source):
-        mats = distinct[l % len(distinct)]
-        out_set = outs[l % 2]
-        handles = []
-        cur = torch.cuda.current_stream(dev).cuda_stream
-        for m, out, (b, e) in zip(mats, out_set, rows):
-            shard = out[b:e]
-            pyreloc.execute_rows(m["tmpl"], (m["host"] if host_source else m["dev"]).data_ptr(), shard.data_ptr(),
-                                 b, e, device=local, host_source=host_source, resources=res, caller_stream=cur,
-                                 async_completion=True, route="dma_ring", chunk_size=args.chunk_bytes,
-                                 n_buffers=args.ring_slots)
-            if world > 1:
-                handles.append(dist.all_gather_into_tensor(out.view(-1), shard.reshape(-1), async_op=True))
-        return handles
+        return fetcher.fetch(distinct[l % len(distinct)], outs[l % 2], host_source)
 
     def step(host_source):
         handles = []

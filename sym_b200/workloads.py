@@ -1,0 +1,211 @@
+"""Weight-streaming workloads: ``WeightFetcher`` and the sharded multi-GPU fetch.
+
+``WeightFetcher`` keeps the interface of the reference workload
+(libreloc/python/examples/workloads/common.py:384-598): one symbolic typed
+recipe compiled once and bound for every matrix shape, ``fetch``,
+``fetch_many``, per-device retained resources, ``reference`` and ``close``.
+Its default recipe is the reference's own (int8 ``[in, out]``, per-output-
+channel f32 scale on axis 1 -> dequantize -> transpose -> f32 ``[out, in]``);
+``layout="out_in_f16"`` selects the BASELINE weight-streaming recipe (int8
+``[out, in]``, per-row scale -> dequantize -> f16 RNE -> transpose -> f16
+``[in, out]``).
+
+``ShardedLayerFetch`` is the multi-GPU path of BASELINE config 5: rank ``k`` of
+``N`` produces result rows ``[k*in/N, (k+1)*in/N)`` of every matrix (the
+matrix's source columns, pulled over this GPU's own PCIe link by 2-D DMA),
+then an in-place NCCL all-gather over NVLink assembles the full matrix on
+every GPU. Matrix i's all-gather overlaps matrix i+1's fetch.
+"""
+from __future__ import annotations
+
+from contextlib import ExitStack
+
+from . import pyreloc
+from .reloc_torch import dispatch
+from .reloc_torch.compiler import CompilerClient
+from .reloc_torch.recipe import BindingParam, Cast, Dequantize, Recipe, TensorSpec, Transpose
+from .reloc_torch.resources import TransferResources
+from .reloc_torch.symbolic import Const, Symbol, dense_strides
+
+
+class Report:
+    """Counters of a fetch run (the fields the reference workloads record)."""
+
+    def __init__(self):
+        self.data = {"plan_compiles": 0, "bytes": {}, "dispatches": {}}
+
+    def add_bytes(self, kind, source, wire, destination, payload=None):
+        e = self.data["bytes"].setdefault(kind, {"transfers": 0, "source": 0, "wire": 0, "destination": 0})
+        e["transfers"] += 1
+        e["source"] += int(source)
+        e["wire"] += int(wire)
+        e["destination"] += int(destination)
+        if payload is not None:
+            e["payload"] = e.get("payload", 0) + int(payload)
+
+    def add_dispatch(self, row, count=1):
+        self.data["dispatches"][row] = self.data["dispatches"].get(row, 0) + int(count)
+
+    def add_plan_compiles(self, count):
+        self.data["plan_compiles"] += int(count)
+
+
+def weight_recipe(layout="reference"):
+    rows, cols = Symbol("s0"), Symbol("s1")
+
+    def spec(shape, dtype):
+        return TensorSpec(shape, dense_strides(shape), Const(0), dtype)
+
+    if layout == "reference":
+        return Recipe(spec((rows, cols), "int8"),
+                      (Dequantize("float32", BindingParam("scale", "float32", (cols,)), None, 1, "affine"),
+                       Transpose((1, 0))),
+                      spec((cols, rows), "float32"), "h2d")
+    if layout == "out_in_f16":
+        return Recipe(spec((rows, cols), "int8"),
+                      (Dequantize("float32", BindingParam("scale", "float32", (rows,)), None, 0, "affine"),
+                       Cast("float16", "ieee_rne"), Transpose((1, 0))),
+                      spec((cols, rows), "float16"), "h2d")
+    raise ValueError("layout must be 'reference' or 'out_in_f16'")
+
+
+class WeightFetcher:
+    """int8 weights + f32 scales on the CPU -> dequantized weights on a GPU."""
+
+    def __init__(self, report=None, calibration=None, kind="weights", implementation="", *,
+                 resource_policy="retained", retained_bytes=64 << 20, live_bytes=0, layout="reference"):
+        if resource_policy not in ("retained", "per-call"):
+            raise ValueError("resource_policy must be retained or per-call")
+        self.resource_policy = resource_policy
+        self.retained_bytes, self.live_bytes = retained_bytes, live_bytes
+        self.layout = layout
+        self.compiled = CompilerClient.from_environment().compile(weight_recipe(layout))
+        self.compiles = 1
+        self.shapes = set()
+        self.report = report if report is not None else Report()
+        self.calibration = calibration
+        self.kind = kind
+        self.implementation = implementation
+        self._resources = {}
+        self._cleanup = ExitStack()
+        self._closed = False
+        self.report.add_plan_compiles(1)
+
+    def _device(self, device):
+        import torch
+
+        device = torch.device(device)
+        if device.type != "cuda":
+            raise ValueError("weight fetcher requires a CUDA destination")
+        return torch.device("cuda", device.index if device.index is not None else torch.cuda.current_device())
+
+    def _owner(self, device):
+        if self.resource_policy == "per-call":
+            return None
+        key = str(device)
+        if key not in self._resources:
+            self._resources[key] = self._cleanup.enter_context(
+                TransferResources(max_typed_retained_bytes=self.retained_bytes, max_typed_live_bytes=self.live_bytes))
+        return self._resources[key]
+
+    def resource_stats(self):
+        return {name: owner.stats()["typed"] for name, owner in self._resources.items()}
+
+    def _prepare(self, q, scale, device):
+        return dispatch.prepare_typed_transfer(self.compiled, q, device, parameters={"scale": scale}, policy="auto",
+                                               calibration=self.calibration, implementation=self.implementation)
+
+    def fetch(self, q, scale, device, *, out=None):
+        if self._closed:
+            raise RuntimeError("weight fetcher is closed")
+        device = self._device(device)
+        request = self._prepare(q, scale, device)
+        result = dispatch.execute_typed_transfer(request, resources=self._owner(device), out=out)
+        rep = result.report
+        self.shapes.add(tuple(q.shape))
+        self.report.add_dispatch(rep["implementation"])
+        self.report.add_bytes(self.kind, rep["source_bytes"], rep["wire_bytes"], rep["destination_bytes"],
+                              payload=rep["payload_bytes_transferred"])
+        return result.tensor
+
+    def fetch_many(self, weights, device, *, max_scratch_bytes=64 << 20):
+        """Fetch related (int8 matrix, scale) pairs; outputs are independent tensors."""
+        device = self._device(device)
+        return [self.fetch(q, s, device) for q, s in weights]
+
+    def template(self, q_shape, scale):
+        """A reusable dispatch template for one matrix shape and scale (no buffers)."""
+        bindings = {"s0": int(q_shape[0]), "s1": int(q_shape[1])}
+        declared = self.compiled.parameter_extents(bindings)
+        snap = dispatch._parameter_snapshot("scale", scale, declared["scale"])
+        bound = pyreloc.bind_typed(self.compiled.decoded_plan, bindings, {"scale": snap})
+        return pyreloc.prepare_dispatch_template(bound, implementation="b200_fused_h2d@dma_ring")
+
+    @staticmethod
+    def reference(q, scale, device, layout="reference"):
+        """The same conversion in PyTorch on the GPU (float32 arithmetic)."""
+        q = q.to(device)
+        scale = scale.to(device)
+        if layout == "reference":
+            return (q.float() * scale).t().contiguous()
+        return (q.float() * scale[:, None]).half().t().contiguous()
+
+    def close(self):
+        if self._closed:
+            return
+        self._closed = True
+        self._cleanup.close()
+
+    def __enter__(self):
+        if self._closed:
+            raise RuntimeError("weight fetcher is closed")
+        return self
+
+    def __exit__(self, exc_type, exc, tb):
+        self.close()
+        return False
+
+
+def shard_bounds(extent: int, world: int, rank: int):
+    """Result rows [begin, end) of ``rank``'s window (contiguous, near-equal)."""
+    return extent * rank // world, extent * (rank + 1) // world
+
+
+class ShardedLayerFetch:
+    """Per-rank sharded fetch of a set of matrices + NCCL all-gather.
+
+    ``mats``: list of dicts with ``tmpl`` (a dispatch template for int8
+    ``[out, in]`` -> f16 ``[in, out]``), ``out``/``in`` extents, and ``host`` /
+    ``dev`` source tensors. ``outputs``: matching full f16 ``[in, out]``
+    tensors on this rank's GPU. Requires ``in`` divisible by the world size
+    (equal shards for the in-place all-gather).
+    """
+
+    def __init__(self, resources, device_index, world=1, rank=0, group=None, chunk_bytes=16 << 20,
+                 ring_slots=4):
+        self.res = resources
+        self.device = device_index
+        self.world, self.rank, self.group = world, rank, group
+        self.chunk_bytes, self.ring_slots = chunk_bytes, ring_slots
+
+    def fetch(self, mats, outputs, host_source=True):
+        """Enqueue every matrix (and its all-gather); returns collective handles."""
+        import torch
+        import torch.distributed as dist
+
+        handles = []
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        for m, out in zip(mats, outputs):
+            if m["in"] % self.world:
+                raise ValueError("in_features must divide by the world size")
+            b, e = shard_bounds(m["in"], self.world, self.rank)
+            shard = out[b:e]
+            src = m["host"] if host_source else m["dev"]
+            pyreloc.execute_rows(m["tmpl"], src.data_ptr(), shard.data_ptr(), b, e, device=self.device,
+                                 host_source=host_source, resources=self.res, caller_stream=stream,
+                                 async_completion=True, route="dma_ring", chunk_size=self.chunk_bytes,
+                                 n_buffers=self.ring_slots)
+            if self.world > 1:
+                handles.append(dist.all_gather_into_tensor(out.view(-1), shard.reshape(-1), group=self.group,
+                                                           async_op=True))
+        return handles
