@@ -74,9 +74,11 @@ std::string q(const std::string &s) {
   for (char c : s) {
     if (c == '"' || c == '\\')
       o += '\\';
-    if (static_cast<unsigned char>(c) < 0x20) {
+    // Control and non-ASCII bytes are escaped byte-wise (names are opaque
+    // wire bytes, not necessarily UTF-8).
+    if (static_cast<unsigned char>(c) < 0x20 || static_cast<unsigned char>(c) >= 0x80) {
       char b[8];
-      std::snprintf(b, sizeof b, "\\u%04x", c);
+      std::snprintf(b, sizeof b, "\\u%04x", static_cast<unsigned char>(c));
       o += b;
       continue;
     }

@@ -280,6 +280,12 @@ def _fold_reshape(st, shape):
             else:
                 raise UnsupportedRecipe("invalid_reshape", "cannot match extents")
         n_old, n_new = i_end - i, j_end - j
+        if not split_ok and n_old == 1 and n_new > 1:
+            # products matched symbolically (X floordiv C times C): the split
+            # still needs its divisibility guard
+            split_ok, divisor = _matches_split(_padded(st, i), targets[j:j_end])
+            if not split_ok:
+                raise UnsupportedRecipe("invalid_reshape", "cannot split the axis into the target run")
         if split_ok or (n_old == 1 and n_new > 1):
             if _has_pad(st, i):
                 raise UnsupportedRecipe("reshape_pad", "splitting a padded axis")
