@@ -116,6 +116,10 @@ int sbc_relocate_transpose(const sbc_relocate *desc, void *stream);
 int sbc_fill(void *dst, int64_t count, int32_t width, uint64_t bits, void *stream);
 /* Kernels launched by this library since load (instrumentation). */
 uint64_t sbc_launch_count(void);
+/* The current device's kernel fault word, then cleared: 0 none, 2 a TMA copy
+ * a kernel waited for did not land within the wait limit (the kernel left
+ * early; its output is incomplete). Synchronizes with the device. */
+int sbc_device_fault(int *code);
 
 /* ---- devices, memory and copies */
 int sbc_device_count(int *count);

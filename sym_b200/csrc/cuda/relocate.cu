@@ -18,9 +18,12 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
+#include <cudaTypedefs.h>
 
 #include <atomic>
 #include <cstdint>
+#include <cstdlib>
+#include <mutex>
 
 namespace {
 
@@ -748,6 +751,198 @@ __global__ void __launch_bounds__(256, 4) k_tile_s8(const __grid_constant__ sbc_
 }
 
 // ---------------------------------------------------------------------------
+// TMA-pipelined int8 tile transpose (dequantize -> f16/bf16), sm_100a.
+//
+// The source box is viewed by a 3-D tensor map (x = A bytes, y = group of 8
+// source rows, z = row within the group; strides 8*Sb and Sb), so one
+// 128 x 8 x 8 box lands source row 8c+j at shared slot 8j+c. With the 128-byte
+// swizzle (16-byte chunk index XOR slot mod 8) the store phase -- thread
+// (ag, c) reads rows 8c..8c+7 at byte column 4*ag -- hits 32 distinct banks.
+// Each CTA keeps KStages tiles in flight: thread 0 arms an mbarrier with the
+// tile's byte count and issues cp.async.bulk.tensor (no multicast, local
+// memory only); the tile's consumers start once the barrier phase completes.
+// Conversion and the 16-byte streaming stores are those of k_tile_s8.
+//
+// Waits are bounded: thread 0 polls the barrier at most kWaitLimit times and
+// broadcasts the outcome through shared memory at the CTA barrier, so the
+// whole CTA leaves together on a timeout (status word set to 2) after a
+// bounded drain of the copies it issued; no thread can be left at a barrier.
+// ---------------------------------------------------------------------------
+
+/// Set by a kernel whose bounded wait ran out (2 = TMA copy never landed);
+/// read and cleared by sbc_device_fault.
+__device__ int g_device_fault = 0;
+
+constexpr int KStages = 4;
+constexpr int KTmaTileBytes = 64 * 128;
+constexpr uint32_t kWaitLimit = 1u << 24;
+
+__device__ __forceinline__ uint32_t smem_addr(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+               : "memory");
+}
+
+/// Bounded wait for `parity`; true when the phase completed.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+  const uint32_t a = smem_addr(bar);
+  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+    uint32_t done;
+    asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+                 " selp.u32 %0, 1, 0, p;\n}"
+                 : "=r"(done)
+                 : "r"(a), "r"(parity)
+                 : "memory");
+    if (done)
+      return true;
+  }
+  return false;
+}
+
+__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, int32_t x, int32_t y, int32_t z,
+                                            uint64_t *bar) {
+  asm volatile("cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+               " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_addr(dst)),
+               "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_addr(bar))
+               : "memory");
+}
+
+template <int CHAIN, int CH_ON>
+__global__ void __launch_bounds__(256, 3) k_tma_s8(const __grid_constant__ CUtensorMap tmap,
+                                                   const __grid_constant__ sbc_relocate d, FastDiv div_b,
+                                                   uint32_t tiles) {
+  constexpr int TB = 64, VD = 8;
+  extern __shared__ __align__(1024) uint8_t dyn[];
+  __shared__ __align__(8) uint64_t full[KStages];
+  __shared__ int timed_out;
+  uint8_t *stage0 = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(dyn) + 1023) & ~uintptr_t(1023));
+  const int t = threadIdx.x, ag = t >> 3, c = t & 7;
+  const int64_t Da = d.dst_strides[0], DaB = Da * 2;
+  uint8_t *const dst0 = static_cast<uint8_t *>(d.dst) - d.dst_offset * 2;
+  const sbc_stage &s = d.stages[0];
+  const uint32_t G = gridDim.x;
+
+  auto tile_xy = [&](uint32_t job, uint32_t &ta, uint32_t &tb) {
+    ta = fdiv(job, div_b);
+    tb = job - ta * div_b.d;
+  };
+  auto issue = [&](uint32_t k) { // thread 0 only: tile of local index k into stage k % KStages
+    const uint32_t job = blockIdx.x + k * G;
+    if (job >= tiles)
+      return;
+    uint32_t ta, tb;
+    tile_xy(job, ta, tb);
+    const int st = k % KStages;
+    mbar_expect_tx(&full[st], KTmaTileBytes);
+    tma_load_3d(stage0 + st * KTmaTileBytes, &tmap, static_cast<int32_t>(ta * 128), static_cast<int32_t>(tb * 8), 0,
+                &full[st]);
+  };
+
+  if (t == 0) {
+    for (int i = 0; i < KStages; ++i)
+      mbar_init(&full[i], 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap)) : "memory");
+    timed_out = 0;
+  }
+  __syncthreads();
+  if (t == 0)
+    for (int i = 0; i < KStages; ++i)
+      issue(i);
+
+  for (uint32_t k = 0;; ++k) {
+    const uint32_t job = blockIdx.x + k * G;
+    if (job >= tiles)
+      break;
+    const int st = k % KStages;
+    if (t == 0 && !mbar_wait(&full[st], (k / KStages) & 1))
+      timed_out = 1;
+    __syncthreads(); // tile k landed (or timed out); every thread is done reading tile k-1
+    if (timed_out) {
+      if (t == 0) {
+        if (d.status)
+          atomicExch(d.status, 2);
+        atomicExch(&g_device_fault, 2);
+        // bounded drain of this CTA's copies still in flight
+        for (uint32_t q = k; q + 1 < k + KStages && blockIdx.x + q * G < tiles; ++q)
+          mbar_wait(&full[q % KStages], (q / KStages) & 1);
+      }
+      return;
+    }
+    if (t == 0 && k > 0) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      issue(k - 1 + KStages); // stage of tile k-1 is free
+    }
+    uint32_t ta, tb;
+    tile_xy(job, ta, tb);
+    const int64_t a0 = d.box_lo[0] + static_cast<int64_t>(ta) * 128;
+    const int64_t b0 = d.box_lo[1] + static_cast<int64_t>(tb) * TB;
+    const uint8_t *sp = stage0 + st * KTmaTileBytes;
+    uint32_t w[VD];
+#pragma unroll
+    for (int j = 0; j < VD; ++j)
+      w[j] = *reinterpret_cast<const uint32_t *>(sp + (j * 8 + c) * 128 + ((((4 * ag) >> 4) ^ c) << 4) +
+                                                 ((4 * ag) & 15)) ^
+             0x80808080u;
+    float ps[VD], bias[VD];
+    bool ok = true;
+#pragma unroll
+    for (int j = 0; j < VD; ++j) {
+      int64_t ch = CH_ON == 2 ? b0 + c * VD + j : 0;
+      if (ch >= s.channel_length) {
+        ok = false;
+        ch = 0;
+      }
+      ps[j] = s.param[ch];
+      bias[j] = 8388736.0f + static_cast<float>(zp_of(s, ch));
+    }
+    uint8_t *dp = dst0 + (a0 * Da + b0) * 2 + static_cast<int64_t>(4 * ag) * DaB + c * 16;
+#pragma unroll
+    for (int i = 0; i < 4; ++i, dp += DaB) {
+      if constexpr (CH_ON == 1) {
+        int64_t ch = a0 + 4 * ag + i;
+        if (ch >= s.channel_length) {
+          ok = false;
+          ch = 0;
+        }
+        const float sc = s.param[ch], bi = 8388736.0f + static_cast<float>(zp_of(s, ch));
+#pragma unroll
+        for (int j = 0; j < VD; ++j) {
+          ps[j] = sc;
+          bias[j] = bi;
+        }
+      }
+      float f[VD];
+#pragma unroll
+      for (int j = 0; j < VD; ++j)
+        f[j] = __fmul_rn(__fsub_rn(__int_as_float(__byte_perm(w[j], 0x4B000000u, 0x7650 + i)), bias[j]), ps[j]);
+      uint4 out;
+      uint32_t *u = reinterpret_cast<uint32_t *>(&out);
+#pragma unroll
+      for (int j = 0; j < VD; j += 2) {
+        if constexpr (CHAIN == CH_DQ_BF16) {
+          const __nv_bfloat162 h = __floats2bfloat162_rn(f[j], f[j + 1]);
+          u[j / 2] = *reinterpret_cast<const uint32_t *>(&h);
+        } else {
+          const __half2 h = __floats2half2_rn(f[j], f[j + 1]);
+          u[j / 2] = *reinterpret_cast<const uint32_t *>(&h);
+        }
+      }
+      __stcs(reinterpret_cast<uint4 *>(dp), out);
+    }
+    if (!ok)
+      flag(d);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Fill
 // ---------------------------------------------------------------------------
 
@@ -893,6 +1088,59 @@ template <int WS, int WD, int CH> struct TransposeLaunch {
     }
   }
 };
+
+FastDiv make_fastdiv(uint32_t dv) {
+  FastDiv f;
+  uint32_t l = 0;
+  while ((1ull << l) < dv)
+    ++l;
+  f.s = 31 + l;
+  f.d = dv;
+  f.m = ((1ull << f.s) + dv - 1) / dv;
+  return f;
+}
+
+/// TMA path switch: on unless SYM_B200_TMA=0 (kept for A/B measurement).
+bool tma_enabled() {
+  static const bool on = [] {
+    const char *v = std::getenv("SYM_B200_TMA");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    else
+      cudaGetLastError();
+  });
+  return fn;
+}
+
+/// The 3-D view of an int8 [rows, cols] box used by k_tma_s8: x = column
+/// bytes, y = group of 8 rows (stride 8*pitch), z = row in group (stride
+/// pitch); box 128 x 8 x 8 with the 128-byte swizzle. False when the driver
+/// rejects the description (the caller then uses k_tile_s8).
+bool encode_rows3d(CUtensorMap *map, const void *base, int64_t cols, int64_t rows, int64_t pitch) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+  if (!enc || reinterpret_cast<uintptr_t>(base) % 16 || pitch % 16 || rows % 8)
+    return false;
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows / 8), 8};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(pitch * 8), static_cast<cuuint64_t>(pitch)};
+  const cuuint32_t box[3] = {128, 8, 8};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void *>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
 
 template <int WS, int WD, int CH> struct TileLaunch {
   static int run(const sbc_relocate &d, int ch_on, int64_t tiles_b, int64_t tiles, int64_t nbatch, cudaStream_t s) {
@@ -1066,6 +1314,29 @@ int sbc_relocate_transpose(const sbc_relocate *desc, void *stream) {
     return 0;
   const int ch_on = tile_eligible(d);
   const bool dq = chain == CH_DQ || chain == CH_DQ_F16 || chain == CH_DQ_BF16;
+  if (ch_on >= 0 && d.rank == 2 && d.src_width == 1 && d.dst_width == 2 &&
+      (chain == CH_DQ_F16 || chain == CH_DQ_BF16) && ext_a % 128 == 0 && ext_b % 64 == 0 &&
+      (ext_a / 128) * (ext_b / 64) < (int64_t(1) << 31) && tma_enabled()) {
+    CUtensorMap map;
+    const uint8_t *base = static_cast<const uint8_t *>(d.src) + d.box_lo[0] + d.box_lo[1] * d.src_strides[1] -
+                          d.src_offset;
+    if (encode_rows3d(&map, base, ext_a, ext_b, d.src_strides[1])) {
+      const int64_t tiles_b = ext_b / 64, tiles = (ext_a / 128) * tiles_b;
+      const int64_t cap = static_cast<int64_t>(sm_count()) * 3;
+      const unsigned blocks = static_cast<unsigned>(tiles < cap ? tiles : cap);
+      const FastDiv div_b = make_fastdiv(static_cast<uint32_t>(tiles_b));
+      const size_t smem = KStages * KTmaTileBytes + 1024;
+      cudaStream_t st = static_cast<cudaStream_t>(stream);
+      const uint32_t nt = static_cast<uint32_t>(tiles);
+#define SBC_TMA(CH_, ON_) k_tma_s8<CH_, ON_><<<blocks, 256, smem, st>>>(map, d, div_b, nt)
+      if (chain == CH_DQ_F16)
+        ch_on == 0 ? SBC_TMA(CH_DQ_F16, 0) : ch_on == 1 ? SBC_TMA(CH_DQ_F16, 1) : SBC_TMA(CH_DQ_F16, 2);
+      else
+        ch_on == 0 ? SBC_TMA(CH_DQ_BF16, 0) : ch_on == 1 ? SBC_TMA(CH_DQ_BF16, 1) : SBC_TMA(CH_DQ_BF16, 2);
+#undef SBC_TMA
+      return launched(cudaSuccess);
+    }
+  }
   if (ch_on >= 0 && dq && d.src_width == 1 && ext_a >= 128 && ext_b * d.dst_width >= 128 &&
       ((ext_a + 127) / 128) * ((ext_b * d.dst_width + 127) / 128) * nbatch < (int64_t(1) << 31)) {
     const int64_t tbn = 128 / d.dst_width;
@@ -1141,5 +1412,13 @@ int sbc_fill(void *dst, int64_t count, int32_t width, uint64_t bits, void *strea
 }
 
 uint64_t sbc_launch_count(void) { return g_launches.load(); }
+
+int sbc_device_fault(int *code) {
+  int zero = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(code, g_device_fault, sizeof(int));
+  if (e == cudaSuccess && *code)
+    e = cudaMemcpyToSymbol(g_device_fault, &zero, sizeof(int));
+  return e;
+}
 
 } // extern "C"

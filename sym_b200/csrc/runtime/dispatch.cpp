@@ -212,6 +212,13 @@ std::optional<TransferError> finish(const b200::Lowered &l, CudaBackend &b, cons
     b.fail("completion", rc);
     return terr("backend_failure", b.error());
   }
+  int fault = 0;
+  if ((rc = sbc_device_fault(&fault))) {
+    b.fail("fault word", rc);
+    return terr("backend_failure", b.error());
+  }
+  if (fault)
+    return terr("backend_failure", "a kernel's bounded wait for a TMA copy ran out; the output is incomplete");
   if (timed) {
     float ms = 0;
     if (sbc_event_elapsed_ms(b.startEvent(), b.stopEvent(), &ms) == 0 && bytes > 0) {
