@@ -773,7 +773,7 @@ __global__ void __launch_bounds__(256, 4) k_tile_s8(const __grid_constant__ sbc_
 /// read and cleared by sbc_device_fault.
 __device__ int g_device_fault = 0;
 
-constexpr int KStages = 4;
+constexpr int KStages = 6;
 constexpr int KTmaTileBytes = 64 * 128;
 constexpr uint32_t kWaitLimit = 1u << 24;
 
@@ -822,6 +822,10 @@ __global__ void __launch_bounds__(256, 3) k_tma_s8(const __grid_constant__ CUten
   extern __shared__ __align__(1024) uint8_t dyn[];
   __shared__ __align__(8) uint64_t full[KStages];
   __shared__ int timed_out;
+  // Per-column dequantize parameters of a tile, staged one tile ahead.
+  __shared__ __align__(16) float s_scale[2][64];
+  __shared__ __align__(16) float s_bias[2][64];
+  __shared__ int s_bad[2];
   uint8_t *stage0 = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(dyn) + 1023) & ~uintptr_t(1023));
   const int t = threadIdx.x, ag = t >> 3, c = t & 7;
   const int64_t Da = d.dst_strides[0], DaB = Da * 2;
@@ -845,6 +849,35 @@ __global__ void __launch_bounds__(256, 3) k_tma_s8(const __grid_constant__ CUten
                 &full[st]);
   };
 
+  // Threads 0..63 load the parameters of local tile k's 64 columns (CH_ON == 2).
+  auto stage_params = [&](uint32_t k) {
+    if constexpr (CH_ON == 2) {
+      const uint32_t job = blockIdx.x + k * G;
+      if (t < 64 && job < tiles) {
+        uint32_t ta, tb;
+        tile_xy(job, ta, tb);
+        int64_t ch = d.box_lo[1] + static_cast<int64_t>(tb) * TB + t;
+        if (ch >= s.channel_length) {
+          s_bad[k & 1] = 1;
+          ch = 0;
+        }
+        s_scale[k & 1][t] = s.param[ch];
+        s_bias[k & 1][t] = 8388736.0f + static_cast<float>(zp_of(s, ch));
+      }
+    }
+  };
+  if (t < 2)
+    s_bad[t] = 0;
+  __syncthreads();
+  stage_params(0);
+  float ps[VD], bias[VD];
+  if constexpr (CH_ON == 0) {
+#pragma unroll
+    for (int j = 0; j < VD; ++j) {
+      ps[j] = s.param[0];
+      bias[j] = 8388736.0f + static_cast<float>(zp_of(s, 0));
+    }
+  }
   if (t == 0) {
     for (int i = 0; i < KStages; ++i)
       mbar_init(&full[i], 1);
@@ -880,6 +913,18 @@ __global__ void __launch_bounds__(256, 3) k_tma_s8(const __grid_constant__ CUten
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       issue(k - 1 + KStages); // stage of tile k-1 is free
     }
+    bool ok = true;
+    if constexpr (CH_ON == 2) {
+      const float4 *sc4 = reinterpret_cast<const float4 *>(&s_scale[k & 1][c * VD]);
+      const float4 *bi4 = reinterpret_cast<const float4 *>(&s_bias[k & 1][c * VD]);
+      const float4 s0 = sc4[0], s1 = sc4[1], b0v = bi4[0], b1v = bi4[1];
+      ps[0] = s0.x, ps[1] = s0.y, ps[2] = s0.z, ps[3] = s0.w, ps[4] = s1.x, ps[5] = s1.y, ps[6] = s1.z, ps[7] = s1.w;
+      bias[0] = b0v.x, bias[1] = b0v.y, bias[2] = b0v.z, bias[3] = b0v.w;
+      bias[4] = b1v.x, bias[5] = b1v.y, bias[6] = b1v.z, bias[7] = b1v.w;
+      ok = !s_bad[k & 1];
+    }
+    // parameters of tile k+1 into the other buffer (read by everyone at k+1)
+    stage_params(k + 1);
     uint32_t ta, tb;
     tile_xy(job, ta, tb);
     const int64_t a0 = d.box_lo[0] + static_cast<int64_t>(ta) * 128;
@@ -891,18 +936,6 @@ __global__ void __launch_bounds__(256, 3) k_tma_s8(const __grid_constant__ CUten
       w[j] = *reinterpret_cast<const uint32_t *>(sp + (j * 8 + c) * 128 + ((((4 * ag) >> 4) ^ c) << 4) +
                                                  ((4 * ag) & 15)) ^
              0x80808080u;
-    float ps[VD], bias[VD];
-    bool ok = true;
-#pragma unroll
-    for (int j = 0; j < VD; ++j) {
-      int64_t ch = CH_ON == 2 ? b0 + c * VD + j : 0;
-      if (ch >= s.channel_length) {
-        ok = false;
-        ch = 0;
-      }
-      ps[j] = s.param[ch];
-      bias[j] = 8388736.0f + static_cast<float>(zp_of(s, ch));
-    }
     uint8_t *dp = dst0 + (a0 * Da + b0) * 2 + static_cast<int64_t>(4 * ag) * DaB + c * 16;
 #pragma unroll
     for (int i = 0; i < 4; ++i, dp += DaB) {
@@ -1328,7 +1361,9 @@ int sbc_relocate_transpose(const sbc_relocate *desc, void *stream) {
       const size_t smem = KStages * KTmaTileBytes + 1024;
       cudaStream_t st = static_cast<cudaStream_t>(stream);
       const uint32_t nt = static_cast<uint32_t>(tiles);
-#define SBC_TMA(CH_, ON_) k_tma_s8<CH_, ON_><<<blocks, 256, smem, st>>>(map, d, div_b, nt)
+#define SBC_TMA(CH_, ON_)                                                                                      \
+  (cudaFuncSetAttribute(k_tma_s8<CH_, ON_>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)),     \
+   k_tma_s8<CH_, ON_><<<blocks, 256, smem, st>>>(map, d, div_b, nt))
       if (chain == CH_DQ_F16)
         ch_on == 0 ? SBC_TMA(CH_DQ_F16, 0) : ch_on == 1 ? SBC_TMA(CH_DQ_F16, 1) : SBC_TMA(CH_DQ_F16, 2);
       else
