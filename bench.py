@@ -51,6 +51,11 @@ METRIC = "relocated GB/s/GPU (H2D+transform) as % of pinned memcpy ceiling; laye
 LLAMA70B = [("q", 8192, 8192), ("k", 1024, 8192), ("v", 1024, 8192), ("o", 8192, 8192),
             ("gate", 28672, 8192), ("up", 28672, 8192), ("down", 8192, 28672)]  # (name, out, in)
 LAYERS = 16
+# DRAM bytes (read + write) per element of the gate launch, from one ncu
+# capture of `bench.py --kernel-case`: 247.8 MB + 414.5 MB over 28672 x 8192
+# elements. Writes sit below the algorithmic 2 B/element because the last
+# dirty lines are still in L2 when the kernel ends.
+GATE_DRAM_BYTES_PER_ELEM = (247.833344e6 + 414.507264e6) / (28672 * 8192)
 
 
 def _peaks():
@@ -290,22 +295,32 @@ def run_ours(args):
     ck = clocks.stop() if clocks else None
     launches_value = l1 - l0
 
-    # dominant kernel: one layer's fused dequant->f16->transpose kernels on
-    # the compute stream, device-resident source (bytes: int8 read + f16 write)
+    # dominant kernel (k_tma_s8, every launch of the step): one launch on the
+    # largest matrix (gate, this rank's result rows), device-resident source,
+    # timed on the compute stream it runs on. Algorithmic bytes per launch:
+    # 1 B int8 read + 2 B f16 written per element + 4 B per source-row scale.
     torch.cuda.synchronize(dev)
+    gi = [m["name"] for m in distinct[0]].index("gate")
+    gm, gout, (gb, ge) = distinct[0][gi], outs[0][gi], rows[gi]
+
+    def gate_launch():
+        pyreloc.execute_rows(gm["tmpl"], gm["dev"].data_ptr(), gout[gb:ge].data_ptr(), gb, ge, device=local,
+                             host_source=False, resources=res, async_completion=True)
+
+    for _ in range(3):
+        gate_launch()
     ka, kb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    reps = 3
+    reps = 10  # 705 MB per launch at N=1: larger than L2, so launches do not hit each other's lines
     ka.record(compute_stream)
     for _ in range(reps):
-        for m, out, (b, e) in zip(distinct[0], outs[0], rows):
-            pyreloc.execute_rows(m["tmpl"], m["dev"].data_ptr(), out[b:e].data_ptr(), b, e, device=local,
-                                 host_source=False, resources=res, async_completion=True)
+        gate_launch()
     kb.record(compute_stream)
     torch.cuda.synchronize(dev)
     kernel_s = ka.elapsed_time(kb) * 1e-3 / reps
-    elems_rank = sum(m["out"] * (e - b) for m, (b, e) in zip(distinct[0], rows))
-    kernel_bytes = elems_rank * 3 + sum(m["out"] * 4 for m in distinct[0])
+    gate_elems = gm["out"] * (ge - gb)
+    kernel_bytes = gate_elems * 3 + gm["out"] * 4
     achieved_gbs = kernel_bytes / kernel_s / 1e9
+    traffic = GATE_DRAM_BYTES_PER_ELEM * gate_elems
 
     ceiling = pinned_h2d_gbs(torch, dev)
     ceiling = min(ceiling, max_over_ranks(ceiling)) if world > 1 else ceiling
@@ -347,9 +362,12 @@ def run_ours(args):
         "e2e": {"value": layers_e2e, "unit": "layers/s", "ms_per_step": 1e3 * t_e2e / args.steps,
                 "h2d_bytes_per_step": int(per_gpu_wire * LAYERS), "d2h_bytes_per_step": int(sample.numel() * 2)},
         "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": hbm, "unit": "GB/s",
-                     "frac": achieved_gbs / hbm, "traffic": None, "peak_source": peak_note,
-                     "kernel": "k_transpose<1,2,CH_DQ_F16> (one layer, this rank's windows)",
-                     "bytes_per_launch_note": "int8 read + f16 write per element + 4 B per row scale"},
+                     "frac": achieved_gbs / hbm, "traffic": traffic, "peak_source": peak_note,
+                     "kernel": "k_tma_s8<CH_DQ_F16, per-column scale> on gate [28672, 8192], this rank's rows",
+                     "bytes_per_launch": kernel_bytes, "launch_ms": kernel_s * 1e3,
+                     "bytes_per_launch_note": "int8 read + f16 write per element + 4 B per source-row scale",
+                     "traffic_note": "ncu dram__bytes_read.sum + dram__bytes_write.sum of the full gate launch "
+                                     "(--kernel-case), scaled by this rank's share of its elements"},
         "gpu_launches": int(launches_value), "clocks": ck,
     }
     if cpu:

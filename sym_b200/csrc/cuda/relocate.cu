@@ -758,15 +758,23 @@ __global__ void __launch_bounds__(256, 4) k_tile_s8(const __grid_constant__ sbc_
 // 128 x 8 x 8 box lands source row 8c+j at shared slot 8j+c. With the 128-byte
 // swizzle (16-byte chunk index XOR slot mod 8) the store phase -- thread
 // (ag, c) reads rows 8c..8c+7 at byte column 4*ag -- hits 32 distinct banks.
-// Each CTA keeps KStages tiles in flight: thread 0 arms an mbarrier with the
-// tile's byte count and issues cp.async.bulk.tensor (no multicast, local
-// memory only); the tile's consumers start once the barrier phase completes.
+//
+// Warp roles: warps 0-7 convert and store, warp 8 produces. The producer keeps
+// KStages tiles in flight in a ring of shared-memory stages, each with a
+// `full` mbarrier (32 producer arrivals + the tile's byte count) and an
+// `empty` mbarrier (one arrival per consumer warp). Per tile it waits for the
+// stage to be empty, lane 0 arms `full` with the byte count and issues
+// cp.async.bulk.tensor (no multicast, local memory only), then the lanes stage
+// the tile's 64 per-column scales and biases next to it and arrive. Consumer
+// warps wait on `full`, read the tile and its parameters into registers,
+// release the stage and convert; there is no CTA-wide barrier in the loop, so
+// warps drift up to KStages tiles apart instead of meeting every tile.
 // Conversion and the 16-byte streaming stores are those of k_tile_s8.
 //
-// Waits are bounded: thread 0 polls the barrier at most kWaitLimit times and
-// broadcasts the outcome through shared memory at the CTA barrier, so the
-// whole CTA leaves together on a timeout (status word set to 2) after a
-// bounded drain of the copies it issued; no thread can be left at a barrier.
+// Every wait is bounded (kWaitLimit polls). A thread whose wait runs out sets
+// the status word and the device fault word to 2 and leaves; thread 0 (or the
+// producer) first waits, again bounded, for the copies that may still be in
+// flight into this CTA's shared memory.
 // ---------------------------------------------------------------------------
 
 /// Set by a kernel whose bounded wait ran out (2 = TMA copy never landed);
@@ -775,6 +783,8 @@ __device__ int g_device_fault = 0;
 
 constexpr int KStages = 6;
 constexpr int KTmaTileBytes = 64 * 128;
+constexpr int KTmaConsumers = 256;              // warps 0-7
+constexpr int KTmaThreads = KTmaConsumers + 32; // + the producer warp
 constexpr uint32_t kWaitLimit = 1u << 24;
 
 __device__ __forceinline__ uint32_t smem_addr(const void *p) {
@@ -788,6 +798,31 @@ __device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
 __device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
                : "memory");
+}
+
+/// Job order of k_tma_s8. Jobs walk groups of 2^lg source-column blocks (of
+/// 128 bytes); inside a group the column block varies fastest, so the tiles
+/// in flight at once read 2^lg * 128 contiguous bytes of each source row
+/// while their outputs still cover whole runs of destination rows.
+/// group.d = 2^lg * (source-row blocks of 64).
+struct TileOrder {
+  FastDiv group;
+  uint32_t lg;
+};
+
+__device__ __forceinline__ void tile_of(uint32_t job, const TileOrder &o, uint32_t &ta, uint32_t &tb) {
+  const uint32_t g = fdiv(job, o.group), r = job - g * o.group.d;
+  ta = (g << o.lg) + (r & ((1u << o.lg) - 1));
+  tb = r >> o.lg;
+}
+
+/// Shared-memory slot of parameter column n (0..63) of a tile: columns 32..63
+/// swap their 16-byte halves, so the eight float4 reads of a warp (column
+/// groups 8c..8c+3 or 8c+4..8c+7, c = 0..7) fall on 32 distinct banks.
+__device__ __forceinline__ int param_slot(int n) { return n ^ (((n >> 5) & 1) << 2); }
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
 
 /// Bounded wait for `parity`; true when the phase completed.
@@ -815,61 +850,114 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, i
 }
 
 template <int CHAIN, int CH_ON>
-__global__ void __launch_bounds__(256, 3) k_tma_s8(const __grid_constant__ CUtensorMap tmap,
-                                                   const __grid_constant__ sbc_relocate d, FastDiv div_b,
-                                                   uint32_t tiles) {
+__global__ void __launch_bounds__(KTmaThreads, 3) k_tma_s8(const __grid_constant__ CUtensorMap tmap,
+                                                           const __grid_constant__ sbc_relocate d, TileOrder ord,
+                                                           uint32_t tiles) {
   constexpr int TB = 64, VD = 8;
   extern __shared__ __align__(1024) uint8_t dyn[];
-  __shared__ __align__(8) uint64_t full[KStages];
+  __shared__ __align__(8) uint64_t full[KStages], empty[KStages];
+  // Per-column dequantize parameters of the tile in each stage (CH_ON == 2).
+  __shared__ __align__(16) float s_scale[KStages][64];
+  __shared__ __align__(16) float s_bias[KStages][64];
+  __shared__ int s_bad[KStages];
   __shared__ int timed_out;
-  // Per-column dequantize parameters of a tile, staged one tile ahead.
-  __shared__ __align__(16) float s_scale[2][64];
-  __shared__ __align__(16) float s_bias[2][64];
-  __shared__ int s_bad[2];
   uint8_t *stage0 = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(dyn) + 1023) & ~uintptr_t(1023));
-  const int t = threadIdx.x, ag = t >> 3, c = t & 7;
-  const int64_t Da = d.dst_strides[0], DaB = Da * 2;
-  uint8_t *const dst0 = static_cast<uint8_t *>(d.dst) - d.dst_offset * 2;
+  const int t = threadIdx.x;
   const sbc_stage &s = d.stages[0];
   const uint32_t G = gridDim.x;
 
-  auto tile_xy = [&](uint32_t job, uint32_t &ta, uint32_t &tb) {
-    ta = fdiv(job, div_b);
-    tb = job - ta * div_b.d;
-  };
-  auto issue = [&](uint32_t k) { // thread 0 only: tile of local index k into stage k % KStages
-    const uint32_t job = blockIdx.x + k * G;
-    if (job >= tiles)
-      return;
-    uint32_t ta, tb;
-    tile_xy(job, ta, tb);
-    const int st = k % KStages;
-    mbar_expect_tx(&full[st], KTmaTileBytes);
-    tma_load_3d(stage0 + st * KTmaTileBytes, &tmap, static_cast<int32_t>(ta * 128), static_cast<int32_t>(tb * 8), 0,
-                &full[st]);
-  };
-
-  // Threads 0..63 load the parameters of local tile k's 64 columns (CH_ON == 2).
-  auto stage_params = [&](uint32_t k) {
-    if constexpr (CH_ON == 2) {
-      const uint32_t job = blockIdx.x + k * G;
-      if (t < 64 && job < tiles) {
-        uint32_t ta, tb;
-        tile_xy(job, ta, tb);
-        int64_t ch = d.box_lo[1] + static_cast<int64_t>(tb) * TB + t;
-        if (ch >= s.channel_length) {
-          s_bad[k & 1] = 1;
-          ch = 0;
-        }
-        s_scale[k & 1][t] = s.param[ch];
-        s_bias[k & 1][t] = 8388736.0f + static_cast<float>(zp_of(s, ch));
-      }
+  if (t == 0) {
+    for (int i = 0; i < KStages; ++i) {
+      mbar_init(&full[i], 32);
+      mbar_init(&empty[i], KTmaConsumers / 32);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    timed_out = 0;
+  }
+  __syncthreads(); // the only CTA-wide barrier
+  auto fail = [&]() {
+    if (atomicExch(&timed_out, 1) == 0) {
+      if (d.status)
+        atomicExch(d.status, 2);
+      atomicExch(&g_device_fault, 2);
     }
   };
-  if (t < 2)
-    s_bad[t] = 0;
-  __syncthreads();
-  stage_params(0);
+  // Bounded wait for the copies of local tiles [lo, hi) (issued, maybe in flight).
+  auto drain = [&](uint32_t lo, uint32_t hi) {
+    for (uint32_t q = lo; q < hi && blockIdx.x + q * G < tiles; ++q)
+      mbar_wait(&full[q % KStages], (q / KStages) & 1);
+  };
+
+  if (t >= KTmaConsumers) { // ---- producer warp
+    const int lane = t - KTmaConsumers;
+    if (lane == 0)
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap)) : "memory");
+    // This lane's two parameter columns of a tile, loaded one tile ahead so
+    // the global-load latency overlaps the wait for a free stage.
+    float p_scale[2], p_bias[2];
+    bool p_bad = false;
+    auto load_params = [&](uint32_t k) {
+      if constexpr (CH_ON == 2) {
+        const uint32_t job = blockIdx.x + k * G;
+        if (job >= tiles)
+          return;
+        uint32_t ta, tb;
+        tile_of(job, ord, ta, tb);
+        p_bad = false;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          int64_t ch = d.box_lo[1] + static_cast<int64_t>(tb) * TB + lane + 32 * h;
+          if (ch >= s.channel_length) {
+            p_bad = true;
+            ch = 0;
+          }
+          p_scale[h] = s.param[ch];
+          p_bias[h] = 8388736.0f + static_cast<float>(zp_of(s, ch));
+        }
+      }
+    };
+    load_params(0);
+    for (uint32_t k = 0;; ++k) {
+      const uint32_t job = blockIdx.x + k * G;
+      if (job >= tiles)
+        break;
+      const int st = k % KStages;
+      if (k >= KStages && !mbar_wait(&empty[st], (k / KStages - 1) & 1)) {
+        fail();
+        if (lane == 0)
+          drain(k - KStages, k);
+        return;
+      }
+      // Every lane writes its parameters before its own arrival (lane 0's is
+      // the expect_tx), so the phase completes only after all of them.
+      if constexpr (CH_ON == 2) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          s_scale[st][param_slot(lane + 32 * h)] = p_scale[h];
+          s_bias[st][param_slot(lane + 32 * h)] = p_bias[h];
+        }
+        const bool bad = __any_sync(0xffffffffu, p_bad);
+        if (lane == 0)
+          s_bad[st] = bad;
+      }
+      if (lane == 0) {
+        uint32_t ta, tb;
+        tile_of(job, ord, ta, tb);
+        mbar_expect_tx(&full[st], KTmaTileBytes); // lane 0's arrival
+        tma_load_3d(stage0 + st * KTmaTileBytes, &tmap, static_cast<int32_t>(ta * 128), static_cast<int32_t>(tb * 8),
+                    0, &full[st]);
+      } else {
+        mbar_arrive(&full[st]);
+      }
+      load_params(k + 1);
+    }
+    return;
+  }
+
+  // ---- consumer warps
+  const int ag = t >> 3, c = t & 7;
+  const int64_t Da = d.dst_strides[0], DaB = Da * 2;
+  uint8_t *const dst0 = static_cast<uint8_t *>(d.dst) - d.dst_offset * 2;
   float ps[VD], bias[VD];
   if constexpr (CH_ON == 0) {
 #pragma unroll
@@ -878,55 +966,31 @@ __global__ void __launch_bounds__(256, 3) k_tma_s8(const __grid_constant__ CUten
       bias[j] = 8388736.0f + static_cast<float>(zp_of(s, 0));
     }
   }
-  if (t == 0) {
-    for (int i = 0; i < KStages; ++i)
-      mbar_init(&full[i], 1);
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap)) : "memory");
-    timed_out = 0;
-  }
-  __syncthreads();
-  if (t == 0)
-    for (int i = 0; i < KStages; ++i)
-      issue(i);
-
   for (uint32_t k = 0;; ++k) {
     const uint32_t job = blockIdx.x + k * G;
     if (job >= tiles)
       break;
     const int st = k % KStages;
-    if (t == 0 && !mbar_wait(&full[st], (k / KStages) & 1))
-      timed_out = 1;
-    __syncthreads(); // tile k landed (or timed out); every thread is done reading tile k-1
-    if (timed_out) {
-      if (t == 0) {
-        if (d.status)
-          atomicExch(d.status, 2);
-        atomicExch(&g_device_fault, 2);
-        // bounded drain of this CTA's copies still in flight
-        for (uint32_t q = k; q + 1 < k + KStages && blockIdx.x + q * G < tiles; ++q)
-          mbar_wait(&full[q % KStages], (q / KStages) & 1);
-      }
+    if (!mbar_wait(&full[st], (k / KStages) & 1)) {
+      fail();
+      if (t == 0) // the producer cannot pass tile k + KStages - 1 before this warp releases tile k
+        drain(k, k + KStages);
       return;
-    }
-    if (t == 0 && k > 0) {
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      issue(k - 1 + KStages); // stage of tile k-1 is free
     }
     bool ok = true;
     if constexpr (CH_ON == 2) {
-      const float4 *sc4 = reinterpret_cast<const float4 *>(&s_scale[k & 1][c * VD]);
-      const float4 *bi4 = reinterpret_cast<const float4 *>(&s_bias[k & 1][c * VD]);
-      const float4 s0 = sc4[0], s1 = sc4[1], b0v = bi4[0], b1v = bi4[1];
+      const int lo = param_slot(c * VD), hi = param_slot(c * VD + 4);
+      const float4 s0 = *reinterpret_cast<const float4 *>(&s_scale[st][lo]);
+      const float4 s1 = *reinterpret_cast<const float4 *>(&s_scale[st][hi]);
+      const float4 b0v = *reinterpret_cast<const float4 *>(&s_bias[st][lo]);
+      const float4 b1v = *reinterpret_cast<const float4 *>(&s_bias[st][hi]);
       ps[0] = s0.x, ps[1] = s0.y, ps[2] = s0.z, ps[3] = s0.w, ps[4] = s1.x, ps[5] = s1.y, ps[6] = s1.z, ps[7] = s1.w;
       bias[0] = b0v.x, bias[1] = b0v.y, bias[2] = b0v.z, bias[3] = b0v.w;
       bias[4] = b1v.x, bias[5] = b1v.y, bias[6] = b1v.z, bias[7] = b1v.w;
-      ok = !s_bad[k & 1];
+      ok = !s_bad[st];
     }
-    // parameters of tile k+1 into the other buffer (read by everyone at k+1)
-    stage_params(k + 1);
     uint32_t ta, tb;
-    tile_xy(job, ta, tb);
+    tile_of(job, ord, ta, tb);
     const int64_t a0 = d.box_lo[0] + static_cast<int64_t>(ta) * 128;
     const int64_t b0 = d.box_lo[1] + static_cast<int64_t>(tb) * TB;
     const uint8_t *sp = stage0 + st * KTmaTileBytes;
@@ -936,6 +1000,9 @@ __global__ void __launch_bounds__(256, 3) k_tma_s8(const __grid_constant__ CUten
       w[j] = *reinterpret_cast<const uint32_t *>(sp + (j * 8 + c) * 128 + ((((4 * ag) >> 4) ^ c) << 4) +
                                                  ((4 * ag) & 15)) ^
              0x80808080u;
+    __syncwarp();
+    if ((t & 31) == 0)
+      mbar_arrive(&empty[st]); // this warp is done with the stage
     uint8_t *dp = dst0 + (a0 * Da + b0) * 2 + static_cast<int64_t>(4 * ag) * DaB + c * 16;
 #pragma unroll
     for (int i = 0; i < 4; ++i, dp += DaB) {
@@ -1140,6 +1207,17 @@ bool tma_enabled() {
     return !(v && v[0] == '0');
   }();
   return on;
+}
+
+/// log2 of the column-block group of k_tma_s8's job order (SYM_B200_TMA_GROUP,
+/// 0..6; default 3).
+uint32_t tma_group_log2() {
+  static const uint32_t lg = [] {
+    const char *v = std::getenv("SYM_B200_TMA_GROUP");
+    const int x = v ? std::atoi(v) : 3;
+    return static_cast<uint32_t>(x < 0 ? 0 : x > 6 ? 6 : x);
+  }();
+  return lg;
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
@@ -1357,13 +1435,17 @@ int sbc_relocate_transpose(const sbc_relocate *desc, void *stream) {
       const int64_t tiles_b = ext_b / 64, tiles = (ext_a / 128) * tiles_b;
       const int64_t cap = static_cast<int64_t>(sm_count()) * 3;
       const unsigned blocks = static_cast<unsigned>(tiles < cap ? tiles : cap);
-      const FastDiv div_b = make_fastdiv(static_cast<uint32_t>(tiles_b));
+      TileOrder ord;
+      ord.lg = tma_group_log2();
+      while (ord.lg > 0 && (ext_a / 128) % (int64_t(1) << ord.lg))
+        --ord.lg;
+      ord.group = make_fastdiv(static_cast<uint32_t>(tiles_b << ord.lg));
       const size_t smem = KStages * KTmaTileBytes + 1024;
       cudaStream_t st = static_cast<cudaStream_t>(stream);
       const uint32_t nt = static_cast<uint32_t>(tiles);
 #define SBC_TMA(CH_, ON_)                                                                                      \
   (cudaFuncSetAttribute(k_tma_s8<CH_, ON_>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)),     \
-   k_tma_s8<CH_, ON_><<<blocks, 256, smem, st>>>(map, d, div_b, nt))
+   k_tma_s8<CH_, ON_><<<blocks, KTmaThreads, smem, st>>>(map, d, ord, nt))
       if (chain == CH_DQ_F16)
         ch_on == 0 ? SBC_TMA(CH_DQ_F16, 0) : ch_on == 1 ? SBC_TMA(CH_DQ_F16, 1) : SBC_TMA(CH_DQ_F16, 2);
       else
