@@ -256,59 +256,207 @@ __global__ void __launch_bounds__(256) k_generic(const __grid_constant__ sbc_rel
 }
 
 // ---------------------------------------------------------------------------
-// Contiguous runs: rank 1, unit strides. 16-byte vector loads and stores on
-// the valid, aligned body; scalar head/tail and pad cells.
+// Contiguous runs: rank 1, unit strides, on the valid 16-byte aligned body
+// (scalar head/tail and pad cells go to the generic kernel).
+//
+// Work is cut into units of U = 16 / max(WS, WD) elements: one 16-byte vector
+// on the wider side and 16 / R bytes on the narrower one (R = wider / narrower
+// width). A warp takes 32 * R consecutive units and lane l handles units
+// k * 32 + l (k < R), so every load and every store instruction of the warp
+// covers one contiguous span (512 bytes on the wide side): each instruction
+// is fully coalesced, and a thread keeps R independent loads in flight.
 // ---------------------------------------------------------------------------
 
+template <int BYTES> struct Bytes;
+template <> struct Bytes<4> { using T = uint32_t; };
+template <> struct Bytes<8> { using T = uint2; };
+template <> struct Bytes<16> { using T = uint4; };
+
 template <int WS, int WD>
-struct Vec {
+struct Units {
+  static constexpr int MAXW = WS > WD ? WS : WD;
   static constexpr int MINW = WS < WD ? WS : WD;
-  static constexpr int V = 16 / MINW;                // elements per thread-step
-  static constexpr int LOADS = (V * WS) / 16;        // 16-byte loads
-  static constexpr int STORES = (V * WD) / 16;       // 16-byte stores
+  static constexpr int R = MAXW / MINW; // units per lane per warp block
+  static constexpr int U = 16 / MAXW;   // elements per unit
 };
 
 template <int WS, int WD, int CHAIN>
 __global__ void __launch_bounds__(256) k_contiguous(const __grid_constant__ sbc_relocate d, int64_t vbegin,
-                                                     int64_t nvec) {
+                                                     int64_t nunits) {
   using S = typename Word<WS>::T;
   using D = typename Word<WD>::T;
-  constexpr int V = Vec<WS, WD>::V;
-  const S *src = static_cast<const S *>(d.src);
-  D *dst = static_cast<D *>(d.dst);
+  constexpr int R = Units<WS, WD>::R, U = Units<WS, WD>::U;
+  using SU = typename Bytes<U * WS>::T;
+  using DU = typename Bytes<U * WD>::T;
   const int64_t lo = d.pad_lo[0];
-  for (int64_t g = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; g < nvec;
-       g += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t c0 = vbegin + g * V; // padded coordinate of the first element
-    const int64_t s0 = c0 - lo - d.src_offset;
-    const int64_t d0 = c0 - d.dst_offset;
+  // body start (16-byte aligned on both sides), viewed as arrays of units
+  const SU *src = reinterpret_cast<const SU *>(static_cast<const S *>(d.src) + (vbegin - lo - d.src_offset));
+  DU *dst = reinterpret_cast<DU *>(static_cast<D *>(d.dst) + (vbegin - d.dst_offset));
+  // One parameter for every element (per-tensor scale): read it once per
+  // thread instead of resolving a channel per element.
+  constexpr bool kParam = CHAIN == CH_Q || CHAIN == CH_DQ || CHAIN == CH_DQ_F16 || CHAIN == CH_DQ_BF16;
+  const bool uniform = kParam && d.stages[0].channel == SBC_CH_NONE && d.stages[0].channel_length >= 1;
+  float p0 = 0.0f;
+  int32_t zp0 = 0;
+  if (uniform) {
+    p0 = d.stages[0].param[0];
+    zp0 = zp_of(d.stages[0], 0);
+  }
+  const int lane = threadIdx.x & 31;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  for (int64_t w = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5; w * 32 * R < nunits;
+       w += nwarps) {
     union {
-      uint4 q[Vec<WS, WD>::LOADS];
-      S e[V];
-    } in;
+      SU q;
+      S e[U];
+    } in[R];
+#pragma unroll
+    for (int k = 0; k < R; ++k) {
+      const int64_t u = (w * R + k) * 32 + lane;
+      if (u < nunits)
+        in[k].q = __ldcs(src + u); // streamed once: evict-first
+    }
+#pragma unroll
+    for (int k = 0; k < R; ++k) {
+      const int64_t u = (w * R + k) * 32 + lane;
+      if (u >= nunits)
+        continue;
+      union {
+        DU q;
+        D e[U];
+      } out;
+      bool ok = true;
+      if (uniform) {
+#pragma unroll
+        for (int i = 0; i < U; ++i) {
+          uint32_t v = static_cast<uint32_t>(in[k].e[i]);
+          if constexpr (CHAIN == CH_Q) {
+            v = quantize(v, p0);
+          } else if constexpr (kParam) {
+            v = dequantize(v, zp0, p0);
+            if constexpr (CHAIN == CH_DQ_F16)
+              v = narrow_f16(v);
+            if constexpr (CHAIN == CH_DQ_BF16)
+              v = narrow_bf16(v);
+          }
+          out.e[i] = static_cast<D>(v);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < U; ++i) {
+          int64_t c = vbegin + u * U + i; // padded coordinate
+          uint32_t v = static_cast<uint32_t>(in[k].e[i]);
+          ok &= run_chain<CHAIN, 1>(d, v, &c, c);
+          out.e[i] = static_cast<D>(v);
+        }
+      }
+      if (!ok) {
+        flag(d);
+        continue;
+      }
+      __stcs(dst + u, out.q);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Narrow transposes: the destination-contiguous axis B has NB (2..4) padded
+// cells and the destination is dense over (A, B) -- NCHW -> NHWC with three
+// channels padded to four is the case. Each thread takes VA = 16 / WS
+// consecutive cells of the source-contiguous axis A, reads one 16-byte vector
+// from each of the NB source planes (valid B cells; pad cells take the fill),
+// and writes its VA x NB destination cells as one contiguous run. A warp
+// reads 512 contiguous bytes per plane and writes 32 * VA * NB * WD
+// contiguous bytes: both sides coalesce without shared memory.
+// Parameter stages are supported only with one parameter for every element.
+// ---------------------------------------------------------------------------
+
+/// Division by a runtime divisor d for numerators below 2^31:
+/// n / d == (n * m) >> s with s = 31 + ceil(log2 d), m = ceil(2^s / d)
+/// (exact because n * (m * d - 2^s) < 2^31 * d <= 2^s).
+struct FastDiv {
+  unsigned long long m;
+  uint32_t s, d;
+};
+
+__device__ __forceinline__ uint32_t fdiv(uint32_t n, const FastDiv &f) {
+  return static_cast<uint32_t>((static_cast<unsigned long long>(n) * f.m) >> f.s);
+}
+
+template <int BYTES> struct StoreVec { using T = uint4; };
+template <> struct StoreVec<8> { using T = uint2; };
+template <> struct StoreVec<4> { using T = uint32_t; };
+
+template <int WS, int WD, int CHAIN, int NB>
+__global__ void __launch_bounds__(256) k_narrow(const __grid_constant__ sbc_relocate d, FastDiv per_batch,
+                                                 uint32_t total) {
+  using S = typename Word<WS>::T;
+  using D = typename Word<WD>::T;
+  constexpr int VA = 16 / WS;
+  constexpr int RUN = VA * NB * WD; // bytes a thread writes
+  constexpr int SV = RUN % 16 == 0 ? 16 : RUN % 8 == 0 ? 8 : 4;
+  using ST = typename StoreVec<SV>::T;
+  const int ax_a = d.rank - 2, ax_b = d.rank - 1;
+  const int64_t Sb = d.src_strides[ax_b];
+  const int64_t lo_b = d.pad_lo[ax_b], hi_b = d.pad_lo[ax_b] + d.extents[ax_b];
+  const int64_t b0 = d.box_lo[ax_b];
+  const S *src = static_cast<const S *>(d.src);
+  uint8_t *dst = static_cast<uint8_t *>(d.dst);
+  const sbc_stage &s = d.stages[0];
+  float p0 = 0.0f;
+  int32_t zp0 = 0;
+  if constexpr (CHAIN == CH_Q || CHAIN == CH_DQ) {
+    p0 = s.param[0];
+    zp0 = zp_of(s, 0);
+  }
+  for (uint32_t g = blockIdx.x * blockDim.x + threadIdx.x; g < total; g += gridDim.x * blockDim.x) {
+    const uint32_t n = d.rank == 3 ? fdiv(g, per_batch) : 0; // total < 2^31 (host-checked)
+    const int64_t a = d.box_lo[ax_a] + static_cast<int64_t>(g - n * per_batch.d) * VA;
+    int64_t sbase = (a - d.pad_lo[ax_a]) - d.src_offset;
+    int64_t dbase = a * d.dst_strides[ax_a] + b0 - d.dst_offset;
+    if (d.rank == 3) {
+      sbase += (d.box_lo[0] + n - d.pad_lo[0]) * d.src_strides[0];
+      dbase += (d.box_lo[0] + n) * d.dst_strides[0];
+    }
     union {
-      uint4 q[Vec<WS, WD>::STORES];
-      D e[V];
+      ST q[RUN / SV];
+      D e[VA * NB];
     } out;
-    const uint4 *sp = reinterpret_cast<const uint4 *>(src + s0);
 #pragma unroll
-    for (int i = 0; i < Vec<WS, WD>::LOADS; ++i)
-      in.q[i] = __ldcs(sp + i); // streamed once: evict-first
-    bool ok = true;
+    for (int j = 0; j < NB; ++j) {
+      const int64_t b = b0 + j;
+      if (b >= lo_b && b < hi_b) {
+        union {
+          uint4 q;
+          S e[VA];
+        } in;
+        in.q = __ldcs(reinterpret_cast<const uint4 *>(src + sbase + (b - lo_b) * Sb));
 #pragma unroll
-    for (int i = 0; i < V; ++i) {
-      int64_t c = c0 + i;
-      uint32_t v = static_cast<uint32_t>(in.e[i]);
-      ok &= run_chain<CHAIN, 1>(d, v, &c, c);
-      out.e[i] = static_cast<D>(v);
+        for (int i = 0; i < VA; ++i) {
+          uint32_t v = static_cast<uint32_t>(in.e[i]);
+          if constexpr (CHAIN == CH_F16)
+            v = narrow_f16(v);
+          else if constexpr (CHAIN == CH_BF16)
+            v = narrow_bf16(v);
+          else if constexpr (CHAIN == CH_W16)
+            v = widen_f16(v);
+          else if constexpr (CHAIN == CH_WB16)
+            v = widen_bf16(v);
+          else if constexpr (CHAIN == CH_Q)
+            v = quantize(v, p0);
+          else if constexpr (CHAIN == CH_DQ)
+            v = dequantize(v, zp0, p0);
+          out.e[i * NB + j] = static_cast<D>(v);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < VA; ++i)
+          out.e[i * NB + j] = static_cast<D>(d.fill_bits);
+      }
     }
-    if (!ok) {
-      flag(d);
-      continue;
-    }
-    uint4 *dp = reinterpret_cast<uint4 *>(dst + d0);
+    ST *dp = reinterpret_cast<ST *>(dst + dbase * WD);
 #pragma unroll
-    for (int i = 0; i < Vec<WS, WD>::STORES; ++i)
+    for (int i = 0; i < RUN / SV; ++i)
       __stcs(dp + i, out.q[i]);
   }
 }
@@ -584,18 +732,6 @@ __global__ void __launch_bounds__(256) k_tile(const __grid_constant__ sbc_reloca
 // per tile.
 // ---------------------------------------------------------------------------
 
-/// Division by a runtime divisor d for numerators below 2^31:
-/// n / d == (n * m) >> s with s = 31 + ceil(log2 d), m = ceil(2^s / d)
-/// (exact because n * (m * d - 2^s) < 2^31 * d <= 2^s).
-struct FastDiv {
-  unsigned long long m;
-  uint32_t s, d;
-};
-
-__device__ __forceinline__ uint32_t fdiv(uint32_t n, const FastDiv &f) {
-  return static_cast<uint32_t>((static_cast<unsigned long long>(n) * f.m) >> f.s);
-}
-
 template <int WD, int CHAIN, int CH_ON>
 __global__ void __launch_bounds__(256, 4) k_tile_s8(const __grid_constant__ sbc_relocate d, FastDiv div_b,
                                                     FastDiv div_t, uint32_t total) {
@@ -751,13 +887,15 @@ __global__ void __launch_bounds__(256, 4) k_tile_s8(const __grid_constant__ sbc_
 }
 
 // ---------------------------------------------------------------------------
-// TMA-pipelined int8 tile transpose (dequantize -> f16/bf16), sm_100a.
+// TMA-pipelined tile transposes, sm_100a: int8 -> f16/bf16 dequantize (the
+// weight-fetch kernel) and 32-bit copies or f32 -> f16/bf16 casts.
 //
-// The source box is viewed by a 3-D tensor map (x = A bytes, y = group of 8
-// source rows, z = row within the group; strides 8*Sb and Sb), so one
-// 128 x 8 x 8 box lands source row 8c+j at shared slot 8j+c. With the 128-byte
-// swizzle (16-byte chunk index XOR slot mod 8) the store phase -- thread
-// (ag, c) reads rows 8c..8c+7 at byte column 4*ag -- hits 32 distinct banks.
+// The source box is viewed by a 3-D tensor map (x = A cells, 128 bytes per
+// box; y = group of 8 source rows, z = row within the group; strides 8*Sb and
+// Sb), so one box of 128 bytes x 8 x 8 lands source row 8c+j at shared slot
+// 8j+c. With the 128-byte swizzle (16-byte chunk index XOR slot mod 8) the
+// store phase -- thread (ag, c) reads rows 8c..8c+7 at byte column 4*ag (four
+// int8 cells or one 32-bit cell) -- hits 32 distinct banks.
 //
 // Warp roles: warps 0-7 convert and store, warp 8 produces. The producer keeps
 // KStages tiles in flight in a ring of shared-memory stages, each with a
@@ -800,7 +938,7 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
                : "memory");
 }
 
-/// Job order of k_tma_s8. Jobs walk groups of 2^lg source-column blocks (of
+/// Job order of k_tma_tile. Jobs walk groups of 2^lg source-column blocks (of
 /// 128 bytes); inside a group the column block varies fastest, so the tiles
 /// in flight at once read 2^lg * 128 contiguous bytes of each source row
 /// while their outputs still cover whole runs of destination rows.
@@ -849,11 +987,24 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, i
                : "memory");
 }
 
-template <int CHAIN, int CH_ON>
-__global__ void __launch_bounds__(KTmaThreads, 3) k_tma_s8(const __grid_constant__ CUtensorMap tmap,
-                                                           const __grid_constant__ sbc_relocate d, TileOrder ord,
-                                                           uint32_t tiles) {
+/// WS = 1: int8 source, CHAIN CH_DQ_F16 / CH_DQ_BF16 (f16/bf16 result), tiles
+/// of 128 A x 64 B cells. WS = 4: 32-bit source, CHAIN CH_COPY (32-bit
+/// result) or CH_F16 / CH_BF16, CH_ON = 0, tiles of 32 A x 64 B cells. Both
+/// move one 8 KB box per tile through the same shared-memory layout.
+template <int WS, int CHAIN, int CH_ON>
+__global__ void __launch_bounds__(KTmaThreads, 3) k_tma_tile(const __grid_constant__ CUtensorMap tmap,
+                                                             const __grid_constant__ sbc_relocate d, TileOrder ord,
+                                                             uint32_t tiles) {
   constexpr int TB = 64, VD = 8;
+  constexpr int TA = 128 / WS;                     // A cells per tile
+  constexpr int WD = CHAIN == CH_COPY ? WS : 2;    // result bytes per cell
+  // Rows per group of the tensor-map view (source row GR*y + z lands at slot
+  // z * (64 / GR) + y). 32-bit copies use groups of 4: thread c then reads
+  // rows 4c..4c+3 and 32+4c..32+4c+3 (slots 16j + c and 16j + 8 + c, still 8
+  // distinct swizzle phases) and its two 16-byte stores each join the other
+  // threads of its row in one contiguous 128-byte segment.
+  constexpr int GR = (WS == 4 && CHAIN == CH_COPY) ? 4 : 8;
+  static_assert(WS == 1 || CH_ON == 0, "32-bit tiles carry no parameters");
   extern __shared__ __align__(1024) uint8_t dyn[];
   __shared__ __align__(8) uint64_t full[KStages], empty[KStages];
   // Per-column dequantize parameters of the tile in each stage (CH_ON == 2).
@@ -944,8 +1095,8 @@ __global__ void __launch_bounds__(KTmaThreads, 3) k_tma_s8(const __grid_constant
         uint32_t ta, tb;
         tile_of(job, ord, ta, tb);
         mbar_expect_tx(&full[st], KTmaTileBytes); // lane 0's arrival
-        tma_load_3d(stage0 + st * KTmaTileBytes, &tmap, static_cast<int32_t>(ta * 128), static_cast<int32_t>(tb * 8),
-                    0, &full[st]);
+        tma_load_3d(stage0 + st * KTmaTileBytes, &tmap, static_cast<int32_t>(ta * TA),
+                    static_cast<int32_t>(tb * (TB / GR)), 0, &full[st]);
       } else {
         mbar_arrive(&full[st]);
       }
@@ -956,10 +1107,10 @@ __global__ void __launch_bounds__(KTmaThreads, 3) k_tma_s8(const __grid_constant
 
   // ---- consumer warps
   const int ag = t >> 3, c = t & 7;
-  const int64_t Da = d.dst_strides[0], DaB = Da * 2;
-  uint8_t *const dst0 = static_cast<uint8_t *>(d.dst) - d.dst_offset * 2;
+  const int64_t Da = d.dst_strides[0], DaB = Da * WD;
+  uint8_t *const dst0 = static_cast<uint8_t *>(d.dst) - d.dst_offset * WD;
   float ps[VD], bias[VD];
-  if constexpr (CH_ON == 0) {
+  if constexpr (WS == 1 && CH_ON == 0) {
 #pragma unroll
     for (int j = 0; j < VD; ++j) {
       ps[j] = s.param[0];
@@ -991,18 +1142,49 @@ __global__ void __launch_bounds__(KTmaThreads, 3) k_tma_s8(const __grid_constant
     }
     uint32_t ta, tb;
     tile_of(job, ord, ta, tb);
-    const int64_t a0 = d.box_lo[0] + static_cast<int64_t>(ta) * 128;
+    const int64_t a0 = d.box_lo[0] + static_cast<int64_t>(ta) * TA;
     const int64_t b0 = d.box_lo[1] + static_cast<int64_t>(tb) * TB;
     const uint8_t *sp = stage0 + st * KTmaTileBytes;
     uint32_t w[VD];
 #pragma unroll
-    for (int j = 0; j < VD; ++j)
-      w[j] = *reinterpret_cast<const uint32_t *>(sp + (j * 8 + c) * 128 + ((((4 * ag) >> 4) ^ c) << 4) +
-                                                 ((4 * ag) & 15)) ^
-             0x80808080u;
+    for (int j = 0; j < VD; ++j) {
+      // GR == 8: word j = source row 8c + j; GR == 4: rows 4c + j (j < 4), 32 + 4c + (j - 4)
+      const int slot = GR == 8 ? j * 8 + c : (j & 3) * 16 + (j >> 2) * 8 + c;
+      w[j] = *reinterpret_cast<const uint32_t *>(sp + slot * 128 + ((((4 * ag) >> 4) ^ c) << 4) + ((4 * ag) & 15));
+    }
     __syncwarp();
     if ((t & 31) == 0)
       mbar_arrive(&empty[st]); // this warp is done with the stage
+    if constexpr (WS == 4 && GR == 4) {
+      // words 0-3: cells (a0 + ag, b0 + 4c + j); words 4-7: cells b0 + 32 + 4c + j
+      uint4 *dp = reinterpret_cast<uint4 *>(dst0 + (a0 * Da + b0) * WD + static_cast<int64_t>(ag) * DaB + c * 16);
+      __stcs(dp, make_uint4(w[0], w[1], w[2], w[3]));
+      __stcs(dp + 8, make_uint4(w[4], w[5], w[6], w[7]));
+      continue;
+    } else if constexpr (WS == 4) {
+      // cell (a0 + ag, b0 + 8c + j) is word j: one result row segment of 8 cells
+      uint4 out[WD / 2];
+      uint32_t *u = reinterpret_cast<uint32_t *>(out);
+#pragma unroll
+      for (int j = 0; j < VD; ++j) {
+        if constexpr (CHAIN == CH_COPY)
+          u[j] = w[j];
+        else if constexpr (CHAIN == CH_F16)
+          reinterpret_cast<uint16_t *>(u)[j] = static_cast<uint16_t>(narrow_f16(w[j]));
+        else
+          reinterpret_cast<uint16_t *>(u)[j] = static_cast<uint16_t>(narrow_bf16(w[j]));
+      }
+      uint4 *dp = reinterpret_cast<uint4 *>(dst0 + (a0 * Da + b0) * WD + static_cast<int64_t>(ag) * DaB +
+                                            c * VD * WD);
+#pragma unroll
+      for (int h = 0; h < WD / 2; ++h)
+        __stcs(dp + h, out[h]);
+      continue;
+    } else {
+#pragma unroll
+      for (int j = 0; j < VD; ++j)
+        w[j] ^= 0x80808080u;
+    }
     uint8_t *dp = dst0 + (a0 * Da + b0) * 2 + static_cast<int64_t>(4 * ag) * DaB + c * 16;
 #pragma unroll
     for (int i = 0; i < 4; ++i, dp += DaB) {
@@ -1160,12 +1342,13 @@ template <int WS, int WD, int CH> struct GenericLaunch {
 };
 
 template <int WS, int WD, int CH> struct ContiguousLaunch {
-  static int run(const sbc_relocate &d, int64_t vbegin, int64_t nvec, cudaStream_t s) {
+  static int run(const sbc_relocate &d, int64_t vbegin, int64_t nunits, cudaStream_t s) {
     if constexpr (WS == 8 || WD == 8) {
       return SBC_EUNSUPPORTED;
     } else {
-      const int64_t blocks = grid_for(nvec, 256, 8);
-      k_contiguous<WS, WD, CH><<<static_cast<unsigned>(blocks), 256, 0, s>>>(d, vbegin, nvec);
+      constexpr int R = Units<WS, WD>::R;
+      const int64_t blocks = grid_for((nunits + R - 1) / R, 256, 8); // a thread takes R units
+      k_contiguous<WS, WD, CH><<<static_cast<unsigned>(blocks), 256, 0, s>>>(d, vbegin, nunits);
       return launched(cudaSuccess);
     }
   }
@@ -1209,7 +1392,7 @@ bool tma_enabled() {
   return on;
 }
 
-/// log2 of the column-block group of k_tma_s8's job order (SYM_B200_TMA_GROUP,
+/// log2 of the column-block group of k_tma_tile's job order (SYM_B200_TMA_GROUP,
 /// 0..6; default 3).
 uint32_t tma_group_log2() {
   static const uint32_t lg = [] {
@@ -1235,21 +1418,26 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   return fn;
 }
 
-/// The 3-D view of an int8 [rows, cols] box used by k_tma_s8: x = column
-/// bytes, y = group of 8 rows (stride 8*pitch), z = row in group (stride
-/// pitch); box 128 x 8 x 8 with the 128-byte swizzle. False when the driver
-/// rejects the description (the caller then uses k_tile_s8).
-bool encode_rows3d(CUtensorMap *map, const void *base, int64_t cols, int64_t rows, int64_t pitch) {
+/// The 3-D view of a [rows, cols] box of `ws`-byte cells used by k_tma_tile:
+/// x = column (128 bytes of cells per box), y = group of `gr` rows (stride
+/// gr*pitch), z = row in group (stride pitch); box (128 / ws) x (64 / gr) x gr
+/// (64 rows) with the 128-byte swizzle. False when the driver rejects the
+/// description (the caller then uses a SIMT tile kernel).
+bool encode_rows3d(CUtensorMap *map, const void *base, int ws, int64_t cols, int64_t rows, int64_t pitch, int gr) {
   PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
-  if (!enc || reinterpret_cast<uintptr_t>(base) % 16 || pitch % 16 || rows % 8)
+  if (!enc || reinterpret_cast<uintptr_t>(base) % 16 || pitch % 16 || rows % gr || (ws != 1 && ws != 4) ||
+      (gr != 4 && gr != 8))
     return false;
-  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows / 8), 8};
-  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(pitch * 8), static_cast<cuuint64_t>(pitch)};
-  const cuuint32_t box[3] = {128, 8, 8};
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows / gr),
+                              static_cast<cuuint64_t>(gr)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(pitch * gr), static_cast<cuuint64_t>(pitch)};
+  const cuuint32_t box[3] = {static_cast<cuuint32_t>(128 / ws), static_cast<cuuint32_t>(64 / gr),
+                             static_cast<cuuint32_t>(gr)};
   const cuuint32_t estr[3] = {1, 1, 1};
-  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void *>(base), dims, strides, box, estr,
-                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  const CUresult r = enc(map, ws == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT32, 3,
+                         const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
 
@@ -1324,6 +1512,74 @@ bool basic_ok(const sbc_relocate &d) {
   return true;
 }
 
+template <int WS, int WD, int CH>
+int launch_narrow(const sbc_relocate &d, int nb, int64_t per_batch, int64_t total, cudaStream_t s) {
+  const unsigned blocks = static_cast<unsigned>(grid_for(total, 256, 8));
+  const FastDiv pb = make_fastdiv(static_cast<uint32_t>(per_batch));
+  const uint32_t n = static_cast<uint32_t>(total);
+  switch (nb) {
+  case 2: k_narrow<WS, WD, CH, 2><<<blocks, 256, 0, s>>>(d, pb, n); break;
+  case 3: k_narrow<WS, WD, CH, 3><<<blocks, 256, 0, s>>>(d, pb, n); break;
+  default: k_narrow<WS, WD, CH, 4><<<blocks, 256, 0, s>>>(d, pb, n); break;
+  }
+  return launched(cudaSuccess);
+}
+
+/// k_narrow when the box fits it (see the kernel); SBC_EUNSUPPORTED otherwise.
+int try_narrow(const sbc_relocate &d, int chain, cudaStream_t s) {
+  const int ax_a = d.rank - 2, ax_b = d.rank - 1;
+  const int64_t ext_a = d.box_hi[ax_a] - d.box_lo[ax_a], nb = d.box_hi[ax_b] - d.box_lo[ax_b];
+  const int ws = d.src_width, wd = d.dst_width;
+  if (nb < 2 || nb > 4 || ws < 2 || d.dst_strides[ax_a] != nb)
+    return SBC_EUNSUPPORTED;
+  if (chain == CH_Q || chain == CH_DQ) {
+    if (d.stages[0].channel != SBC_CH_NONE || d.stages[0].channel_length < 1)
+      return SBC_EUNSUPPORTED;
+  } else if (chain != CH_COPY && chain != CH_F16 && chain != CH_BF16 && chain != CH_W16 && chain != CH_WB16) {
+    return SBC_EUNSUPPORTED;
+  }
+  const int va = 16 / ws;
+  const int run = va * static_cast<int>(nb) * wd;
+  const int sv = run % 16 == 0 ? 16 : run % 8 == 0 ? 8 : 4;
+  if (ext_a % va || run % 4)
+    return SBC_EUNSUPPORTED;
+  // every A (and batch) cell of the box is a valid source cell
+  for (int k = 0; k <= ax_a; ++k)
+    if (d.box_lo[k] < d.pad_lo[k] || d.box_hi[k] > d.pad_lo[k] + d.extents[k])
+      return SBC_EUNSUPPORTED;
+  int64_t s0 = d.box_lo[ax_a] - d.pad_lo[ax_a] - d.src_offset;
+  int64_t d0 = d.box_lo[ax_a] * nb + d.box_lo[ax_b] - d.dst_offset;
+  if (d.rank == 3) {
+    s0 += (d.box_lo[0] - d.pad_lo[0]) * d.src_strides[0];
+    d0 += d.box_lo[0] * d.dst_strides[0];
+    if ((d.src_strides[0] * ws) % 16 || (d.dst_strides[0] * wd) % sv)
+      return SBC_EUNSUPPORTED;
+  }
+  if ((reinterpret_cast<uintptr_t>(d.src) + s0 * ws) % 16 || (d.src_strides[ax_b] * ws) % 16 ||
+      (reinterpret_cast<uintptr_t>(d.dst) + d0 * wd) % sv)
+    return SBC_EUNSUPPORTED;
+  const int64_t per_batch = ext_a / va;
+  const int64_t total = per_batch * (d.rank == 3 ? d.box_hi[0] - d.box_lo[0] : 1);
+  if (total >= (int64_t(1) << 31) - 256 * 8 * 1024) // 32-bit thread indices, grid stride included
+    return SBC_EUNSUPPORTED;
+  const int n = static_cast<int>(nb);
+  if (chain == CH_COPY && ws == 4 && wd == 4)
+    return launch_narrow<4, 4, CH_COPY>(d, n, per_batch, total, s);
+  if (chain == CH_COPY && ws == 2 && wd == 2)
+    return launch_narrow<2, 2, CH_COPY>(d, n, per_batch, total, s);
+  if (chain == CH_F16 && ws == 4 && wd == 2)
+    return launch_narrow<4, 2, CH_F16>(d, n, per_batch, total, s);
+  if (chain == CH_BF16 && ws == 4 && wd == 2)
+    return launch_narrow<4, 2, CH_BF16>(d, n, per_batch, total, s);
+  if (chain == CH_W16 && ws == 2 && wd == 4)
+    return launch_narrow<2, 4, CH_W16>(d, n, per_batch, total, s);
+  if (chain == CH_WB16 && ws == 2 && wd == 4)
+    return launch_narrow<2, 4, CH_WB16>(d, n, per_batch, total, s);
+  if (chain == CH_Q && ws == 4 && wd == 1)
+    return launch_narrow<4, 1, CH_Q>(d, n, per_batch, total, s);
+  return SBC_EUNSUPPORTED;
+}
+
 int64_t box_count(const sbc_relocate &d) {
   int64_t n = 1;
   for (int k = 0; k < d.rank; ++k)
@@ -1362,14 +1618,14 @@ int sbc_relocate_contiguous(const sbc_relocate *desc, void *stream) {
   const int ws = d.src_width, wd = d.dst_width;
   if (ws == 8 || wd == 8)
     return SBC_EUNSUPPORTED;
-  const int minw = ws < wd ? ws : wd;
-  const int V = 16 / minw;
-  // Valid part of the box, then its 16-byte aligned vector body.
+  const int minw = ws < wd ? ws : wd, maxw = ws < wd ? wd : ws;
+  const int V = 16 / minw, U = 16 / maxw; // alignment period; elements per kernel unit
+  // Valid part of the box, then its 16-byte aligned body of whole units.
   const int64_t lo = d.box_lo[0], hi = d.box_hi[0];
   const int64_t v0 = lo > d.pad_lo[0] ? lo : d.pad_lo[0];
   const int64_t vend = d.pad_lo[0] + d.extents[0];
   const int64_t v1 = hi < vend ? hi : vend;
-  int64_t body0 = v0, nvec = 0;
+  int64_t body0 = v0, nunits = 0;
   if (v1 > v0) {
     const uintptr_t sa = reinterpret_cast<uintptr_t>(d.src) + (v0 - d.pad_lo[0] - d.src_offset) * ws;
     const uintptr_t da = reinterpret_cast<uintptr_t>(d.dst) + (v0 - d.dst_offset) * wd;
@@ -1382,7 +1638,7 @@ int sbc_relocate_contiguous(const sbc_relocate *desc, void *stream) {
       }
     if (skip >= 0) {
       body0 = v0 + skip;
-      nvec = (v1 - body0) / V;
+      nunits = (v1 - body0) / U;
     }
   }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -1395,14 +1651,14 @@ int sbc_relocate_contiguous(const sbc_relocate *desc, void *stream) {
     part.box_hi[0] = b;
     return sbc_relocate_generic(&part, stream);
   };
-  if (nvec == 0)
+  if (nunits == 0)
     return generic_range(lo, hi);
-  int rc = dispatch<ContiguousLaunch>(ws, wd, chain, d, body0, nvec, s);
+  int rc = dispatch<ContiguousLaunch>(ws, wd, chain, d, body0, nunits, s);
   if (rc)
     return rc;
   if ((rc = generic_range(lo, body0)))
     return rc;
-  return generic_range(body0 + nvec * V, hi);
+  return generic_range(body0 + nunits * U, hi);
 }
 
 int sbc_relocate_transpose(const sbc_relocate *desc, void *stream) {
@@ -1423,33 +1679,47 @@ int sbc_relocate_transpose(const sbc_relocate *desc, void *stream) {
   const int64_t nbatch = d.rank == 3 ? d.box_hi[0] - d.box_lo[0] : 1;
   if (ext_a == 0 || ext_b == 0 || nbatch == 0)
     return 0;
+  if (ext_b <= 4) {
+    const int rc = try_narrow(d, chain, static_cast<cudaStream_t>(stream));
+    if (rc != SBC_EUNSUPPORTED)
+      return rc;
+  }
   const int ch_on = tile_eligible(d);
   const bool dq = chain == CH_DQ || chain == CH_DQ_F16 || chain == CH_DQ_BF16;
-  if (ch_on >= 0 && d.rank == 2 && d.src_width == 1 && d.dst_width == 2 &&
-      (chain == CH_DQ_F16 || chain == CH_DQ_BF16) && ext_a % 128 == 0 && ext_b % 64 == 0 &&
-      (ext_a / 128) * (ext_b / 64) < (int64_t(1) << 31) && tma_enabled()) {
+  // TMA tiles: int8 -> f16/bf16 dequantize, or 32-bit copy / narrowing cast
+  const bool tma_s8 = d.src_width == 1 && d.dst_width == 2 && (chain == CH_DQ_F16 || chain == CH_DQ_BF16);
+  const bool tma_32 = d.src_width == 4 && ch_on == 0 &&
+                      ((chain == CH_COPY && d.dst_width == 4) ||
+                       ((chain == CH_F16 || chain == CH_BF16) && d.dst_width == 2));
+  const int64_t tma_ta = 128 / d.src_width;
+  if (ch_on >= 0 && d.rank == 2 && (tma_s8 || tma_32) && ext_a % tma_ta == 0 && ext_b % 64 == 0 &&
+      (ext_a / tma_ta) * (ext_b / 64) < (int64_t(1) << 31) && tma_enabled()) {
     CUtensorMap map;
-    const uint8_t *base = static_cast<const uint8_t *>(d.src) + d.box_lo[0] + d.box_lo[1] * d.src_strides[1] -
-                          d.src_offset;
-    if (encode_rows3d(&map, base, ext_a, ext_b, d.src_strides[1])) {
-      const int64_t tiles_b = ext_b / 64, tiles = (ext_a / 128) * tiles_b;
+    const uint8_t *base = static_cast<const uint8_t *>(d.src) +
+                          (d.box_lo[0] + d.box_lo[1] * d.src_strides[1] - d.src_offset) * d.src_width;
+    const int group = tma_32 && chain == CH_COPY ? 4 : 8; // rows per view group, as the kernel's GR
+    if (encode_rows3d(&map, base, d.src_width, ext_a, ext_b, d.src_strides[1] * d.src_width, group)) {
+      const int64_t tiles_b = ext_b / 64, tiles = (ext_a / tma_ta) * tiles_b;
       const int64_t cap = static_cast<int64_t>(sm_count()) * 3;
       const unsigned blocks = static_cast<unsigned>(tiles < cap ? tiles : cap);
       TileOrder ord;
       ord.lg = tma_group_log2();
-      while (ord.lg > 0 && (ext_a / 128) % (int64_t(1) << ord.lg))
+      while (ord.lg > 0 && (ext_a / tma_ta) % (int64_t(1) << ord.lg))
         --ord.lg;
       ord.group = make_fastdiv(static_cast<uint32_t>(tiles_b << ord.lg));
       const size_t smem = KStages * KTmaTileBytes + 1024;
       cudaStream_t st = static_cast<cudaStream_t>(stream);
       const uint32_t nt = static_cast<uint32_t>(tiles);
-#define SBC_TMA(CH_, ON_)                                                                                      \
-  (cudaFuncSetAttribute(k_tma_s8<CH_, ON_>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)),     \
-   k_tma_s8<CH_, ON_><<<blocks, KTmaThreads, smem, st>>>(map, d, ord, nt))
-      if (chain == CH_DQ_F16)
-        ch_on == 0 ? SBC_TMA(CH_DQ_F16, 0) : ch_on == 1 ? SBC_TMA(CH_DQ_F16, 1) : SBC_TMA(CH_DQ_F16, 2);
+#define SBC_TMA(WS_, CH_, ON_)                                                                                 \
+  (cudaFuncSetAttribute(k_tma_tile<WS_, CH_, ON_>, cudaFuncAttributeMaxDynamicSharedMemorySize,                    \
+                        static_cast<int>(smem)),                                                                 \
+   k_tma_tile<WS_, CH_, ON_><<<blocks, KTmaThreads, smem, st>>>(map, d, ord, nt))
+      if (tma_32)
+        chain == CH_COPY ? SBC_TMA(4, CH_COPY, 0) : chain == CH_F16 ? SBC_TMA(4, CH_F16, 0) : SBC_TMA(4, CH_BF16, 0);
+      else if (chain == CH_DQ_F16)
+        ch_on == 0 ? SBC_TMA(1, CH_DQ_F16, 0) : ch_on == 1 ? SBC_TMA(1, CH_DQ_F16, 1) : SBC_TMA(1, CH_DQ_F16, 2);
       else
-        ch_on == 0 ? SBC_TMA(CH_DQ_BF16, 0) : ch_on == 1 ? SBC_TMA(CH_DQ_BF16, 1) : SBC_TMA(CH_DQ_BF16, 2);
+        ch_on == 0 ? SBC_TMA(1, CH_DQ_BF16, 0) : ch_on == 1 ? SBC_TMA(1, CH_DQ_BF16, 1) : SBC_TMA(1, CH_DQ_BF16, 2);
 #undef SBC_TMA
       return launched(cudaSuccess);
     }

@@ -78,6 +78,82 @@ def test_c2_nchw_to_nhwc_pad_f16(shape, route):
     assert rep["device_kernel"] == "transpose"
 
 
+def _channels_last(batch, channels, hw, pad, op):
+    """NCHW f32 -> NHWC with `pad` fill channels after the value op: the
+    narrow-transpose family (C2 and its neighbours)."""
+    from sym_b200.reloc_torch import recipe as R
+    from sym_b200.reloc_torch import symbolic as S
+
+    shape = tuple(S.Const(x) for x in (batch, channels, hw, 1))
+    src = R.TensorSpec(shape, S.dense_strides(shape), S.Const(0), "float32")
+    result_dtype = {"copy": "float32", "f16": "float16", "bf16": "bfloat16", "quantize": "int8"}[op]
+    ops = [R.Transpose((0, 2, 3, 1))]
+    if op in ("f16", "bf16"):
+        ops.append(R.Cast(result_dtype, "ieee_rne"))
+    elif op == "quantize":
+        ops.append(R.Quantize("int8", R.InlineParam("float32", (), (0x3D4CCCCD,)), None, None, "symmetric_rne"))
+    if pad:
+        ops.append(R.Pad(3, S.Const(0), S.Const(pad), R.Fill(result_dtype, 0)))
+    out = tuple(S.Const(x) for x in (batch, hw, 1, channels + pad))
+    return R.Recipe(src, tuple(ops), R.TensorSpec(out, S.dense_strides(out), S.Const(0), result_dtype), "h2d")
+
+
+@pytest.mark.parametrize("channels,pad", [(3, 1), (2, 0), (3, 0), (4, 0), (2, 2), (1, 1)])
+@pytest.mark.parametrize("op", ["copy", "f16", "bf16", "quantize"])
+@pytest.mark.parametrize("hw", [4096, 4093])
+def test_narrow_channels_last(channels, pad, op, hw):
+    """Every narrow variant (2-4 destination channels, with and without pad
+    channels, copy / casts / per-tensor quantize) and a pixel count that is
+    not a multiple of the vector width (the tiled fallback) stay
+    bit-identical to the reference."""
+    blob = encode(_channels_last(3, channels, hw, pad, op))
+    x = _specials_f32(np.random.default_rng(5), 3 * channels * hw)
+    for route in ("dma_ring", "zero_copy"):
+        if op == "copy":  # no value stage: the encoder emits a layout-only (wire v0) plan
+            from layout_gpu import expected_layout, run_layout_gpu
+
+            out = run_layout_gpu(blob, {}, x, route=route)
+            assert np.array_equal(out, expected_layout(blob, {}, x)), route
+            continue
+        out, rep = run_typed_gpu(blob, {}, {}, x, route=route)
+        assert np.array_equal(out, expected(blob, {}, {}, x)), route
+
+
+def _transpose_2d(rows, cols, op):
+    """f32 [rows, cols] -> [cols, rows], optionally narrowed after the transpose."""
+    from sym_b200.reloc_torch import recipe as R
+    from sym_b200.reloc_torch import symbolic as S
+
+    shape = (S.Const(rows), S.Const(cols))
+    src = R.TensorSpec(shape, S.dense_strides(shape), S.Const(0), "float32")
+    result_dtype = {"copy": "float32", "f16": "float16", "bf16": "bfloat16"}[op]
+    ops = [R.Transpose((1, 0))]
+    if op != "copy":
+        ops.append(R.Cast(result_dtype, "ieee_rne"))
+    out = (S.Const(cols), S.Const(rows))
+    return R.Recipe(src, tuple(ops), R.TensorSpec(out, S.dense_strides(out), S.Const(0), result_dtype), "h2d")
+
+
+@pytest.mark.parametrize("rows,cols", [(64, 32), (128, 96), (1024, 640), (4096, 4096), (200, 96), (64, 33)])
+@pytest.mark.parametrize("op", ["copy", "f16", "bf16"])
+def test_f32_transposes(rows, cols, op):
+    """32-bit tile transposes (TMA tiles of 32 x 64 cells where the extents
+    allow, the SIMT tiles elsewhere, ring chunks of whole rows) against the
+    reference."""
+    blob = encode(_transpose_2d(rows, cols, op))
+    x = _specials_f32(np.random.default_rng(6), rows * cols)
+    for route, chunk in (("dma_ring", 0), ("dma_ring", 64 << 10), ("zero_copy", 0)):
+        if op == "copy":  # layout-only plan (wire v0)
+            from layout_gpu import expected_layout, run_layout_gpu
+
+            out = run_layout_gpu(blob, {}, x, route=route, chunk_size=chunk)
+            assert np.array_equal(out, expected_layout(blob, {}, x)), (route, chunk)
+            continue
+        out, rep = run_typed_gpu(blob, {}, {}, x, route=route, chunk_size=chunk)
+        assert np.array_equal(out, expected(blob, {}, {}, x)), (route, chunk)
+        assert rep["device_kernel"] == "transpose"
+
+
 @pytest.mark.parametrize("seq", [1, 3, 128])
 @pytest.mark.parametrize("route", ROUTES)
 def test_c3_quantize_dequantize(seq, route):
