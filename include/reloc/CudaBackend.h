@@ -75,6 +75,9 @@ public:
   uint64_t eventWaits = 0;
   uint64_t callerWaits = 0;
   uint64_t kernelLaunches = 0;
+  /// Set while a group runs: its members share one status word, cleared once
+  /// before the first member instead of once per execution.
+  bool keepStatus = false;
 
   /// Measured route choice per plan class: key -> seconds per byte of each
   /// route (negative = not yet measured).

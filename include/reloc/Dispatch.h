@@ -154,6 +154,42 @@ std::optional<TransferError> executeWindow(const DispatchTemplate &tmpl, CudaBac
                                            bool hostSource, void *dst, int64_t rowBegin, int64_t rowEnd,
                                            const TransferOptions &options, Report &report);
 
+/// Explicit consumer-sized group (reference Dispatch.h:177-214,
+/// prepareDispatchGroup :213): fresh views per member, one CUDA device, one
+/// caller-stream ordering and one completion for all members. Typed
+/// templates and layout plans (through their transfer template) mix freely.
+struct GroupEntry {
+  const DispatchTemplate *plan = nullptr; // read during preparation only
+  BufferView source, destination;
+  TransferDirection direction = TransferDirection::HostToDevice;
+};
+struct GroupReport {
+  uint64_t payloadCopyCalls = 0, parameterUploads = 0, parameterReuses = 0;
+  uint64_t parameterUploadBytes = 0, hostTransformBytes = 0;
+  uint64_t packingBytes = 0; // payloads are never packed together
+  uint64_t kernelLaunches = 0, outputBytes = 0;
+  uint64_t copyCalls = 0, eventRecords = 0, eventWaits = 0, callerWaits = 0;
+  size_t scratchPeakBytes = 0;
+};
+struct GroupRequest {
+  std::vector<DispatchRequest> items;
+  std::vector<Report> reports;
+  GroupReport report;
+  int device = -1;
+  bool consumed = false, executing = false, failed = false;
+};
+/// Validate the whole group before anything is allocated or launched: 1 to
+/// 256 members, host-to-device only, one destination device, and no
+/// destination overlapping another member's destination or any source.
+std::variant<GroupRequest, TransferError> prepareDispatchGroup(const std::vector<GroupEntry> &entries);
+/// Enqueue every member on `backend` after one wait on the caller stream,
+/// then order the caller stream after all of them. Blocks until the group
+/// completed unless options.asyncCompletion; `completionEvent` (an event of
+/// the sb_cuda layer, or null) is recorded after the last member either way.
+/// Marks the group consumed before launching; never retries a member.
+std::optional<TransferError> executeGroup(GroupRequest &group, CudaBackend &backend, const TransferOptions &options,
+                                          void *completionEvent);
+
 } // namespace dispatch
 } // namespace reloc
 

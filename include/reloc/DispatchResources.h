@@ -19,9 +19,32 @@
 #include <memory>
 #include <mutex>
 #include <optional>
+#include <variant>
 
 namespace reloc {
 namespace dispatch {
+
+/// The pending completion of a submitted group (reference
+/// DispatchResources.h:9-25). It owns one event recorded after the group's
+/// last member. Dropping a handle without wait() still waits (drains).
+class Completion {
+public:
+  struct State;
+  explicit Completion(std::shared_ptr<State> state);
+  ~Completion();
+  Completion(const Completion &) = delete;
+  Completion &operator=(const Completion &) = delete;
+  /// Host wait; then the device fault word is checked. Idempotent.
+  TransferOutcome wait();
+  /// true once complete (and finalized as by wait()), false while pending.
+  std::variant<bool, TransferError> query();
+  /// GPU-side dependency: `consumer` (a cudaStream_t) waits for the group
+  /// without blocking the host.
+  std::optional<TransferError> waitStream(const void *consumer);
+
+private:
+  std::shared_ptr<State> state_;
+};
 
 struct ResourceStats {
   uint64_t requests = 0, hits = 0, contexts = 0;
@@ -43,6 +66,14 @@ public:
   /// Lease the context of `device` and run the request on it.
   TransferOutcome execute(DispatchRequest &request, int device, int streams, const TransferOptions &options,
                           std::shared_ptr<void> owners);
+  /// Run a group on the context of its device and complete it (blocking
+  /// unless options.asyncCompletion, then the caller stream carries it).
+  TransferOutcome execute(GroupRequest &group, const TransferOptions &options, std::shared_ptr<void> owners);
+  /// Enqueue a group and return its completion without waiting (reference
+  /// DispatchResources.h:85-86). Plans with device-checked channel maps still
+  /// complete before returning (their status word is read back).
+  std::variant<std::shared_ptr<Completion>, TransferError> submit(GroupRequest &group, const TransferOptions &options,
+                                                                  std::shared_ptr<void> owners);
   /// Run `fn` with the leased context of `device` (window/device executions).
   TransferOutcome withContext(int device, const std::function<std::optional<TransferError>(CudaBackend &)> &fn);
 

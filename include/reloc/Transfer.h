@@ -74,9 +74,6 @@ struct TransferOptions {
   bool asyncCompletion = false;
 };
 
-/// Byte span addressed by a view (overflow-checked); error on empty,
-/// negative-stride or overlapping views.
-std::optional<TransferError> viewSpanBytes(const BufferView &view, const char *role, size_t &span);
 
 } // namespace reloc
 

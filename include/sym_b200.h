@@ -146,6 +146,48 @@ int sb_execute_rows(const sb_template *tmpl, sb_resources *resources, int32_t de
 int sb_execute_h2d_static(const sb_template *tmpl, const void *source, void *destination, void *stream,
                           sb_error *err);
 
+/* ---- consumer-sized groups and asynchronous completion ------------------- */
+typedef struct sb_group sb_group;           /* a validated single-use group of requests */
+typedef struct sb_completion sb_completion; /* a submitted group's pending completion */
+
+/* One group member: a template (typed, or a layout plan's transfer
+ * template) with fresh source/destination views. direction: 0 h2d. */
+typedef struct {
+  const sb_template *plan;
+  sb_view source;
+  sb_view destination;
+  int32_t direction;
+} sb_group_entry;
+
+/* pyreloc.prepare_dispatch_group (PyDispatch.cpp:645; dispatch::
+ * prepareDispatchGroup, Dispatch.h:213): validate 1..256 members together
+ * (one device, no destination overlapping another destination or any source)
+ * before anything is allocated or launched. */
+int sb_prepare_dispatch_group(const sb_group_entry *entries, size_t count, sb_group **out, sb_error *err);
+/* pyreloc.execute_dispatch_group (PyDispatch.cpp:648): every member after one
+ * wait on the caller stream, one completion for all (blocking unless
+ * options->async_completion). report: the group report JSON. */
+int sb_execute_dispatch_group(sb_group *group, sb_resources *resources, const sb_options *options, char *report,
+                              size_t cap, sb_error *err);
+/* pyreloc.submit_dispatch_group (PyDispatch.cpp:696; Resources::submit,
+ * DispatchResources.h:85): enqueue the group and return its completion
+ * without waiting. resources may be NULL (a private context kept alive by the
+ * completion). Source and destination buffers must stay valid until the
+ * completion reports done. */
+int sb_submit_dispatch_group(sb_group *group, sb_resources *resources, const sb_options *options,
+                             sb_completion **out, sb_error *err);
+/* The group report (totals and one report per member) as JSON. */
+int sb_group_report(const sb_group *group, char *json, size_t cap);
+void sb_group_free(sb_group *group);
+/* DispatchCompletion.wait / query / wait_stream (PyDispatch.cpp:659-692). */
+int sb_completion_wait(sb_completion *completion, sb_error *err);
+/* *done = 1 once complete, 0 while pending. */
+int sb_completion_query(sb_completion *completion, int32_t *done, sb_error *err);
+/* Order `stream` (a cudaStream_t) after the group, without a host wait. */
+int sb_completion_wait_stream(sb_completion *completion, void *stream, sb_error *err);
+/* Releases the handle; waits for the group first if it is still pending. */
+void sb_completion_free(sb_completion *completion);
+
 /* pyreloc.DispatchResources (PyDispatch.cpp:700-801) / dispatch::Resources. */
 int sb_resources_create(uint64_t max_retained_bytes, uint64_t max_live_bytes, uint32_t max_contexts,
                         sb_resources **out, sb_error *err);

@@ -39,6 +39,10 @@ class SbOptions(ctypes.Structure):
     ]
 
 
+class SbGroupEntry(ctypes.Structure):
+    _fields_ = [("plan", ctypes.c_void_p), ("source", SbView), ("destination", SbView), ("direction", ctypes.c_int32)]
+
+
 ROUTES = {"auto": 0, "dma_ring": 1, "zero_copy": 2, "staged": 3}
 
 _lib = None
@@ -88,6 +92,15 @@ def lib():
         "sb_resources_clear": (ctypes.c_int, [vp, ep]),
         "sb_resources_close": (ctypes.c_int, [vp, ep]),
         "sb_resources_free": (None, [vp]),
+        "sb_prepare_dispatch_group": (ctypes.c_int, [ctypes.POINTER(SbGroupEntry), sz, pp, ep]),
+        "sb_execute_dispatch_group": (ctypes.c_int, [vp, vp, ctypes.POINTER(SbOptions), ctypes.c_char_p, sz, ep]),
+        "sb_submit_dispatch_group": (ctypes.c_int, [vp, vp, ctypes.POINTER(SbOptions), pp, ep]),
+        "sb_group_report": (ctypes.c_int, [vp, ctypes.c_char_p, sz]),
+        "sb_group_free": (None, [vp]),
+        "sb_completion_wait": (ctypes.c_int, [vp, ep]),
+        "sb_completion_query": (ctypes.c_int, [vp, ctypes.POINTER(i32), ep]),
+        "sb_completion_wait_stream": (ctypes.c_int, [vp, vp, ep]),
+        "sb_completion_free": (None, [vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)

@@ -47,6 +47,16 @@ struct sb_resources {
   sb_resources(size_t a, size_t b, unsigned c) : res(a, b, c) {}
 };
 
+struct sb_group {
+  dispatch::GroupRequest g;
+};
+
+struct sb_completion {
+  std::shared_ptr<dispatch::Resources> ephemeral; // private context when the caller passed none
+  std::shared_ptr<dispatch::Completion> c;
+  ~sb_completion() { c.reset(); } // drains before the private context goes
+};
+
 namespace {
 
 const char *kVersion = "sym_b200 0.1.0 (libreloc wire v0/v1, sm_100a)";
@@ -614,5 +624,115 @@ int sb_resources_close(sb_resources *r, sb_error *err) {
 }
 
 void sb_resources_free(sb_resources *r) { delete r; }
+
+int sb_prepare_dispatch_group(const sb_group_entry *entries, size_t count, sb_group **out, sb_error *err) {
+  std::vector<dispatch::GroupEntry> es;
+  es.reserve(count);
+  for (size_t i = 0; i < count; ++i) {
+    dispatch::GroupEntry e;
+    e.plan = entries[i].plan ? &entries[i].plan->t : nullptr;
+    e.source = toView(entries[i].source);
+    e.destination = toView(entries[i].destination);
+    e.direction = entries[i].direction == 1 ? TransferDirection::DeviceToHost : TransferDirection::HostToDevice;
+    es.push_back(std::move(e));
+  }
+  auto r = dispatch::prepareDispatchGroup(es);
+  if (auto *e = std::get_if<TransferError>(&r))
+    return setErr(err, e->code, e->message);
+  *out = new sb_group{std::get<dispatch::GroupRequest>(std::move(r))};
+  return 0;
+}
+
+int sb_group_report(const sb_group *grp, char *json, size_t cap) {
+  const dispatch::GroupRequest &g = grp->g;
+  const dispatch::GroupReport &r = g.report;
+  std::ostringstream os;
+  int64_t src = 0, wire = 0, dst = 0, payload = 0;
+  for (const auto &rep : g.reports) {
+    src += rep.sourceBytes;
+    wire += rep.wireBytes;
+    dst += rep.destinationBytes;
+    payload += rep.payloadBytesTransferred;
+  }
+  os << "{\"logical_transfers\":" << g.items.size() << ",\"device\":" << g.device
+     << ",\"consumed\":" << (g.consumed ? "true" : "false") << ",\"failed\":" << (g.failed ? "true" : "false")
+     << ",\"payload_copy_calls\":" << r.payloadCopyCalls << ",\"parameter_uploads\":" << r.parameterUploads
+     << ",\"parameter_reuses\":" << r.parameterReuses << ",\"parameter_upload_bytes\":" << r.parameterUploadBytes
+     << ",\"host_transform_bytes\":" << r.hostTransformBytes << ",\"packing_bytes\":" << r.packingBytes
+     << ",\"kernel_launches\":" << r.kernelLaunches << ",\"output_bytes\":" << r.outputBytes
+     << ",\"copy_calls\":" << r.copyCalls << ",\"event_records\":" << r.eventRecords
+     << ",\"event_waits\":" << r.eventWaits << ",\"caller_waits\":" << r.callerWaits
+     << ",\"scratch_peak_bytes\":" << r.scratchPeakBytes << ",\"source_bytes\":" << src
+     << ",\"wire_bytes\":" << wire << ",\"destination_bytes\":" << dst << ",\"payload_bytes_transferred\":" << payload
+     << ",\"items\":[";
+  for (size_t i = 0; i < g.reports.size(); ++i) {
+    dispatch::Report rep = g.reports[i];
+    if (!rep.executed && i < g.items.size())
+      rep = g.items[i].report;
+    os << (i ? "," : "") << reportJson(rep);
+  }
+  os << "]}";
+  return putJson(os.str(), json, cap);
+}
+
+int sb_execute_dispatch_group(sb_group *grp, sb_resources *res, const sb_options *opts, char *report, size_t cap,
+                              sb_error *err) {
+  const TransferOptions o = toOptions(opts);
+  TransferOutcome out;
+  if (res) {
+    out = res->res.execute(grp->g, o, nullptr);
+  } else {
+    dispatch::Resources local(0, 0, 1);
+    TransferOptions blocking = o;
+    blocking.asyncCompletion = false; // the private context ends with this call
+    out = local.execute(grp->g, blocking, nullptr);
+  }
+  sb_group_report(grp, report, cap);
+  if (out.error)
+    return setErr(err, out.error->code, out.error->message);
+  return 0;
+}
+
+int sb_submit_dispatch_group(sb_group *grp, sb_resources *res, const sb_options *opts, sb_completion **out,
+                             sb_error *err) {
+  const TransferOptions o = toOptions(opts);
+  auto handle = std::make_unique<sb_completion>();
+  dispatch::Resources *owner = res ? &res->res : nullptr;
+  if (!owner) {
+    handle->ephemeral = std::make_shared<dispatch::Resources>(0, 0, 1);
+    owner = handle->ephemeral.get();
+  }
+  auto r = owner->submit(grp->g, o, nullptr);
+  if (auto *e = std::get_if<TransferError>(&r))
+    return setErr(err, e->code, e->message);
+  handle->c = std::get<std::shared_ptr<dispatch::Completion>>(std::move(r));
+  *out = handle.release();
+  return 0;
+}
+
+void sb_group_free(sb_group *g) { delete g; }
+
+int sb_completion_wait(sb_completion *c, sb_error *err) {
+  const TransferOutcome o = c->c->wait();
+  if (o.error)
+    return setErr(err, o.error->code, o.error->message);
+  return 0;
+}
+
+int sb_completion_query(sb_completion *c, int32_t *done, sb_error *err) {
+  auto r = c->c->query();
+  if (auto *e = std::get_if<TransferError>(&r))
+    return setErr(err, e->code, e->message);
+  *done = std::get<bool>(r) ? 1 : 0;
+  return 0;
+}
+
+int sb_completion_wait_stream(sb_completion *c, void *stream, sb_error *err) {
+  if (auto e = c->c->waitStream(stream))
+    return setErr(err, e->code, e->message);
+  return 0;
+}
+
+void sb_completion_free(sb_completion *c) { delete c; }
 
 } // extern "C"

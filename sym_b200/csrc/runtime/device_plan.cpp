@@ -326,6 +326,8 @@ std::optional<TransferError> zeroStatus(const Lowered &l, CudaBackend &b, sbc_re
   if (!l.needsStatus)
     return std::nullopt;
   d.status = b.statusWord();
+  if (b.keepStatus) // a group cleared it before its first member
+    return std::nullopt;
   const int rc = sbc_fill(b.statusWord(), 1, 4, 0, b.computeStream());
   if (rc) {
     b.fail("status reset", rc);

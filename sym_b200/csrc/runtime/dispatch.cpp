@@ -199,16 +199,26 @@ Route routeOf(const Implementation &row, const TransferOptions &o) {
   return o.route;
 }
 
-/// Shared tail of a blocking execution: wait, read the status word, learn
-/// the route timing.
-std::optional<TransferError> finish(const b200::Lowered &l, CudaBackend &b, const TransferOptions &o, bool timed,
-                                    Route route, int64_t bytes) {
+/// Shared tail of an execution: signal the caller stream, record
+/// `completionEvent`, then (blocking, or when a status word or a route timing
+/// must be read) wait, check the device fault word and the status word, and
+/// learn the route timing.
+std::optional<TransferError> finish(bool needsStatus, const std::string &classKey, CudaBackend &b,
+                                    const TransferOptions &o, bool timed, Route route, int64_t bytes,
+                                    void *completionEvent = nullptr) {
   if (!b.signalStream(o.callerStream, o.hasCallerStream))
     return terr("backend_failure", b.error());
-  if (o.asyncCompletion && !l.needsStatus && !timed)
+  int rc;
+  if (completionEvent) {
+    if ((rc = sbc_event_record(completionEvent, b.computeStream()))) {
+      b.fail("cudaEventRecord(completion)", rc);
+      return terr("backend_failure", b.error());
+    }
+    ++b.eventRecords;
+  }
+  if (o.asyncCompletion && !needsStatus && !timed)
     return std::nullopt;
-  int rc = sbc_event_synchronize(b.doneEvent());
-  if (rc) {
+  if ((rc = sbc_event_synchronize(b.doneEvent()))) {
     b.fail("completion", rc);
     return terr("backend_failure", b.error());
   }
@@ -222,7 +232,7 @@ std::optional<TransferError> finish(const b200::Lowered &l, CudaBackend &b, cons
   if (timed) {
     float ms = 0;
     if (sbc_event_elapsed_ms(b.startEvent(), b.stopEvent(), &ms) == 0 && bytes > 0) {
-      auto &s = b.routeStats[l.classKey];
+      auto &s = b.routeStats[classKey];
       const double spb = (ms * 1e-3) / static_cast<double>(bytes);
       if (route == Route::DmaRing)
         s.dmaSecondsPerByte = spb;
@@ -230,7 +240,7 @@ std::optional<TransferError> finish(const b200::Lowered &l, CudaBackend &b, cons
         s.zeroCopySecondsPerByte = spb;
     }
   }
-  if (l.needsStatus) {
+  if (needsStatus) {
     if ((rc = sbc_memcpy_d2h_async(b.statusHost(), b.statusWord(), 4, b.computeStream())) ||
         (rc = sbc_stream_synchronize(b.computeStream()))) {
       b.fail("status readback", rc);
@@ -242,31 +252,16 @@ std::optional<TransferError> finish(const b200::Lowered &l, CudaBackend &b, cons
   return std::nullopt;
 }
 
-} // namespace
-
-std::optional<TransferError> executeDispatch(DispatchRequest &req, CudaBackend &b, const TransferOptions &o) {
-  if (req.consumed)
-    return terr("already_executed", "dispatch requests are single-use");
-  req.consumed = true;
-  if (!req.lowered)
-    return terr("implementation_unavailable", "request has no lowered program");
-  if (req.destination.device != b.device())
-    return terr("device_mismatch", "destination lives on cuda:" + std::to_string(req.destination.device) +
-                                       ", the context on cuda:" + std::to_string(b.device()));
-  if (b.failed())
-    return terr("backend_failure", b.error());
-  if (!b.activate())
-    return terr("backend_failure", b.error());
+/// Enqueue one request's copies and kernels (after the caller-stream wait,
+/// before the completion). `timed`: bracket it with the route-timing events.
+std::optional<TransferError> launch(DispatchRequest &req, CudaBackend &b, const TransferOptions &o, bool timed,
+                                    Route &route) {
   const b200::Lowered &l = *req.lowered;
   const void *src = reinterpret_cast<const void *>(req.source.base + req.source.offsetBytes);
   void *dst = reinterpret_cast<void *>(req.destination.base + req.destination.offsetBytes);
-  if (o.hasCallerStream && !b.waitStream(o.callerStream))
-    return terr("backend_failure", b.error());
   TransferOptions ro = o;
   ro.route = routeOf(req.selected, o);
-  const Route route = b200::chooseRoute(l, b, src, ro);
-  // Auto mode learns each route's cost per plan class from event timings.
-  const bool timed = ro.route == Route::Auto && !o.asyncCompletion;
+  route = b200::chooseRoute(l, b, src, ro);
   if (timed)
     sbc_event_record(b.startEvent(), b.copyStream());
   b200::RunStats st;
@@ -288,7 +283,137 @@ std::optional<TransferError> executeDispatch(DispatchRequest &req, CudaBackend &
   rep.copyCalls = b.copyCalls - copies0;
   rep.implementation = req.selected.variant.empty() ? std::string(kB200FusedH2D) + "@" + st.route
                                                     : req.selected.label();
-  return finish(l, b, o, timed, route, req.program.plan.sourceBytes);
+  return std::nullopt;
+}
+
+} // namespace
+
+std::optional<TransferError> executeDispatch(DispatchRequest &req, CudaBackend &b, const TransferOptions &o) {
+  if (req.consumed)
+    return terr("already_executed", "dispatch requests are single-use");
+  req.consumed = true;
+  if (!req.lowered)
+    return terr("implementation_unavailable", "request has no lowered program");
+  if (req.destination.device != b.device())
+    return terr("device_mismatch", "destination lives on cuda:" + std::to_string(req.destination.device) +
+                                       ", the context on cuda:" + std::to_string(b.device()));
+  if (b.failed())
+    return terr("backend_failure", b.error());
+  if (!b.activate())
+    return terr("backend_failure", b.error());
+  if (o.hasCallerStream && !b.waitStream(o.callerStream))
+    return terr("backend_failure", b.error());
+  // Auto mode learns each route's cost per plan class from event timings.
+  const bool timed = routeOf(req.selected, o) == Route::Auto && !o.asyncCompletion;
+  Route route = Route::Auto;
+  if (auto e = launch(req, b, o, timed, route))
+    return e;
+  return finish(req.lowered->needsStatus, req.lowered->classKey, b, o, timed, route, req.program.plan.sourceBytes);
+}
+
+std::variant<GroupRequest, TransferError> prepareDispatchGroup(const std::vector<GroupEntry> &entries) {
+  if (entries.empty() || entries.size() > 256)
+    return terr("invalid_options", "a group must contain between 1 and 256 members");
+  GroupRequest g;
+  std::vector<std::pair<uintptr_t, uintptr_t>> dsts, srcs;
+  for (size_t i = 0; i < entries.size(); ++i) {
+    const GroupEntry &e = entries[i];
+    const std::string who = "group member " + std::to_string(i) + ": ";
+    if (!e.plan)
+      return terr("invalid_options", who + "no plan");
+    if (e.direction != TransferDirection::HostToDevice)
+      return terr("implementation_unavailable", who + "device-to-host transfers are outside this executor");
+    auto r = prepareDispatch(*e.plan, e.source, e.destination);
+    if (auto *err = std::get_if<TransferError>(&r))
+      return terr(err->code.c_str(), who + err->message);
+    DispatchRequest req = std::move(std::get<DispatchRequest>(r));
+    if (g.device < 0)
+      g.device = req.destination.device;
+    else if (req.destination.device != g.device)
+      return terr("device_mismatch", who + "destination on cuda:" + std::to_string(req.destination.device) +
+                                         ", the group on cuda:" + std::to_string(g.device));
+    // prepareDispatch admits dense row-major views only: their spans are the plan's byte counts
+    const size_t sspan = static_cast<size_t>(req.program.plan.sourceBytes);
+    const size_t dspan = static_cast<size_t>(req.program.plan.destinationBytes);
+    const uintptr_t s0 = req.source.base + req.source.offsetBytes, d0 = req.destination.base + req.destination.offsetBytes;
+    srcs.push_back({s0, s0 + sspan});
+    dsts.push_back({d0, d0 + dspan});
+    g.report.outputBytes += dspan;
+    g.items.push_back(std::move(req));
+  }
+  auto overlap = [](const std::pair<uintptr_t, uintptr_t> &a, const std::pair<uintptr_t, uintptr_t> &b) {
+    return a.first < b.second && b.first < a.second;
+  };
+  for (size_t i = 0; i < dsts.size(); ++i)
+    for (size_t j = 0; j < dsts.size(); ++j) {
+      if (j > i && overlap(dsts[i], dsts[j]))
+        return terr("invalid_view", "group members " + std::to_string(i) + " and " + std::to_string(j) +
+                                        " write overlapping destinations");
+      if (overlap(dsts[i], srcs[j]))
+        return terr("invalid_view", "the destination of group member " + std::to_string(i) +
+                                        " overlaps the source of member " + std::to_string(j));
+    }
+  g.reports.resize(g.items.size());
+  return g;
+}
+
+std::optional<TransferError> executeGroup(GroupRequest &g, CudaBackend &b, const TransferOptions &o,
+                                          void *completionEvent) {
+  if (g.consumed)
+    return terr("already_executed", "dispatch groups are single-use");
+  g.consumed = true;
+  if (g.device != b.device())
+    return terr("device_mismatch", "group destinations live on cuda:" + std::to_string(g.device) +
+                                       ", the context on cuda:" + std::to_string(b.device()));
+  for (const DispatchRequest &r : g.items)
+    if (r.consumed || !r.lowered)
+      return terr("already_executed", "a group member was already executed");
+  if (b.failed())
+    return terr("backend_failure", b.error());
+  if (!b.activate())
+    return terr("backend_failure", b.error());
+  const uint64_t copies0 = b.copyCalls, launches0 = b.kernelLaunches, records0 = b.eventRecords,
+                 waits0 = b.eventWaits, callers0 = b.callerWaits;
+  if (o.hasCallerStream && !b.waitStream(o.callerStream))
+    return terr("backend_failure", b.error());
+  // One status word serves the whole group: cleared once here, not per member.
+  bool needsStatus = false;
+  for (const DispatchRequest &r : g.items)
+    needsStatus = needsStatus || r.lowered->needsStatus;
+  if (needsStatus) {
+    const int rc = sbc_fill(b.statusWord(), 1, 4, 0, b.computeStream());
+    if (rc) {
+      b.fail("status reset", rc);
+      return terr("backend_failure", b.error());
+    }
+  }
+  struct Keep {
+    CudaBackend &b;
+    ~Keep() { b.keepStatus = false; }
+  } keep{b};
+  b.keepStatus = true;
+  for (size_t i = 0; i < g.items.size(); ++i) {
+    DispatchRequest &r = g.items[i];
+    r.consumed = true;
+    Route route = Route::Auto;
+    if (auto e = launch(r, b, o, false, route)) {
+      g.failed = true;
+      return terr(e->code.c_str(), "group member " + std::to_string(i) + ": " + e->message);
+    }
+    g.reports[i] = r.report;
+  }
+  b.keepStatus = false;
+  GroupReport &gr = g.report;
+  gr.copyCalls = b.copyCalls - copies0;
+  gr.payloadCopyCalls = gr.copyCalls;
+  gr.kernelLaunches = b.kernelLaunches - launches0;
+  auto e = finish(needsStatus, std::string(), b, o, false, Route::Auto, 0, completionEvent);
+  gr.eventRecords = b.eventRecords - records0;
+  gr.eventWaits = b.eventWaits - waits0;
+  gr.callerWaits = b.callerWaits - callers0;
+  if (e)
+    g.failed = true;
+  return e;
 }
 
 std::optional<TransferError> executeWindow(const DispatchTemplate &t, CudaBackend &b, const void *src, bool hostSource,
@@ -334,7 +459,7 @@ std::optional<TransferError> executeWindow(const DispatchTemplate &t, CudaBacken
   rep.copyCalls = b.copyCalls - copies0;
   rep.sourceBytes = t.program.plan.sourceBytes;
   rep.destinationBytes = t.program.plan.destinationBytes;
-  return finish(l, b, o, false, Route::Auto, 0);
+  return finish(l.needsStatus, l.classKey, b, o, false, Route::Auto, 0);
 }
 
 } // namespace dispatch

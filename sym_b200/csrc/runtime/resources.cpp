@@ -1,6 +1,8 @@
 // Typed contexts; see include/reloc/DispatchResources.h.
 #include "reloc/DispatchResources.h"
 
+#include "sb_cuda.h"
+
 namespace reloc {
 namespace dispatch {
 namespace {
@@ -71,6 +73,149 @@ TransferOutcome Resources::execute(DispatchRequest &request, int device, int /*s
   if (!out.error && options.asyncCompletion)
     out.completion = TransferCompletion::Pending;
   return out;
+}
+
+// ---- groups and completions ---------------------------------------------------
+
+struct Completion::State {
+  std::mutex m;
+  void *event = nullptr;
+  int device = -1;
+  bool finished = false;
+  TransferOutcome outcome;
+  std::shared_ptr<void> owners; // buffers kept alive until completion
+  ~State() {
+    if (event) {
+      if (!finished)
+        sbc_event_synchronize(event); // drain before releasing anything
+      sbc_event_destroy(event);
+    }
+  }
+  /// Finalize after the event completed: the device's fault word.
+  void finalizeLocked() {
+    finished = true;
+    int fault = 0;
+    int dev = -1;
+    sbc_get_device(&dev);
+    if (dev != device)
+      sbc_set_device(device);
+    const int rc = sbc_device_fault(&fault);
+    if (dev != device && dev >= 0)
+      sbc_set_device(dev);
+    if (rc) {
+      outcome.error = terr("backend_failure", std::string("fault word: ") + sbc_error_string(rc));
+      outcome.completion = TransferCompletion::Unknown;
+    } else if (fault) {
+      outcome.error = terr("backend_failure", "a kernel's bounded wait for a TMA copy ran out; the output is incomplete");
+      outcome.completion = TransferCompletion::Complete;
+    } else {
+      outcome.completion = TransferCompletion::Complete;
+    }
+    owners.reset();
+  }
+};
+
+Completion::Completion(std::shared_ptr<State> state) : state_(std::move(state)) {}
+
+Completion::~Completion() {
+  if (state_) {
+    std::lock_guard<std::mutex> g(state_->m);
+    if (!state_->finished && state_->event && sbc_event_synchronize(state_->event) == 0)
+      state_->finalizeLocked();
+  }
+}
+
+TransferOutcome Completion::wait() {
+  std::lock_guard<std::mutex> g(state_->m);
+  if (!state_->finished) {
+    const int rc = sbc_event_synchronize(state_->event);
+    if (rc) {
+      state_->finished = true;
+      state_->outcome.error = terr("backend_failure", std::string("completion: ") + sbc_error_string(rc));
+      state_->outcome.completion = TransferCompletion::Unknown; // owners stay referenced for good
+      return state_->outcome;
+    }
+    state_->finalizeLocked();
+  }
+  return state_->outcome;
+}
+
+std::variant<bool, TransferError> Completion::query() {
+  std::lock_guard<std::mutex> g(state_->m);
+  if (state_->finished) {
+    if (state_->outcome.error)
+      return *state_->outcome.error;
+    return true;
+  }
+  const int rc = sbc_event_query(state_->event);
+  if (rc == 1)
+    return false;
+  if (rc) {
+    state_->finished = true;
+    state_->outcome.error = terr("backend_failure", std::string("completion: ") + sbc_error_string(rc));
+    state_->outcome.completion = TransferCompletion::Unknown;
+    return *state_->outcome.error;
+  }
+  state_->finalizeLocked();
+  if (state_->outcome.error)
+    return *state_->outcome.error;
+  return true;
+}
+
+std::optional<TransferError> Completion::waitStream(const void *consumer) {
+  std::lock_guard<std::mutex> g(state_->m);
+  if (state_->finished && state_->outcome.error)
+    return state_->outcome.error;
+  const int rc = sbc_stream_wait_event(const_cast<void *>(consumer), state_->event);
+  if (rc)
+    return terr("backend_failure", std::string("cudaStreamWaitEvent(consumer): ") + sbc_error_string(rc));
+  return std::nullopt;
+}
+
+TransferOutcome Resources::execute(GroupRequest &group, const TransferOptions &options, std::shared_ptr<void> owners) {
+  if (group.consumed) {
+    TransferOutcome out;
+    out.error = terr("already_executed", "dispatch groups are single-use");
+    return out;
+  }
+  TransferOutcome out =
+      withContext(group.device, [&](CudaBackend &b) { return executeGroup(group, b, options, nullptr); });
+  if (out.completion == TransferCompletion::Unknown) {
+    std::lock_guard<std::mutex> g(mutex_);
+    quarantinedOwners_.push_back(std::move(owners));
+  }
+  if (!out.error && options.asyncCompletion)
+    out.completion = TransferCompletion::Pending;
+  return out;
+}
+
+std::variant<std::shared_ptr<Completion>, TransferError>
+Resources::submit(GroupRequest &group, const TransferOptions &options, std::shared_ptr<void> owners) {
+  if (group.consumed)
+    return terr("already_executed", "dispatch groups are single-use");
+  auto state = std::make_shared<Completion::State>();
+  state->device = group.device;
+  TransferOptions o = options;
+  o.asyncCompletion = true;
+  TransferOutcome out = withContext(group.device, [&](CudaBackend &b) -> std::optional<TransferError> {
+    if (!b.activate())
+      return terr("backend_failure", b.error());
+    const int rc = sbc_event_create(&state->event, 0);
+    if (rc) {
+      state->event = nullptr;
+      return terr("backend_failure", std::string("cudaEventCreate: ") + sbc_error_string(rc));
+    }
+    return executeGroup(group, b, o, state->event);
+  });
+  if (out.error) {
+    if (out.completion == TransferCompletion::Unknown) {
+      std::lock_guard<std::mutex> g(mutex_);
+      quarantinedOwners_.push_back(std::move(owners));
+    }
+    return *out.error;
+  }
+  state->owners = std::move(owners);
+  return std::make_shared<Completion>(std::move(state));
 }
 
 ResourceStats Resources::stats() const {

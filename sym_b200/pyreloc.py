@@ -528,3 +528,162 @@ def execute_transfer(request: DispatchRequest, caller_stream=None, n_buffers=4, 
     """Run a prepared layout transfer (GPU-only, like execute_dispatch)."""
     return execute_dispatch(request, caller_stream=caller_stream, n_buffers=n_buffers, resources=resources,
                             route=route, chunk_size=chunk_size, async_completion=async_completion)
+
+
+# ---------------------------------------------------------------------------
+# consumer-sized groups and asynchronous completion
+# (reference pyreloc: prepare_dispatch_group / execute_dispatch_group /
+# submit_dispatch_group / DispatchCompletion, PyDispatch.cpp:625-700)
+# ---------------------------------------------------------------------------
+
+class DispatchGroup(_Handle):
+    """A validated, single-use group of requests on one CUDA device."""
+
+    _free = "sb_group_free"
+
+    def __init__(self, ptr, templates):
+        super().__init__(ptr)
+        self.templates = templates  # kept alive with the group
+        self.consumed = False
+        self.failed = False
+        self._executing = False
+
+    @property
+    def report(self):
+        if self._executing:
+            raise ValueError("report is unavailable during execution")
+        return MappingProxyType(json_call(_native.lib().sb_group_report, self._ptr))
+
+
+def prepare_dispatch_group(entries):
+    """Validate ``(plan, source_view, destination_view, direction)`` entries
+    together. ``plan`` is a typed ``DispatchTemplate`` or a layout
+    ``BoundPlan`` (read through its transfer template, with the views spanned
+    like ``make_transfer``). Launches nothing."""
+    from ._native import SbGroupEntry
+
+    entries = list(entries)
+    if not 1 <= len(entries) <= 256:
+        raise TransferError("invalid_options", "a group must contain between 1 and 256 members")
+    arr = (SbGroupEntry * len(entries))()
+    templates = []
+    for i, (plan, source, destination, direction) in enumerate(entries):
+        if direction not in _DIRECTIONS:
+            raise ValueError("direction must be 'h2d' or 'd2h'")
+        if isinstance(plan, BoundPlan):
+            tmpl = prepare_transfer_template(plan)
+            span = 1 + sum((e - 1) * s for e, s in zip(plan.extents, plan.src_strides))
+            source = _span_view(source, span)
+            destination = _span_view(destination, plan.total_bytes // plan.element_size)
+        elif isinstance(plan, DispatchTemplate):
+            tmpl = plan
+        else:
+            raise TypeError("group plans are dispatch templates or layout bound plans")
+        templates.append(tmpl)
+        arr[i].plan = tmpl.ptr
+        arr[i].source = source.native()
+        arr[i].destination = destination.native()
+        arr[i].direction = _DIRECTIONS[direction]
+    out = ctypes.c_void_p()
+    err = SbError()
+    if _native.lib().sb_prepare_dispatch_group(arr, len(entries), ctypes.byref(out), ctypes.byref(err)):
+        _raise_transfer(err)
+    return DispatchGroup(out, templates)
+
+
+def _group_call(group, name):
+    if not isinstance(group, DispatchGroup):
+        raise TypeError("expected a DispatchGroup")
+    if group.consumed or group._executing:
+        raise TransferError("already_executed", "dispatch groups are single-use")
+
+
+def execute_dispatch_group(group, *, caller_stream=None, gather_threads=8, gather_pool=None, pinning="auto",
+                           min_pinned_bytes=None, max_scratch_bytes=64 << 20, resources=None, owners=None,
+                           device_layout=False, n_buffers=4, chunked_members=False, route="auto", chunk_size=0):
+    """Run every member after one wait on ``caller_stream`` and complete once
+    (blocking). Host-worker knobs of the reference are accepted and ignored."""
+    _group_call(group, "execute")
+    group._executing = True
+    opts = _options(n_buffers, route, chunk_size, caller_stream, False)
+    err = SbError()
+    buf = ctypes.create_string_buffer(1 << 20)
+    _keep = owners
+    try:
+        rc = _native.lib().sb_execute_dispatch_group(group.ptr, resources.handle if resources is not None else None,
+                                                     ctypes.byref(opts), buf, 1 << 20, ctypes.byref(err))
+    finally:
+        group._executing = False
+        group.consumed = True
+        del _keep
+    if rc:
+        group.failed = True
+        _raise_transfer(err)
+    import json
+
+    return MappingProxyType(json.loads(buf.value.decode()))
+
+
+class DispatchCompletion(_Handle):
+    """The pending completion of a submitted group. ``wait()`` blocks the
+    host; ``wait_stream(stream)`` orders a consumer stream after the group
+    without blocking; ``query()`` polls. Buffer owners are held until the
+    group is known complete. Dropping the handle waits for the group."""
+
+    _free = "sb_completion_free"
+
+    def __init__(self, ptr, group, owners):
+        super().__init__(ptr)
+        self._group = group
+        self._owners = owners
+
+    def _done(self):
+        self._owners = None
+
+    def wait(self):
+        err = SbError()
+        if _native.lib().sb_completion_wait(self._ptr, ctypes.byref(err)):
+            code = err.code.decode()
+            if code != "backend_failure" or "completion" not in err.message.decode():
+                self._done()
+            _raise_transfer(err)
+        self._done()
+
+    def query(self):
+        done = ctypes.c_int32()
+        err = SbError()
+        if _native.lib().sb_completion_query(self._ptr, ctypes.byref(done), ctypes.byref(err)):
+            _raise_transfer(err)
+        if done.value:
+            self._done()
+        return bool(done.value)
+
+    def wait_stream(self, stream):
+        err = SbError()
+        if _native.lib().sb_completion_wait_stream(self._ptr, ctypes.c_void_p(int(stream or 0)),
+                                                   ctypes.byref(err)):
+            _raise_transfer(err)
+
+    def __reduce_ex__(self, protocol):
+        raise TypeError("dispatch completions cannot be serialized")
+
+
+def submit_dispatch_group(group, *, caller_stream=None, gather_threads=8, gather_pool=None, pinning="auto",
+                          min_pinned_bytes=None, max_scratch_bytes=64 << 20, resources=None, owners=None,
+                          device_layout=False, n_buffers=4, chunked_members=False, route="auto", chunk_size=0):
+    """Enqueue the group and return its ``DispatchCompletion`` without waiting."""
+    _group_call(group, "submit")
+    group._executing = True
+    opts = _options(n_buffers, route, chunk_size, caller_stream, True)
+    err = SbError()
+    out = ctypes.c_void_p()
+    try:
+        rc = _native.lib().sb_submit_dispatch_group(group.ptr, resources.handle if resources is not None else None,
+                                                    ctypes.byref(opts), ctypes.byref(out), ctypes.byref(err))
+    finally:
+        group._executing = False
+        group.consumed = True
+    if rc:
+        group.failed = True
+        _raise_transfer(err)
+    return DispatchCompletion(out, group, owners)

@@ -111,6 +111,28 @@ class PreparedTypedTransfer:
     def report(self):
         return MappingProxyType(dict(self.selected))
 
+    direction = "h2d"
+
+    @property
+    def destination(self):
+        """The fresh output this request produces: dense, on ``device``."""
+        shape = tuple(int(e) for e in self.bound.result_extents)
+        strides, run = [], 1
+        for e in reversed(shape):
+            strides.append(run)
+            run *= e
+        return TensorDescriptor(shape, tuple(reversed(strides)), self.bound.result_dtype, self.device)
+
+
+@dataclass(frozen=True)
+class TensorDescriptor:
+    """Shape, strides (elements), dtype name and device of a transfer output."""
+
+    shape: tuple
+    strides: tuple
+    dtype: str
+    device: object
+
 
 def prepare_typed_transfer(compiled, source, device, *, parameters=None, policy="auto", calibration=None,
                            threads=8, implementation=""):

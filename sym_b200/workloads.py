@@ -3,7 +3,9 @@
 ``WeightFetcher`` keeps the interface of the reference workload
 (libreloc/python/examples/workloads/common.py:384-598): one symbolic typed
 recipe compiled once and bound for every matrix shape, ``fetch``,
-``fetch_many``, per-device retained resources, ``reference`` and ``close``.
+``fetch_many`` (one transfer group), ``prepare_many``, ``prefetch`` (a
+bounded asynchronous window), per-device retained resources, ``reference``
+and ``close``.
 Its default recipe is the reference's own (int8 ``[in, out]``, per-output-
 channel f32 scale on axis 1 -> dequantize -> transpose -> f32 ``[out, in]``);
 ``layout="out_in_f16"`` selects the BASELINE weight-streaming recipe (int8
@@ -18,7 +20,7 @@ every GPU. Matrix i's all-gather overlaps matrix i+1's fetch.
 """
 from __future__ import annotations
 
-from contextlib import ExitStack
+from contextlib import ExitStack, contextmanager
 
 from . import pyreloc
 from .reloc_torch import dispatch
@@ -87,6 +89,7 @@ class WeightFetcher:
         self.kind = kind
         self.implementation = implementation
         self._resources = {}
+        self._queues = {}
         self._cleanup = ExitStack()
         self._closed = False
         self.report.add_plan_compiles(1)
@@ -129,9 +132,82 @@ class WeightFetcher:
         return result.tensor
 
     def fetch_many(self, weights, device, *, max_scratch_bytes=64 << 20):
-        """Fetch related (int8 matrix, scale) pairs; outputs are independent tensors."""
+        """Fetch related (int8 matrix, scale) pairs as ONE transfer group: one
+        caller-stream ordering and one completion for all of them (reference
+        common.py:481-513). Outputs are independent tensors."""
+        from .reloc_torch.group import execute_transfer_group
+
+        if self._closed:
+            raise RuntimeError("weight fetcher is closed")
         device = self._device(device)
-        return [self.fetch(q, s, device) for q, s in weights]
+        weights = tuple(weights)
+        result = execute_transfer_group(self.prepare_many(weights, device), resources=self._owner(device),
+                                        max_scratch_bytes=max_scratch_bytes)
+        for (q, _), rep in zip(weights, result.report["items"]):
+            self.shapes.add(tuple(q.shape))
+            self.report.add_dispatch(rep["implementation"])
+            self.report.add_bytes(self.kind, rep["source_bytes"], rep["wire_bytes"], rep["destination_bytes"],
+                                  payload=rep["payload_bytes_transferred"])
+        totals = self.report.data.setdefault("transfer_groups", {"groups": 0})
+        totals["groups"] += 1
+        for name in ("logical_transfers", "copy_calls", "event_records", "event_waits", "caller_waits",
+                     "parameter_uploads", "parameter_reuses", "packing_bytes", "kernel_launches"):
+            totals[name] = totals.get(name, 0) + result.report[name]
+        return result.tensors
+
+    def prepare_many(self, weights, device):
+        """Bind the current values of (int8 matrix, scale) pairs into a group
+        without launching anything or caching weight values."""
+        from .reloc_torch.group import prepare_transfer_group
+
+        if self._closed:
+            raise RuntimeError("weight fetcher is closed")
+        device = self._device(device)
+        requests = []
+        for q, scale in weights:
+            requests.append(self._prepare(q, scale, device))
+            self.shapes.add(tuple(q.shape))
+        return prepare_transfer_group(requests)
+
+    @contextmanager
+    def prefetch(self, weight_groups, device, *, max_output_bytes=128 << 20, max_scratch_bytes=64 << 20,
+                 gather_threads=8):
+        """Bounded lookahead over groups of (int8 matrix, scale) pairs (one group
+        per layer or expert set): yields a window whose iteration returns each
+        group's outputs, ordered on the current stream, while the next group's
+        transfer is already in flight (reference common.py:528-571). CPU
+        weights and scales must stay unchanged for the window's lifetime."""
+        from .reloc_torch.asynchronous import TransferQueue
+
+        if self._closed:
+            raise RuntimeError("weight fetcher is closed")
+        if self.resource_policy != "retained":
+            raise ValueError("prefetch requires retained weight resources")
+        device = self._device(device)
+        key = str(device)
+        if key not in self._queues:
+            self._queues[key] = self._cleanup.enter_context(TransferQueue(
+                device, max_output_bytes=max_output_bytes, max_scratch_bytes=max_scratch_bytes,
+                gather_threads=gather_threads, resources=self._owner(device)))
+        queue = self._queues[key]
+        if (queue.max_output_bytes, queue.max_scratch_bytes, queue.gather_threads) != (
+                max_output_bytes, max_scratch_bytes, gather_threads):
+            raise ValueError("prefetch limits cannot change on an existing device queue")
+        before = queue.stats()["totals"]
+        try:
+            with queue.prefetch(self.prepare_many(w, device) for w in weight_groups) as window:
+                yield window
+        finally:
+            after = queue.stats()
+            t = after["totals"]
+            if t["logical_transfers"] > before["logical_transfers"]:
+                self.report.add_bytes(self.kind, t["source_bytes"] - before["source_bytes"],
+                                      t["wire_bytes"] - before["wire_bytes"],
+                                      t["destination_bytes"] - before["destination_bytes"],
+                                      payload=t["payload_bytes_transferred"] - before["payload_bytes_transferred"])
+            for label, count in t["dispatches"].items():
+                self.report.add_dispatch(label, count - before["dispatches"].get(label, 0))
+            self.report.data.setdefault("weight_prefetch", {})[key] = after
 
     def template(self, q_shape, scale):
         """A reusable dispatch template for one matrix shape and scale (no buffers)."""
