@@ -10,6 +10,11 @@
 //   b200_fused_h2d@dma_ring   raw source chunks DMA'd into an HBM ring, then
 //                             the fused transform kernel per chunk
 //   b200_fused_h2d@zero_copy  the fused kernel reads pinned host memory
+//   b200_fused_d2h            device source -> host destination: the fused
+//                             kernel writes result-row chunks into the HBM
+//                             ring, the copy engine drains them to the host
+//                             (@dma_ring), or the kernel writes mapped pinned
+//                             host memory directly (@zero_copy)
 // The reference's CPU rows (cpu_reference, cpu_stages_cuda_stages@k) and its
 // legacy CUDA rows are listed as excluded with a reason: no supported plan
 // executes on the CPU here.
@@ -38,6 +43,7 @@ namespace dispatch {
 enum class Policy { OriginalCpu, Auto };
 
 inline constexpr const char *kB200FusedH2D = "b200_fused_h2d";
+inline constexpr const char *kB200FusedD2H = "b200_fused_d2h";
 inline constexpr const char *kCpuReference = "cpu_reference";
 inline constexpr const char *kCpuStagesCudaStages = "cpu_stages_cuda_stages";
 inline constexpr const char *kCudaStagesThenCpu = "cuda_stages_then_cpu";
@@ -136,6 +142,10 @@ std::variant<DispatchRequest, TransferError> prepareDispatch(const DispatchTempl
 std::variant<DispatchRequest, TransferError> prepareDispatch(const TypedBoundPlan &plan, const BufferView &source,
                                                              const BufferView &destination,
                                                              TransferDirection direction, const Options &options);
+
+/// The CUDA device a request runs on: the destination's (H2D) or the
+/// source's (D2H).
+int executionDevice(const DispatchRequest &request);
 
 /// Run the selected row on `backend` (one device's streams, HBM ring and
 /// parameter buffers). Blocks until this request's work completed unless

@@ -521,7 +521,7 @@ int sb_prepare_dispatch(const sb_template *t, const sb_view *src, const sb_view 
 int sb_execute_dispatch(sb_request *req, sb_resources *res, const sb_options *opts, char *report, size_t cap,
                         sb_error *err) {
   const TransferOptions o = toOptions(opts);
-  const int device = req->r.destination.device;
+  const int device = dispatch::executionDevice(req->r);
   TransferOutcome out;
   if (res) {
     out = res->res.execute(req->r, device, 2, o, nullptr);

@@ -355,6 +355,109 @@ std::optional<TransferError> runDevice(const Lowered &l, CudaBackend &b, const v
   return launch(l, b, d, st);
 }
 
+namespace {
+
+/// Rows of axis 0 are contiguous slabs of the destination (the box covers a
+/// dense destination and axis 0 is its outermost axis).
+bool d2hRows(const Lowered &l) {
+  return l.denseCover && l.desc.dst_strides[0] * l.padded[0] == l.dstElements && l.padded[0] > 1;
+}
+
+bool mappedPinned(void *host, void **mapped) {
+  int kind = 0, dev = -1;
+  return sbc_pointer_info(host, &kind, &dev) == 0 && kind == 1 && sbc_host_device_pointer(host, mapped) == 0;
+}
+
+} // namespace
+
+Route chooseRouteD2H(const Lowered &l, void *hdst, const TransferOptions &o) {
+  if (o.route != Route::Auto)
+    return o.route;
+  void *mapped = nullptr;
+  if (d2hRows(l))
+    return Route::DmaRing;
+  return mappedPinned(hdst, &mapped) ? Route::ZeroCopy : Route::Staged;
+}
+
+std::optional<TransferError> runD2H(const Lowered &l, CudaBackend &b, const void *dsrc, void *hdst, Route route,
+                                    const TransferOptions &o, RunStats &st) {
+  const int wd = l.desc.dst_width;
+  const int64_t dstBytes = l.dstElements * wd;
+  if (route == Route::ZeroCopy) {
+    void *mapped = nullptr;
+    if (!mappedPinned(hdst, &mapped))
+      return terr("invalid_view", "zero_copy needs a mapped pinned host destination");
+    st.route = "zero_copy";
+    st.payloadBytes += dstBytes;
+    return runDevice(l, b, dsrc, mapped, RowWindow{}, st);
+  }
+  // Chunks of whole result rows through the ring; else the whole result
+  // through the staging buffer.
+  const bool rows = route != Route::Staged && d2hRows(l);
+  const int64_t rowBytes = rows ? l.desc.dst_strides[0] * wd : std::max<int64_t>(dstBytes, 1);
+  const int64_t nrows = rows ? l.padded[0] : 1;
+  const size_t target = o.chunkSizeOverride ? o.chunkSizeOverride : kDefaultChunkBytes;
+  int64_t rowsPer = rows ? std::max<int64_t>(1, static_cast<int64_t>(target) / rowBytes) : 1;
+  if (rowsPer >= 64)
+    rowsPer -= rowsPer % 64; // whole kernel tiles per chunk
+  const int slots = rows ? std::max(2, o.nBuffers) : 1;
+  void *stage = nullptr;
+  if (rows) {
+    if (!b.ensureRing(slots, static_cast<size_t>(rowsPer * rowBytes)))
+      return terr("backend_failure", b.error());
+  } else if (!(stage = b.staging(static_cast<size_t>(rowBytes)))) {
+    return terr("backend_failure", b.error());
+  }
+  auto slotOf = [&](int k) { return rows ? b.slot(k) : stage; };
+  auto readyOf = [&](int k) { return rows ? b.slotReady(k) : b.stagingReady(); };
+  auto freeOf = [&](int k) { return rows ? b.slotFree(k) : b.stagingFree(); };
+  st.route = rows ? "dma_ring" : "staged";
+  st.buffers = static_cast<size_t>(slots);
+  st.chunkBytes = static_cast<size_t>(rowsPer * rowBytes);
+  // One status word for all chunks: cleared once here, read once at the end.
+  if (l.needsStatus && !b.keepStatus) {
+    const int rc = sbc_fill(b.statusWord(), 1, 4, 0, b.computeStream());
+    if (rc) {
+      b.fail("status reset", rc);
+      return terr("backend_failure", b.error());
+    }
+  }
+  struct Keep {
+    CudaBackend &b;
+    bool old;
+    ~Keep() { b.keepStatus = old; }
+  } keep{b, b.keepStatus};
+  b.keepStatus = true;
+  int64_t i = 0;
+  for (int64_t r0 = 0; r0 < nrows; r0 += rowsPer, ++i) {
+    const int64_t r1 = std::min(r0 + rowsPer, nrows);
+    const int s = static_cast<int>(i % slots);
+    void *slot = slotOf(s);
+    int rc;
+    if ((rc = sbc_stream_wait_event(b.computeStream(), freeOf(s)))) {
+      b.fail("ring wait", rc);
+      return terr("backend_failure", b.error());
+    }
+    if (auto e = runDevice(l, b, dsrc, slot, rows ? RowWindow{r0, r1} : RowWindow{}, st))
+      return e;
+    const size_t bytes = static_cast<size_t>((r1 - r0) * rowBytes);
+    if ((rc = sbc_event_record(readyOf(s), b.computeStream())) ||
+        (rc = sbc_stream_wait_event(b.copyStream(), readyOf(s))) ||
+        (rc = sbc_memcpy_d2h_async(static_cast<uint8_t *>(hdst) + r0 * rowBytes, slot, bytes, b.copyStream())) ||
+        (rc = sbc_event_record(freeOf(s), b.copyStream()))) {
+      b.fail("ring download", rc);
+      return terr("backend_failure", b.error());
+    }
+    ++b.copyCalls;
+    ++st.copies;
+    b.eventRecords += 2;
+    b.eventWaits += 2;
+    st.payloadBytes += static_cast<int64_t>(bytes);
+    ++st.chunks;
+  }
+  return std::nullopt;
+}
+
 Route chooseRoute(const Lowered &l, CudaBackend &b, const void *hsrc, const TransferOptions &o) {
   if (o.route != Route::Auto)
     return o.route;

@@ -75,6 +75,17 @@ std::optional<TransferError> runDevice(const Lowered &l, CudaBackend &b, const v
 std::optional<TransferError> runH2D(const Lowered &l, CudaBackend &b, const void *hsrc, void *ddst, Route route,
                                     RowWindow window, const TransferOptions &options, RunStats &stats);
 
+/// Device source -> host destination: the fused kernel writes chunks of
+/// result rows into the HBM ring (or, zero copy, straight into mapped pinned
+/// host memory) and the copy engine drains each chunk to the host. Enqueued
+/// on the backend's streams; the caller orders/blocks.
+std::optional<TransferError> runD2H(const Lowered &l, CudaBackend &b, const void *dsrc, void *hdst, Route route,
+                                    const TransferOptions &options, RunStats &stats);
+
+/// Route::Auto for a device-to-host execution: the DMA ring when the result
+/// splits into row chunks, else zero copy into pinned memory, else staged.
+Route chooseRouteD2H(const Lowered &l, void *hdst, const TransferOptions &options);
+
 /// Host source -> device destination on the caller's `stream` through the
 /// statically allocated scratch `scratch` (`scratchBytes`), allocating
 /// nothing: parameters and one staging slot live in the scratch, chunks of

@@ -20,13 +20,14 @@ TransferError terr(const char *code, std::string msg) { return TransferError{cod
 
 const char *const kCpuExcluded = "the B200 executor runs no supported plan on the CPU";
 
-Implementation b200Row(const typed::Program &p, const char *variant, const b200::Lowered *l) {
+Implementation b200Row(const typed::Program &p, const char *variant, const b200::Lowered *l, bool d2h = false) {
   Implementation row;
-  row.id = kB200FusedH2D;
+  row.id = d2h ? kB200FusedD2H : kB200FusedH2D;
   row.variant = variant;
-  row.wireBoundary = 0; // the raw source crosses the link
-  row.wireResultLayout = false;
-  row.wireBytes = p.plan.sourceBytes;
+  // H2D: the raw source crosses the link; D2H: the finished result does
+  row.wireBoundary = d2h ? static_cast<uint32_t>(p.stages.size()) : 0;
+  row.wireResultLayout = d2h;
+  row.wireBytes = d2h ? p.plan.destinationBytes : p.plan.sourceBytes;
   row.deviceTempBytes = 0;
   row.method = "B";
   (void)l;
@@ -43,23 +44,22 @@ Capability queryCapability(const typed::Program &p, TransferDirection direction,
     cap.excluded.push_back({std::string(kCpuStagesCudaStages) + "@" + std::to_string(k), kCpuExcluded});
   cap.excluded.push_back({kCudaDequantRelocate, "superseded by b200_fused_h2d"});
   cap.excluded.push_back({kCudaRelocateF32, "superseded by b200_fused_h2d"});
-  if (direction == TransferDirection::DeviceToHost) {
-    cap.excluded.push_back({kB200FusedH2D, "device-to-host transfers are outside this executor"});
-    return cap;
-  }
+  const bool d2h = direction == TransferDirection::DeviceToHost;
+  const char *id = d2h ? kB200FusedD2H : kB200FusedH2D;
+  cap.excluded.push_back({d2h ? kB200FusedH2D : kB200FusedD2H, "the other transfer direction"});
   if (!cuda) {
-    cap.excluded.push_back({kB200FusedH2D, "no CUDA device end"});
+    cap.excluded.push_back({id, "no CUDA device end"});
     return cap;
   }
   auto lowered = b200::lower(p);
   if (auto *e = std::get_if<TransferError>(&lowered)) {
-    cap.excluded.push_back({kB200FusedH2D, e->code + ": " + e->message});
+    cap.excluded.push_back({id, e->code + ": " + e->message});
     return cap;
   }
   const auto &l = std::get<b200::Lowered>(lowered);
-  cap.eligible.push_back(b200Row(p, "", &l));
-  cap.eligible.push_back(b200Row(p, "dma_ring", &l));
-  cap.eligible.push_back(b200Row(p, "zero_copy", &l));
+  cap.eligible.push_back(b200Row(p, "", &l, d2h));
+  cap.eligible.push_back(b200Row(p, "dma_ring", &l, d2h));
+  cap.eligible.push_back(b200Row(p, "zero_copy", &l, d2h));
   return cap;
 }
 
@@ -86,7 +86,7 @@ std::variant<Selection, TransferError> selectImplementation(const typed::Program
   if (cap.eligible.empty()) {
     std::string why;
     for (const Exclusion &e : cap.excluded)
-      if (e.id == kB200FusedH2D)
+      if (e.id == (direction == TransferDirection::DeviceToHost ? kB200FusedD2H : kB200FusedH2D))
         why = e.reason;
     return terr("implementation_unavailable", "no eligible row: " + why);
   }
@@ -150,15 +150,14 @@ std::optional<TransferError> checkView(const BufferView &v, const std::vector<in
 
 std::variant<DispatchRequest, TransferError> prepareDispatch(const DispatchTemplate &t, const BufferView &src,
                                                              const BufferView &dst) {
-  if (t.direction != TransferDirection::HostToDevice)
-    return terr("implementation_unavailable", "device-to-host transfers are outside this executor");
+  const bool d2h = t.direction == TransferDirection::DeviceToHost;
   const typed::Program &p = t.program;
   const uint32_t n = static_cast<uint32_t>(p.stages.size());
-  if (auto e = checkView(src, p.plan.sourceExtents, typed::widthAt(p, 0), p.plan.sourceBytes, MemoryKind::Host,
-                         "source"))
+  if (auto e = checkView(src, p.plan.sourceExtents, typed::widthAt(p, 0), p.plan.sourceBytes,
+                         d2h ? MemoryKind::Cuda : MemoryKind::Host, "source"))
     return *e;
-  if (auto e = checkView(dst, p.plan.resultExtents, typed::widthAt(p, n), p.plan.destinationBytes, MemoryKind::Cuda,
-                         "destination"))
+  if (auto e = checkView(dst, p.plan.resultExtents, typed::widthAt(p, n), p.plan.destinationBytes,
+                         d2h ? MemoryKind::Host : MemoryKind::Cuda, "destination"))
     return *e;
   DispatchRequest r;
   r.program = p;
@@ -261,12 +260,14 @@ std::optional<TransferError> launch(DispatchRequest &req, CudaBackend &b, const 
   void *dst = reinterpret_cast<void *>(req.destination.base + req.destination.offsetBytes);
   TransferOptions ro = o;
   ro.route = routeOf(req.selected, o);
-  route = b200::chooseRoute(l, b, src, ro);
+  const bool d2h = req.direction == TransferDirection::DeviceToHost;
+  route = d2h ? b200::chooseRouteD2H(l, dst, ro) : b200::chooseRoute(l, b, src, ro);
   if (timed)
     sbc_event_record(b.startEvent(), b.copyStream());
   b200::RunStats st;
   const uint64_t copies0 = b.copyCalls, launches0 = b.kernelLaunches;
-  if (auto e = b200::runH2D(l, b, src, dst, route, b200::RowWindow{}, ro, st))
+  if (auto e = d2h ? b200::runD2H(l, b, src, dst, route, ro, st)
+                   : b200::runH2D(l, b, src, dst, route, b200::RowWindow{}, ro, st))
     return e;
   if (timed)
     sbc_event_record(b.stopEvent(), b.computeStream());
@@ -281,12 +282,15 @@ std::optional<TransferError> launch(DispatchRequest &req, CudaBackend &b, const 
   rep.payloadBytesTransferred = st.payloadBytes + static_cast<int64_t>(l.paramBlob.size());
   rep.kernelLaunches = b.kernelLaunches - launches0;
   rep.copyCalls = b.copyCalls - copies0;
-  rep.implementation = req.selected.variant.empty() ? std::string(kB200FusedH2D) + "@" + st.route
-                                                    : req.selected.label();
+  rep.implementation = req.selected.variant.empty() ? req.selected.id + "@" + st.route : req.selected.label();
   return std::nullopt;
 }
 
 } // namespace
+
+int executionDevice(const DispatchRequest &req) {
+  return req.direction == TransferDirection::DeviceToHost ? req.source.device : req.destination.device;
+}
 
 std::optional<TransferError> executeDispatch(DispatchRequest &req, CudaBackend &b, const TransferOptions &o) {
   if (req.consumed)
@@ -294,8 +298,8 @@ std::optional<TransferError> executeDispatch(DispatchRequest &req, CudaBackend &
   req.consumed = true;
   if (!req.lowered)
     return terr("implementation_unavailable", "request has no lowered program");
-  if (req.destination.device != b.device())
-    return terr("device_mismatch", "destination lives on cuda:" + std::to_string(req.destination.device) +
+  if (executionDevice(req) != b.device())
+    return terr("device_mismatch", "the device end lives on cuda:" + std::to_string(executionDevice(req)) +
                                        ", the context on cuda:" + std::to_string(b.device()));
   if (b.failed())
     return terr("backend_failure", b.error());
@@ -303,8 +307,9 @@ std::optional<TransferError> executeDispatch(DispatchRequest &req, CudaBackend &
     return terr("backend_failure", b.error());
   if (o.hasCallerStream && !b.waitStream(o.callerStream))
     return terr("backend_failure", b.error());
-  // Auto mode learns each route's cost per plan class from event timings.
-  const bool timed = routeOf(req.selected, o) == Route::Auto && !o.asyncCompletion;
+  // Auto mode learns each H2D route's cost per plan class from event timings.
+  const bool timed = routeOf(req.selected, o) == Route::Auto && !o.asyncCompletion &&
+                     req.direction == TransferDirection::HostToDevice;
   Route route = Route::Auto;
   if (auto e = launch(req, b, o, timed, route))
     return e;

@@ -93,6 +93,7 @@ class PreparedTypedTransfer:
     capability: dict
     selected: dict
     consumed: bool = False
+    direction: str = "h2d"
     _storage: tuple = field(default=(), repr=False)
     _execution_lock: object = field(default_factory=Lock, repr=False, compare=False)
 
@@ -110,8 +111,6 @@ class PreparedTypedTransfer:
     @property
     def report(self):
         return MappingProxyType(dict(self.selected))
-
-    direction = "h2d"
 
     @property
     def destination(self):
@@ -144,7 +143,9 @@ def prepare_typed_transfer(compiled, source, device, *, parameters=None, policy=
         raise ValueError(f"policy must be one of {POLICIES}, got {policy!r}")
     threads = operator.index(threads)
     device = torch.device(device)
-    if compiled.recipe.direction != "h2d" or source.device.type != "cpu" or device.type != "cuda":
+    direction = compiled.recipe.direction
+    ends = {"h2d": ("cpu", "cuda"), "d2h": ("cuda", "cpu")}.get(direction)
+    if ends is None or source.device.type != ends[0] or device.type != ends[1]:
         raise UnsupportedRecipe("direction_mismatch",
                                 f"{compiled.recipe.direction} recipe cannot move {source.device} -> {device}")
     if dtype_name(source.dtype) != compiled.recipe.source.dtype:
@@ -160,8 +161,9 @@ def prepare_typed_transfer(compiled, source, device, *, parameters=None, policy=
         raise UnsupportedRecipe("parameter_binding",
                                 f"declared parameters {sorted(declared)}; missing {missing}, unexpected {extra}")
     snapshots = {n: _parameter_snapshot(n, parameters[n], declared[n]) for n in declared}
-    index = device.index if device.index is not None else torch.cuda.current_device()
-    key = ("typed", tuple(sorted(bindings.items())),
+    gpu = source.device if direction == "d2h" else device
+    index = gpu.index if gpu.index is not None else torch.cuda.current_device()
+    key = ("typed", direction, tuple(sorted(bindings.items())),
            tuple((n, d, tuple(e), b) for n, (d, e, b) in sorted(snapshots.items())), index, policy, implementation)
     cache = compiled._execution_templates
     hit = cache.get(key)
@@ -171,7 +173,7 @@ def prepare_typed_transfer(compiled, source, device, *, parameters=None, policy=
         except pyreloc.BindError as error:
             raise UnsupportedRecipe("bind_error", str(error)) from error
         try:
-            template = pyreloc.prepare_dispatch_template(bound, "h2d", "cuda", policy=policy,
+            template = pyreloc.prepare_dispatch_template(bound, direction, "cuda", policy=policy,
                                                          implementation=implementation)
         except pyreloc.TransferError as error:
             raise UnsupportedRecipe(error.code, str(error)) from error
@@ -179,6 +181,10 @@ def prepare_typed_transfer(compiled, source, device, *, parameters=None, policy=
     bound, template = hit
     if list(source.shape) != list(bound.source_extents):
         raise UnsupportedRecipe("shape_mismatch", f"source shape {list(source.shape)} vs {bound.source_extents}")
+    if direction == "d2h":
+        return PreparedTypedTransfer(compiled, source, bindings, bound, template, torch.device("cpu"),
+                                     storage_view(source, "cuda", index), parameters, snapshots,
+                                     template.capability, dict(template.selection), direction="d2h")
     return PreparedTypedTransfer(compiled, source, bindings, bound, template, torch.device("cuda", index),
                                  storage_view(source, "host", -1), parameters, snapshots, template.capability,
                                  dict(template.selection))
@@ -202,25 +208,27 @@ def execute_typed_transfer(request, *, n_buffers=4, n_streams=2, gather_threads=
         request.recheck()
         shape = list(request.bound.result_extents)
         dtype = getattr(torch, request.bound.result_dtype)
+        d2h = request.direction == "d2h"
         if out is None:
-            out = torch.empty(shape, dtype=dtype, device=request.device)
+            out = torch.empty(shape, dtype=dtype, pin_memory=True) if d2h else \
+                torch.empty(shape, dtype=dtype, device=request.device)
         elif list(out.shape) != shape or out.dtype != dtype or out.device != request.device \
                 or not out.is_contiguous():
             raise ValueError("out must be a dense tensor of the result shape, dtype and device")
-        dst_view = storage_view(out, "cuda", out.device.index)
+        dst_view = storage_view(out, "host", -1) if d2h else storage_view(out, "cuda", out.device.index)
         try:
             native = pyreloc.prepare_dispatch_from_template(request.template, request.source_view, dst_view)
         except pyreloc.TransferError as error:
             raise RuntimeError(f"typed dispatch rejected at execution: {error}") from error
         request.consumed = True
-        stream = torch.cuda.current_stream(request.device).cuda_stream
+        stream = torch.cuda.current_stream(request.source.device if d2h else request.device).cuda_stream
         try:
             report = pyreloc.execute_dispatch(
                 native, caller_stream=stream, n_buffers=n_buffers, chunk_size=chunk_size or 0,
                 resources=None if resources is None else resources.native_typed,
                 owners=(request.source, out), route=route)
         except pyreloc.TransferError as error:
-            raise RuntimeError(f"h2d typed dispatch failed: {error}") from error
+            raise RuntimeError(f"{request.direction} typed dispatch failed: {error}") from error
         report = dict(report)
         report["placement_reason"] = request.selected["placement_reason"]
         report["policy"] = request.selected["policy"]

@@ -166,7 +166,12 @@ def test_capability_table():
     excluded = {r["implementation"] for r in cap["excluded"]}
     assert {"cpu_reference", "cpu_stages_cuda_stages@0", "cpu_stages_cuda_stages@1"} <= excluded
     d2h = pyreloc.query_capability(bound, "d2h", "cuda")
-    assert d2h["eligible"] == []
+    assert [r["implementation"] for r in d2h["eligible"]] == \
+        ["b200_fused_d2h", "b200_fused_d2h@dma_ring", "b200_fused_d2h@zero_copy"]
+    # the finished result crosses the link device -> host
+    assert d2h["eligible"][0]["wire_boundary"] == 1 and d2h["eligible"][0]["wire_bytes"] == 2 * 4096
+    assert "b200_fused_h2d" in {r["implementation"] for r in d2h["excluded"]}
+    assert pyreloc.query_capability(bound, "d2h", "host")["eligible"] == []
     with pytest.raises(pyreloc.TransferError) as e:
         pyreloc.prepare_dispatch_template(bound, policy="original_cpu")
     assert e.value.code == "implementation_unavailable"
