@@ -4,17 +4,21 @@
 One step = one model pass: 16 layers x {q, k, v, o, gate, up, down} int8
 [out, in] matrices with per-row f32 scales (lognormal(-5, 0.5)), each
 dequantized, narrowed to f16 (RNE) and transposed to [in, out] on the GPU by
-the fused sm_100a kernel. With N GPUs every rank produces its 1/N row window
-of every matrix (result rows [k*in/N, (k+1)*in/N), i.e. source columns) and an
-in-place NCCL all-gather over NVLink assembles the full f16 layer on every
-GPU; matrix i's all-gather overlaps matrix i+1's fetch.
+the fused sm_100a kernel. With N GPUs (default `--multi peer`) rank k copies
+the contiguous int8 source rows of its shard of every matrix (sized by each
+GPU's measured concurrent PCIe bandwidth, `--balance 1`) into its own HBM,
+and every rank's kernels read all shards -- its peers' over NVLink through
+CUDA IPC mappings -- writing the full f16 layer locally: NVLink carries int8,
+not f16. `--multi allgather`: every rank produces its 1/N window of result
+rows and an in-place NCCL all-gather assembles the layer.
 
 Metric: layers/s of the whole job (every layer assembled on every GPU), with
 relocated GB/s per GPU and its fraction of the measured pinned-memcpy H2D
 ceiling alongside (BASELINE.json metric).
 
-  value : inputs already resident in HBM (int8 sources on each GPU); the
-          timed work is the transform kernels (+ all-gather).
+  value : inputs already resident in HBM (each rank's int8 shards, or the
+          whole int8 matrices with --multi allgather); the timed work is the
+          transform kernels (peer reads over NVLink / the all-gather).
   e2e   : the same through the drop-in C-ABI with HOST pinned sources: each
           rank's window bytes cross PCIe by DMA into the HBM ring inside the
           timed region; one small device->host read of the result per step.
@@ -180,7 +184,9 @@ class Clocks:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def pinned_h2d_gbs(torch, device, nbytes=256 << 20, reps=10):
+def pinned_h2d_gbs(torch, device, nbytes=256 << 20, reps=10, sync=None):
+    """Best-of-``reps`` pinned cudaMemcpyAsync H2D GB/s; with ``sync`` (a
+    barrier), every rank starts each copy together (concurrent bandwidth)."""
     src = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
     dst = torch.empty(nbytes, dtype=torch.uint8, device=device)
     s = torch.cuda.Stream(device)
@@ -189,6 +195,9 @@ def pinned_h2d_gbs(torch, device, nbytes=256 << 20, reps=10):
         for _ in range(3):
             dst.copy_(src, non_blocking=True)
         for _ in range(reps):
+            if sync is not None:
+                s.synchronize()
+                sync()
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record(s)
             dst.copy_(src, non_blocking=True)
@@ -249,14 +258,38 @@ def run_ours(args):
         distinct.append(mats)
     outs = [[torch.empty((m["in"], m["out"]), dtype=torch.float16, device=dev) for m in distinct[0]]
             for _ in range(2)]
-    from sym_b200.workloads import ShardedLayerFetch, shard_bounds
+    from sym_b200.workloads import PeerShardedFetch, ShardedLayerFetch, shard_bounds
 
     rows = [shard_bounds(m["in"], world, rank) for m in distinct[0]]
     sample = torch.empty(32, dtype=torch.float16).pin_memory()
-    fetcher = ShardedLayerFetch(res, local, world, rank, chunk_bytes=args.chunk_bytes, ring_slots=args.ring_slots)
+    # Host->device bandwidth of this rank alone and with every rank copying at
+    # once (the GPUs of one box share the host's memory and PCIe links).
+    alone = pinned_h2d_gbs(torch, dev)
+    concurrent = pinned_h2d_gbs(torch, dev, sync=barrier) if world > 1 else alone
+    peer = world > 1 and args.multi == "peer"
+    weights = None
+    if peer:
+        if args.balance:
+            w = torch.tensor([concurrent], dtype=torch.float64, device=dev)
+            ws = [torch.zeros_like(w) for _ in range(world)]
+            dist.all_gather(ws, w)
+            weights = [float(x.item()) for x in ws]
+        fetcher = PeerShardedFetch(res, local, world, rank, [(m["out"], m["in"]) for m in distinct[0]],
+                                   weights=weights, buffers=len(distinct))
+        for d, mats in enumerate(distinct):
+            fetcher.preload(d, [m["host"] for m in mats])
+        torch.cuda.synchronize(dev)
+        barrier()
+    else:
+        fetcher = ShardedLayerFetch(res, local, world, rank, chunk_bytes=args.chunk_bytes,
+                                    ring_slots=args.ring_slots)
 
     def layer(l, host_source):
-        return fetcher.fetch(distinct[l % len(distinct)], outs[l % 2], host_source)
+        mats = distinct[l % len(distinct)]
+        if peer:
+            hosts = [m["host"] for m in mats] if host_source else None
+            return fetcher.fetch([m["tmpl"] for m in mats], outs[l % 2], l % len(distinct), hosts)
+        return fetcher.fetch(mats, outs[l % 2], host_source)
 
     def step(host_source):
         handles = []
@@ -329,8 +362,8 @@ def run_ours(args):
     # the ncu capture is of the 70B gate launch; other shapes carry no traffic figure
     traffic = GATE_DRAM_BYTES_PER_ELEM * gate_elems if args.config == "c5" else None
 
-    ceiling = pinned_h2d_gbs(torch, dev)
-    ceiling = min(ceiling, max_over_ranks(ceiling)) if world > 1 else ceiling
+    # the ceiling of the slowest rank when all copy at once (the job waits for it)
+    ceiling = -max_over_ranks(-concurrent) if world > 1 else alone
 
     # checksum: size-independent property -- every layer assembled == the
     # same bytes the single-GPU path produces (compared in tests); here the
@@ -361,10 +394,14 @@ def run_ours(args):
         "scaling": "strong", "vs_baseline": None, "dtype": "int8->f16", "data": "synthetic",
         "config": {"workload": workload, "layers_per_step": n_layers,
                    "matrices": {n: [o, i] for n, o, i in shapes}, "distinct_host_layers": args.distinct_layers,
-                   "shard": "result rows [k*in/N,(k+1)*in/N) + in-place NCCL all-gather" if world > 1 else "none",
+                   "shard": ("int8 source rows per rank (weighted by concurrent PCIe bandwidth)" if args.balance
+                             else "int8 source rows per rank, equal") + "; every rank's kernels read all shards "
+                            "(peers' over NVLink, CUDA IPC)" if peer else
+                            "result rows [k*in/N,(k+1)*in/N) + in-place NCCL all-gather" if world > 1 else "none",
+                   "shard_weights": weights,
                    "route": "dma_ring", "ring_slots": args.ring_slots, "chunk_bytes": args.chunk_bytes,
                    "l2": "inputs larger than L2 (855 MB int8 per layer)"},
-        "gbs_per_gpu": gbs_per_gpu, "pinned_h2d_ceiling_gbs": ceiling,
+        "gbs_per_gpu": gbs_per_gpu, "pinned_h2d_ceiling_gbs": ceiling, "pinned_h2d_alone_gbs": alone,
         "pct_of_pinned_memcpy": 100.0 * gbs_per_gpu / ceiling if ceiling else None,
         "e2e": {"value": layers_e2e, "unit": "layers/s", "ms_per_step": 1e3 * t_e2e / args.steps,
                 "h2d_bytes_per_step": int(per_gpu_wire * n_layers), "d2h_bytes_per_step": int(sample.numel() * 2)},
@@ -691,6 +728,11 @@ def main():
     parser.add_argument("--distinct-layers", type=int, default=2)
     parser.add_argument("--chunk-bytes", type=int, default=16 << 20)
     parser.add_argument("--ring-slots", type=int, default=4)
+    parser.add_argument("--multi", default="peer", choices=["peer", "allgather"],
+                        help="N>1: peer (int8 shards read over NVLink by every rank's kernel) or allgather "
+                             "(f16 result rows all-gathered by NCCL)")
+    parser.add_argument("--balance", type=int, default=1,
+                        help="N>1 peer: size shards by each rank's concurrent PCIe bandwidth (1) or equally (0)")
     args = parser.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -164,6 +164,15 @@ std::optional<TransferError> executeWindow(const DispatchTemplate &tmpl, CudaBac
                                            bool hostSource, void *dst, int64_t rowBegin, int64_t rowEnd,
                                            const TransferOptions &options, Report &report);
 
+/// The source-row counterpart of executeWindow: `rows` (device memory of
+/// this GPU, or a peer GPU's mapped into this process) holds source rows
+/// [rowBegin, rowEnd) of the plan's source-outer axis; the transform writes
+/// the result cells those rows produce into the full destination `dst`.
+/// Disjoint row windows, possibly from different GPUs, assemble the result.
+std::optional<TransferError> executeSourceRows(const DispatchTemplate &tmpl, CudaBackend &backend, const void *rows,
+                                               int64_t rowBegin, int64_t rowEnd, void *dst,
+                                               const TransferOptions &options, Report &report);
+
 /// Explicit consumer-sized group (reference Dispatch.h:177-214,
 /// prepareDispatchGroup :213): fresh views per member, one CUDA device, one
 /// caller-stream ordering and one completion for all members. Typed

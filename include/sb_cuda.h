@@ -136,6 +136,13 @@ int sbc_host_register(void *ptr, size_t bytes, int mapped);
 int sbc_host_unregister(void *ptr);
 /* Device address of mapped pinned host memory. */
 int sbc_host_device_pointer(void *host, void **device);
+/* CUDA IPC: the 64-byte handle of the device allocation that contains
+ * `device_ptr` and the pointer's offset in it; the mapping of a peer
+ * process's handle into this process (the allocation's base; peer access
+ * enabled on first use); close unmaps. */
+int sbc_ipc_get_handle(void *device_ptr, unsigned char handle[64], size_t *offset);
+int sbc_ipc_open_handle(const unsigned char handle[64], void **device_ptr);
+int sbc_ipc_close_handle(void *device_ptr);
 /* Where a pointer lives: *kind 0 unregistered host, 1 pinned host, 2 device,
  * 3 managed; *device the owning ordinal (-1 for host). */
 int sbc_pointer_info(const void *ptr, int *kind, int *device);

@@ -126,6 +126,27 @@ int sb_execute_rows(const sb_template *tmpl, sb_resources *resources, int32_t de
                     int32_t host_source, void *dst, int64_t row_begin, int64_t row_end, const sb_options *options,
                     char *report, size_t cap, sb_error *err);
 
+/* The source-row counterpart of sb_execute_rows, for shards that are split
+ * by source rows instead of result rows: `src` is device memory -- this
+ * GPU's, or another GPU's mapped with sb_ipc_open -- holding source rows
+ * [row_begin, row_end) of the plan's source-outer axis (dense, contiguous);
+ * the kernel writes the result cells those rows produce into the full
+ * destination `dst` on `device`. Disjoint windows, read from the GPUs that
+ * hold them, assemble the whole result (the multi-GPU weight fetch reads
+ * its peers' int8 shards over NVLink this way). */
+int sb_execute_source_rows(const sb_template *tmpl, sb_resources *resources, int32_t device, const void *src,
+                           int64_t row_begin, int64_t row_end, void *dst, const sb_options *options, char *report,
+                           size_t cap, sb_error *err);
+
+/* CUDA IPC between the processes of a multi-GPU job (one per GPU): the
+ * 64-byte handle of the device allocation holding `device_ptr` and the
+ * pointer's byte offset in it; the allocation's mapping into this process on
+ * `device` (returns its base: add the offset; peer access enabled); the
+ * unmapping. */
+int sb_ipc_handle(void *device_ptr, uint8_t handle[64], uint64_t *offset, sb_error *err);
+int sb_ipc_open(const uint8_t handle[64], int32_t device, void **device_ptr, sb_error *err);
+int sb_ipc_close(void *device_ptr, sb_error *err);
+
 /* No reference counterpart: a host->device execution of a prepared template
  * that allocates nothing, for callers that cannot call cudaMalloc (code under
  * a caching allocator that owns the device heap, hosts with a fixed device

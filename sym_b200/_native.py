@@ -86,6 +86,11 @@ def lib():
         "sb_execute_rows": (ctypes.c_int, [vp, vp, i32, vp, i32, vp, i64, i64, ctypes.POINTER(SbOptions),
                                            ctypes.c_char_p, sz, ep]),
         "sb_execute_h2d_static": (ctypes.c_int, [vp, vp, vp, vp, ep]),
+        "sb_execute_source_rows": (ctypes.c_int, [vp, vp, i32, vp, i64, i64, vp, ctypes.POINTER(SbOptions),
+                                                  ctypes.c_char_p, sz, ep]),
+        "sb_ipc_handle": (ctypes.c_int, [vp, ctypes.POINTER(ctypes.c_uint8), ctypes.POINTER(u64), ep]),
+        "sb_ipc_open": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint8), i32, pp, ep]),
+        "sb_ipc_close": (ctypes.c_int, [vp, ep]),
         "sb_resources_create": (ctypes.c_int, [u64, u64, ctypes.c_uint32, pp, ep]),
         "sb_resources_stats": (ctypes.c_int, [vp, ctypes.c_char_p, sz]),
         "sb_resources_streams": (ctypes.c_int, [vp, i32, pp, pp, ep]),

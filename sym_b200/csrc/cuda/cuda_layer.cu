@@ -6,6 +6,9 @@
 #include "sb_cuda.h"
 
 #include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <cstring>
 
 namespace {
 cudaStream_t S(void *s) { return static_cast<cudaStream_t>(s); }
@@ -50,6 +53,54 @@ int sbc_host_device_pointer(void *host, void **device) {
     cudaGetLastError(); // an expected probe failure must not poison later launch checks
   return e;
 }
+
+namespace {
+PFN_cuMemGetAddressRange_v3020 address_range() {
+  static PFN_cuMemGetAddressRange_v3020 fn = [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      return reinterpret_cast<PFN_cuMemGetAddressRange_v3020>(p);
+    cudaGetLastError();
+    return static_cast<PFN_cuMemGetAddressRange_v3020>(nullptr);
+  }();
+  return fn;
+}
+} // namespace
+
+int sbc_ipc_get_handle(void *device_ptr, unsigned char handle[64], size_t *offset) {
+  // An IPC handle names a whole allocation; a pointer inside a larger
+  // allocation (a caching allocator's segment) is its base plus an offset.
+  PFN_cuMemGetAddressRange_v3020 range = address_range();
+  if (!range)
+    return cudaErrorNotSupported;
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range(&base, &size, reinterpret_cast<CUdeviceptr>(device_ptr)) != CUDA_SUCCESS)
+    return cudaErrorInvalidDevicePointer;
+  *offset = static_cast<size_t>(reinterpret_cast<CUdeviceptr>(device_ptr) - base);
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void *>(base));
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return e;
+  }
+  static_assert(sizeof(h) == 64, "CUDA IPC handles are 64 bytes");
+  std::memcpy(handle, &h, sizeof(h));
+  return 0;
+}
+
+int sbc_ipc_open_handle(const unsigned char handle[64], void **device_ptr) {
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  const cudaError_t e = cudaIpcOpenMemHandle(device_ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess)
+    cudaGetLastError();
+  return e;
+}
+
+int sbc_ipc_close_handle(void *device_ptr) { return cudaIpcCloseMemHandle(device_ptr); }
 
 int sbc_pointer_info(const void *ptr, int *kind, int *device) {
   cudaPointerAttributes a;

@@ -560,6 +560,54 @@ int sb_execute_rows(const sb_template *t, sb_resources *res, int32_t device, con
   return 0;
 }
 
+int sb_execute_source_rows(const sb_template *t, sb_resources *res, int32_t device, const void *src,
+                           int64_t row_begin, int64_t row_end, void *dst, const sb_options *opts, char *report,
+                           size_t cap, sb_error *err) {
+  const TransferOptions o = toOptions(opts);
+  dispatch::Report rep;
+  rep.implementation = t->t.selection.row.label();
+  rep.policy = t->t.selection.policy;
+  auto fn = [&](CudaBackend &b) {
+    return dispatch::executeSourceRows(t->t, b, src, row_begin, row_end, dst, o, rep);
+  };
+  TransferOutcome out;
+  if (res) {
+    out = res->res.withContext(device, fn);
+  } else {
+    dispatch::Resources local(0, 0, 1);
+    out = local.withContext(device, fn);
+  }
+  putJson(reportJson(rep), report, cap);
+  if (out.error)
+    return setErr(err, out.error->code, out.error->message);
+  return 0;
+}
+
+int sb_ipc_handle(void *device_ptr, uint8_t handle[64], uint64_t *offset, sb_error *err) {
+  size_t off = 0;
+  const int rc = sbc_ipc_get_handle(device_ptr, handle, &off);
+  *offset = off;
+  if (rc)
+    return setErr(err, "backend_failure", std::string("cudaIpcGetMemHandle: ") + sbc_error_string(rc));
+  return 0;
+}
+
+int sb_ipc_open(const uint8_t handle[64], int32_t device, void **device_ptr, sb_error *err) {
+  int rc = sbc_set_device(device);
+  if (!rc)
+    rc = sbc_ipc_open_handle(handle, device_ptr);
+  if (rc)
+    return setErr(err, "backend_failure", std::string("cudaIpcOpenMemHandle: ") + sbc_error_string(rc));
+  return 0;
+}
+
+int sb_ipc_close(void *device_ptr, sb_error *err) {
+  const int rc = sbc_ipc_close_handle(device_ptr);
+  if (rc)
+    return setErr(err, "backend_failure", std::string("cudaIpcCloseMemHandle: ") + sbc_error_string(rc));
+  return 0;
+}
+
 int sb_execute_h2d_static(const sb_template *t, const void *source, void *destination, void *stream,
                           sb_error *err) {
   if (!t->t.lowered)

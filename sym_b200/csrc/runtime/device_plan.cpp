@@ -458,6 +458,33 @@ std::optional<TransferError> runD2H(const Lowered &l, CudaBackend &b, const void
   return std::nullopt;
 }
 
+std::optional<TransferError> runSourceRows(const Lowered &l, CudaBackend &b, const void *rows, int64_t rowBegin,
+                                           int64_t rowEnd, void *ddst, RunStats &st) {
+  if (!l.rowsChunkable || l.srcOuter < 0)
+    return terr("invalid_options", "the plan's source has no row axis (rows are not contiguous blocks)");
+  const int ax = l.srcOuter;
+  const int64_t E = l.desc.extents[ax], lo = l.desc.pad_lo[ax];
+  if (rowBegin < 0 || rowEnd > E || rowEnd <= rowBegin)
+    return terr("invalid_options", "source rows [" + std::to_string(rowBegin) + ", " + std::to_string(rowEnd) +
+                                       ") outside [0, " + std::to_string(E) + ")");
+  if (l.desc.has_fill && !l.denseCover)
+    return terr("invalid_options", "source-row windows need a destination the result box covers densely");
+  sbc_relocate d = l.desc;
+  // the first / last window also produces the pad rows before / after it
+  d.box_lo[ax] = rowBegin == 0 ? 0 : lo + rowBegin;
+  d.box_hi[ax] = rowEnd == E ? l.padded[ax] : lo + rowEnd;
+  if (auto e = uploadParams(l, b, d))
+    return e;
+  if (auto e = zeroStatus(l, b, d))
+    return e;
+  d.src = rows;
+  d.src_offset = rowBegin * l.desc.src_strides[ax];
+  d.dst = ddst;
+  st.kernel = familyName(l.family);
+  st.route = "device";
+  return launch(l, b, d, st);
+}
+
 Route chooseRoute(const Lowered &l, CudaBackend &b, const void *hsrc, const TransferOptions &o) {
   if (o.route != Route::Auto)
     return o.route;

@@ -82,6 +82,14 @@ std::optional<TransferError> runH2D(const Lowered &l, CudaBackend &b, const void
 std::optional<TransferError> runD2H(const Lowered &l, CudaBackend &b, const void *dsrc, void *hdst, Route route,
                                     const TransferOptions &options, RunStats &stats);
 
+/// A window of source rows (the plan's source-outer axis) held in device
+/// memory -- this GPU's or a peer's through an IPC mapping: `rows` points at
+/// source row `rowBegin`; the kernel writes exactly the result cells rows
+/// [rowBegin, rowEnd) produce (plus the pad rows before the first / after
+/// the last row) into the full destination `ddst`.
+std::optional<TransferError> runSourceRows(const Lowered &l, CudaBackend &b, const void *rows, int64_t rowBegin,
+                                           int64_t rowEnd, void *ddst, RunStats &stats);
+
 /// Route::Auto for a device-to-host execution: the DMA ring when the result
 /// splits into row chunks, else zero copy into pinned memory, else staged.
 Route chooseRouteD2H(const Lowered &l, void *hdst, const TransferOptions &options);

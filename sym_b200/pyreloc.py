@@ -424,6 +424,58 @@ def execute_rows(prepared: DispatchTemplate, source_ptr: int, destination_ptr: i
     return MappingProxyType(report)
 
 
+def execute_source_rows(prepared: DispatchTemplate, source_ptr: int, row_begin: int, row_end: int,
+                        destination_ptr: int, *, device: int, resources=None, caller_stream=None,
+                        async_completion=False):
+    """Transform a window of source rows held in device memory (this GPU's or
+    a peer's mapped with ``ipc_open``) into the full destination: the window
+    ``[row_begin, row_end)`` of the plan's source-outer axis starts at
+    ``source_ptr``; only the result cells those rows produce are written."""
+    opts = _options(4, "auto", 0, caller_stream, async_completion)
+    err = SbError()
+    buf = ctypes.create_string_buffer(8192)
+    rc = _native.lib().sb_execute_source_rows(prepared.ptr, resources.handle if resources is not None else None,
+                                              int(device), ctypes.c_void_p(int(source_ptr)), int(row_begin),
+                                              int(row_end), ctypes.c_void_p(int(destination_ptr)),
+                                              ctypes.byref(opts), buf, 8192, ctypes.byref(err))
+    import json
+
+    report = json.loads(buf.value.decode())
+    if rc:
+        _raise_transfer(err)
+    return MappingProxyType(report)
+
+
+def ipc_handle(device_ptr: int):
+    """``(handle, offset)``: the 64-byte CUDA IPC handle of the allocation
+    holding ``device_ptr`` and the pointer's byte offset in it."""
+    h = (ctypes.c_uint8 * 64)()
+    off = ctypes.c_uint64()
+    err = SbError()
+    if _native.lib().sb_ipc_handle(ctypes.c_void_p(int(device_ptr)), h, ctypes.byref(off), ctypes.byref(err)):
+        _raise_transfer(err)
+    return bytes(h), int(off.value)
+
+
+def ipc_open(handle: bytes, device: int) -> int:
+    """Map another process's allocation (its IPC handle) on ``device``;
+    returns the allocation's base (add the offset from ``ipc_handle``)."""
+    if len(handle) != 64:
+        raise ValueError("CUDA IPC handles are 64 bytes")
+    h = (ctypes.c_uint8 * 64).from_buffer_copy(handle)
+    out = ctypes.c_void_p()
+    err = SbError()
+    if _native.lib().sb_ipc_open(h, int(device), ctypes.byref(out), ctypes.byref(err)):
+        _raise_transfer(err)
+    return int(out.value)
+
+
+def ipc_close(device_ptr: int):
+    err = SbError()
+    if _native.lib().sb_ipc_close(ctypes.c_void_p(int(device_ptr)), ctypes.byref(err)):
+        _raise_transfer(err)
+
+
 def execute_h2d_static(prepared: DispatchTemplate, source_ptr: int, destination_ptr: int, stream=None):
     """Host -> device execution that allocates nothing, for callers that cannot
     allocate device memory: staging and parameters live in a statically

@@ -285,3 +285,146 @@ class ShardedLayerFetch:
                 handles.append(dist.all_gather_into_tensor(out.view(-1), shard.reshape(-1), group=self.group,
                                                            async_op=True))
         return handles
+
+
+def weighted_row_bounds(rows: int, weights, align: int = 64):
+    """Split ``rows`` into contiguous per-rank ranges proportional to
+    ``weights`` (e.g. each rank's measured concurrent host-to-device
+    bandwidth), on multiples of ``align`` rows where the extent allows.
+    Returns ``[b_0 = 0, b_1, ..., b_N = rows]``."""
+    n = len(weights)
+    if n == 0 or any(w <= 0 for w in weights):
+        raise ValueError("weights must be positive")
+    unit = align if rows % align == 0 and rows // align >= n else 1
+    units = rows // unit
+    total = float(sum(weights))
+    bounds, acc = [0], 0.0
+    for w in weights[:-1]:
+        acc += w
+        bounds.append(max(bounds[-1], min(units, round(units * acc / total))))
+    bounds.append(units)
+    return [b * unit for b in bounds]
+
+
+class PeerShardedFetch:
+    """Multi-GPU weight fetch that moves int8 over NVLink (config 5, the
+    B200 path): rank ``k`` copies the contiguous int8 source rows
+    ``[b_k, b_{k+1})`` of every matrix from host memory into its own HBM shard
+    buffer (one DMA), then every rank's fused kernel reads all the shards --
+    its own from HBM, its peers' through CUDA IPC mappings over NVLink -- and
+    writes the full f16 result locally. Compared with gathering finished f16
+    shards, NVLink carries 1 byte per element instead of 2 and no gather
+    buffer is written. Shard sizes may follow per-rank weights (the measured
+    concurrent PCIe bandwidth of each GPU).
+
+    Ordering: per matrix, one 4-byte NCCL all-reduce (on the caller's stream)
+    after this rank's copy says every shard of the matrix has landed; the
+    kernels follow it on that stream. Each rank enters an all-reduce only
+    after all its earlier kernels, so the next copy into a buffer (two layers
+    later, with two buffers) waits for the all-reduce of the layer in between,
+    by which every rank had finished reading it. No kernel waits on another
+    GPU.
+    """
+
+    def __init__(self, resources, device_index, world, rank, shapes, *, weights=None, group=None, buffers=2):
+        import torch
+        import torch.distributed as dist
+
+        self.res, self.device, self.world, self.rank = resources, device_index, world, rank
+        self.group, self.buffers = group, buffers
+        weights = list(weights) if weights is not None else [1.0] * world
+        self.bounds = [weighted_row_bounds(out_f, weights) for out_f, _ in shapes]  # per matrix
+        self.shapes = list(shapes)
+        # arena offsets of every rank's shards: [rank][parity][matrix]
+        self.offsets = []
+        sizes = []
+        for j in range(world):
+            off, per_rank = 0, []
+            for _ in range(buffers):
+                row = []
+                for (out_f, in_f), b in zip(shapes, self.bounds):
+                    row.append(off)
+                    off += -(-((b[j + 1] - b[j]) * in_f) // 256) * 256
+                per_rank.append(row)
+            self.offsets.append(per_rank)
+            sizes.append(max(off, 256))
+        dev = torch.device("cuda", device_index)
+        self.arena = torch.empty(sizes[rank], dtype=torch.uint8, device=dev)
+        handle = pyreloc.ipc_handle(self.arena.data_ptr())
+        handles = [None] * world
+        dist.all_gather_object(handles, handle, group=group)
+        self.bases = []
+        self._mapped = []
+        for j, (h, offset) in enumerate(handles):
+            if j == rank:
+                self.bases.append(self.arena.data_ptr())
+            else:
+                base = pyreloc.ipc_open(h, device_index)
+                self._mapped.append(base)
+                self.bases.append(base + offset)
+        self.copy_stream = torch.cuda.Stream(dev)
+        self._flag = torch.zeros(1, dtype=torch.int32, device=dev)
+        self._landed = [[torch.cuda.Event() for _ in shapes] for _ in range(buffers)]
+        # per matrix: the caller-stream event after its latest all-reduce
+        self._last = [None for _ in shapes]
+
+    def shard(self, parity, m):
+        """(row_begin, row_end, device tensor view) of this rank's shard."""
+        b0, b1 = self.bounds[m][self.rank], self.bounds[m][self.rank + 1]
+        in_f = self.shapes[m][1]
+        off = self.offsets[self.rank][parity][m]
+        return b0, b1, self.arena[off:off + (b1 - b0) * in_f]
+
+    def preload(self, parity, host_mats):
+        """Device-resident mode: copy this rank's rows of every matrix once."""
+        for m, q in enumerate(host_mats):
+            b0, b1, view = self.shard(parity, m)
+            view.copy_(q.reshape(-1)[b0 * self.shapes[m][1]:b1 * self.shapes[m][1]])
+
+    def fetch(self, templates, outputs, parity, host_mats=None):
+        """Enqueue one layer: ``templates[m]`` maps int8 ``[out, in]`` to the
+        full ``outputs[m]``; ``host_mats[m]`` (pinned CPU int8) is copied in
+        first, or None when the shards were preloaded."""
+        import torch
+        import torch.distributed as dist
+
+        caller = torch.cuda.current_stream(self.device)
+        for m, (tmpl, out) in enumerate(zip(templates, outputs)):
+            in_f = self.shapes[m][1]
+            if host_mats is not None:
+                b0, b1, view = self.shard(parity, m)
+                # The previous layer's all-reduce of this matrix was entered by
+                # every rank after all its earlier kernels, including those
+                # that read this buffer two layers ago.
+                if self._last[m] is not None:
+                    self.copy_stream.wait_event(self._last[m])
+                with torch.cuda.stream(self.copy_stream):
+                    view.copy_(host_mats[m].reshape(-1)[b0 * in_f:b1 * in_f], non_blocking=True)
+                    self._landed[parity][m].record(self.copy_stream)
+                caller.wait_event(self._landed[parity][m])
+                if self.world > 1:
+                    work = dist.all_reduce(self._flag, group=self.group, async_op=True)
+                    work.wait()  # the caller stream waits: all shards of matrix m are in HBM
+                ev = torch.cuda.Event()
+                ev.record(caller)
+                self._last[m] = ev
+            for j in range(self.world):
+                r0, r1 = self.bounds[m][j], self.bounds[m][j + 1]
+                if r1 <= r0:
+                    continue
+                src = self.bases[j] + self.offsets[j][parity][m]
+                pyreloc.execute_source_rows(tmpl, src, r0, r1, out.data_ptr(), device=self.device,
+                                            resources=self.res, caller_stream=caller.cuda_stream,
+                                            async_completion=True)
+        return []
+
+    def close(self):
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.synchronize(self.device)
+        if self.world > 1:
+            dist.barrier(group=self.group)  # no peer still reads our arena
+        for ptr in self._mapped:
+            pyreloc.ipc_close(ptr)
+        self._mapped = []

@@ -261,3 +261,30 @@ def test_pageable_source_runs_on_the_gpu():
     out, rep = run_typed_gpu(blob, {"B": 8, "S": 5}, {}, x, route="auto", pinned=False)
     assert np.array_equal(out, expected(blob, {"B": 8, "S": 5}, {}, x))
     assert rep["route"] in ("dma_ring", "staged")
+
+
+@pytest.mark.parametrize("out_f,in_f,cuts", [(512, 1024, [0, 64, 320, 512]), (300, 256, [0, 100, 300]),
+                                             (28672 // 8, 512, [0, 1792, 3584])])
+def test_source_row_windows_assemble_the_result(out_f, in_f, cuts):
+    """Source-row windows held in separate device buffers (as the shards of a
+    multi-GPU fetch are) assemble the exact result, each launch writing only
+    the cells its rows produce (the rest of the destination stays as set)."""
+    import torch
+    from helpers import resources
+    from sym_b200 import pyreloc
+
+    blob = encode(recipe_c4())
+    q, scale = _c4_inputs(out_f, in_f, seed=21)
+    sym = {"out_features": out_f, "in_features": in_f}
+    params = {"scale": ("float32", [out_f], scale.tobytes())}
+    tmpl = pyreloc.prepare_dispatch_template(pyreloc.bind_typed(pyreloc.load_typed_plan(blob), sym, params))
+    out = torch.full((in_f * out_f,), 0x7FFF, dtype=torch.int16, device="cuda")
+    shards = [torch.from_numpy(q[b:e].copy()).cuda() for b, e in zip(cuts, cuts[1:])]
+    for (b, e), shard in zip(zip(cuts, cuts[1:]), shards):
+        rep = pyreloc.execute_source_rows(tmpl, shard.data_ptr(), b, e, out.data_ptr(), device=0,
+                                          resources=resources())
+        assert rep["executed"] and rep["route"] == "device"
+    got = out.view(torch.uint8).cpu().numpy()
+    assert np.array_equal(got, expected(blob, sym, params, q))
+    with pytest.raises(pyreloc.TransferError):
+        pyreloc.execute_source_rows(tmpl, shards[0].data_ptr(), 0, out_f + 1, out.data_ptr(), device=0)

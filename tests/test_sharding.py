@@ -75,3 +75,21 @@ def test_shard_bounds_partition():
             assert bounds[0][0] == 0 and bounds[-1][1] == extent
             assert all(bounds[i][1] == bounds[i + 1][0] for i in range(world - 1))
             assert max(e - b for b, e in bounds) - min(e - b for b, e in bounds) <= 1
+
+
+def test_weighted_row_bounds():
+    """Shard sizes follow the weights, on 64-row multiples where possible, and
+    always tile the rows exactly."""
+    from sym_b200.workloads import weighted_row_bounds
+
+    assert weighted_row_bounds(28672, [1] * 8) == [3584 * k for k in range(9)]
+    b = weighted_row_bounds(28672, [23] * 4 + [35] * 4)
+    assert b[0] == 0 and b[-1] == 28672 and all(x % 64 == 0 for x in b)
+    sizes = [b[i + 1] - b[i] for i in range(8)]
+    assert sizes[0] < sizes[7] and abs(sizes[7] / sizes[0] - 35 / 23) < 0.05
+    assert weighted_row_bounds(100, [1, 1, 1]) == [0, 33, 67, 100]  # no 64-row alignment possible
+    assert weighted_row_bounds(1024, [1, 0.001]) == [0, 1024, 1024]  # a rank may get nothing
+    import pytest
+
+    with pytest.raises(ValueError):
+        weighted_row_bounds(64, [1, 0])
