@@ -184,11 +184,13 @@ class Clocks:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def pinned_h2d_gbs(torch, device, nbytes=256 << 20, reps=10, sync=None):
-    """Best-of-``reps`` pinned cudaMemcpyAsync H2D GB/s; with ``sync`` (a
-    barrier), every rank starts each copy together (concurrent bandwidth)."""
-    src = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
-    dst = torch.empty(nbytes, dtype=torch.uint8, device=device)
+def pinned_h2d_gbs(torch, device, nbytes=256 << 20, reps=10, sync=None, d2h=False):
+    """Best-of-``reps`` pinned cudaMemcpyAsync H2D (or D2H) GB/s; with
+    ``sync`` (a barrier), every rank starts each copy together (concurrent
+    bandwidth)."""
+    host = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    gpu = torch.empty(nbytes, dtype=torch.uint8, device=device)
+    src, dst = (gpu, host) if d2h else (host, gpu)
     s = torch.cuda.Stream(device)
     best = 0.0
     with torch.cuda.stream(s):
@@ -534,6 +536,10 @@ def _config_case(name):
                 "dst_bytes": px * 8, "kernel_bytes": 20 * px, "unit": "images/s", "unit_per_step": 64,
                 "workload": "c2_nchw_to_nhwc_pad4_f16", "shape": [64, 3, 224, 224], "dtype": "f32->f16",
                 "bytes_note": "12 B read + 8 B write per pixel"}
+    if name == "c3q_d2h":  # KV-cache eviction: f32 on the GPU -> int8 in host memory
+        case = _config_case("c3q")
+        case.update(d2h=True, workload="c3q_d2h_quantize_evict")
+        return case
     if name in ("c3q", "c3d"):
         s = 8192
         e = 8 * s * 4096
@@ -616,6 +622,8 @@ def run_config(args):
     else:
         bound = pyreloc.bind_typed(pyreloc.load_typed_plan(case["blob"]), case["symbols"], case["params"])
         tmpl = pyreloc.prepare_dispatch_template(bound, "h2d", "cuda")
+    d2h = bool(case.get("d2h"))
+    tmpl_d2h = pyreloc.prepare_dispatch_template(bound, "d2h", "cuda") if d2h else None
     desc = tmpl.describe()
     rows = desc["padded_rows"]
     host = torch.from_numpy(np.ascontiguousarray(case["src"]).reshape(-1).view(np.uint8)).pin_memory()
@@ -649,9 +657,21 @@ def run_config(args):
     t_kernel = statistics.median(times)
 
     # end to end through the public API: pinned host source -> device result
+    # (d2h: device source -> pinned host result)
     sample = torch.empty(4096, dtype=torch.uint8).pin_memory()
     cur = torch.cuda.current_stream(dev)
-    if case["layout"]:
+    host_out = torch.empty(case["dst_bytes"], dtype=torch.uint8).pin_memory() if d2h else None
+    if d2h:
+        info = bound.describe()
+        sw, dw = WIDTH[info["source_dtype"]], WIDTH[info["result_dtype"]]
+
+        def request():
+            sv = pyreloc.BufferView(dsrc.data_ptr(), dsrc.numel(), 0, info["source_extents"],
+                                    _dense(info["source_extents"]), sw, "cuda", 0)
+            dv = pyreloc.BufferView(host_out.data_ptr(), host_out.numel(), 0, info["result_extents"],
+                                    _dense(info["result_extents"]), dw, "host", -1)
+            return pyreloc.prepare_dispatch_from_template(tmpl_d2h, sv, dv)
+    elif case["layout"]:
         def request():
             sv = pyreloc.BufferView(host.data_ptr(), host.numel(), 0, [host.numel() // 4], [1], 4, "host", -1)
             dv = pyreloc.BufferView(out.data_ptr(), out.numel(), 0, [out.numel() // 4], [1], 4, "cuda", 0)
@@ -669,7 +689,8 @@ def run_config(args):
 
     def e2e_step():
         rep = pyreloc.execute_dispatch(request(), resources=res, caller_stream=cur.cuda_stream)
-        sample.copy_(out[:4096], non_blocking=True)
+        if not d2h:
+            sample.copy_(out[:4096], non_blocking=True)
         return rep
 
     for _ in range(3):
@@ -683,12 +704,13 @@ def run_config(args):
     torch.cuda.synchronize(dev)
     t_e2e = a.elapsed_time(b) * 1e-3 / args.steps
     ck = clocks.stop()
-    ceiling = pinned_h2d_gbs(torch, dev)
+    ceiling = pinned_h2d_gbs(torch, dev, d2h=d2h)
     peaks = _peaks()
     hbm = peaks.get("hbm_gbs") or 6650.0
     achieved = case["kernel_bytes"] / t_kernel / 1e9
     cpu_rate, _, cpu_n = _cpu_config(case, threads)
-    h2d = host.numel()
+    h2d = 0 if d2h else host.numel()
+    wire = case["dst_bytes"] if d2h else h2d  # bytes that cross PCIe per step
     print(json.dumps({
         "metric": f"{case['workload']} {case['unit']}", "value": case["unit_per_step"] / t_kernel,
         "unit": case["unit"], "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
@@ -698,10 +720,10 @@ def run_config(args):
                    "l2": "flushed (256 MB read) before each timed kernel launch; the e2e source crosses PCIe "
                          "every step"},
         "e2e": {"value": case["unit_per_step"] / t_e2e, "unit": case["unit"], "ms_per_step": t_e2e * 1e3,
-                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": sample.numel(),
-                "pct_of_pinned_memcpy": 100.0 * (h2d / t_e2e / 1e9) / ceiling,
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": case["dst_bytes"] if d2h else sample.numel(),
+                "pct_of_pinned_memcpy": 100.0 * (wire / t_e2e / 1e9) / ceiling,
                 "route": rep.get("route"), "implementation": rep.get("implementation")},
-        "pinned_h2d_ceiling_gbs": ceiling,
+        ("pinned_d2h_ceiling_gbs" if d2h else "pinned_h2d_ceiling_gbs"): ceiling,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                      "traffic": None, "peak_source": "measured" if peaks.get("hbm_gbs") else "fallback",
                      "kernel": desc.get("device_kernel"), "bytes_per_launch": case["kernel_bytes"],
@@ -716,7 +738,7 @@ def run_config(args):
 
 def main():
     parser = argparse.ArgumentParser()
-    parser.add_argument("--config", default="c5", choices=["c1", "c2", "c3q", "c3d", "c4", "c5"],
+    parser.add_argument("--config", default="c5", choices=["c1", "c2", "c3q", "c3d", "c3q_d2h", "c4", "c5"],
                         help="c5 (default): the headline Llama-70B fetch; c4: Llama-7B, 32 layers; "
                              "c1-c3d: the other configs on one GPU")
     parser.add_argument("--kernel-case", action="store_true",
