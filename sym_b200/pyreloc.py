@@ -643,7 +643,7 @@ def prepare_dispatch_group(entries):
     return DispatchGroup(out, templates)
 
 
-def _group_call(group, name):
+def _group_call(group):
     if not isinstance(group, DispatchGroup):
         raise TypeError("expected a DispatchGroup")
     if group.consumed or group._executing:
@@ -655,7 +655,7 @@ def execute_dispatch_group(group, *, caller_stream=None, gather_threads=8, gathe
                            device_layout=False, n_buffers=4, chunked_members=False, route="auto", chunk_size=0):
     """Run every member after one wait on ``caller_stream`` and complete once
     (blocking). Host-worker knobs of the reference are accepted and ignored."""
-    _group_call(group, "execute")
+    _group_call(group)
     group._executing = True
     opts = _options(n_buffers, route, chunk_size, caller_stream, False)
     err = SbError()
@@ -724,7 +724,7 @@ def submit_dispatch_group(group, *, caller_stream=None, gather_threads=8, gather
                           min_pinned_bytes=None, max_scratch_bytes=64 << 20, resources=None, owners=None,
                           device_layout=False, n_buffers=4, chunked_members=False, route="auto", chunk_size=0):
     """Enqueue the group and return its ``DispatchCompletion`` without waiting."""
-    _group_call(group, "submit")
+    _group_call(group)
     group._executing = True
     opts = _options(n_buffers, route, chunk_size, caller_stream, True)
     err = SbError()
