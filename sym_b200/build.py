@@ -64,8 +64,10 @@ def build(force: bool = False, verbose: bool = False) -> None:
     LIB_DIR.mkdir(exist_ok=True)
     inc = ["-I", ROOT / "include"]
     if force or _stale(CUDA_LIB, CUDA_SOURCES + HEADERS):
+        # SYM_B200_NVCC_DEFINES: extra -D tuning definitions (e.g. "SBC_TMA_STAGES=8")
+        defines = [f"-D{d}" for d in os.environ.get("SYM_B200_NVCC_DEFINES", "").split() if d]
         cmd = [_nvcc(), *ARCH, "-lineinfo", "-O3", "-std=c++17", "--shared", "-Xcompiler", "-fPIC",
-               "-ccbin", _cxx(), *inc, *CUDA_SOURCES, "-o", CUDA_LIB]
+               "-ccbin", _cxx(), *defines, *inc, *CUDA_SOURCES, "-o", CUDA_LIB]
         _run(cmd, verbose)
     if force or _stale(RUNTIME_LIB, RUNTIME_SOURCES + HEADERS + [CUDA_LIB]):
         cmd = [_cxx(), "-O2", "-std=c++17", "-fPIC", "-shared", "-ffp-contract=off", "-fno-fast-math",

@@ -919,7 +919,15 @@ __global__ void __launch_bounds__(256, 4) k_tile_s8(const __grid_constant__ sbc_
 /// read and cleared by sbc_device_fault.
 __device__ int g_device_fault = 0;
 
-constexpr int KStages = 6;
+// Ring depth and resident CTAs per SM of k_tma_tile (compile-time tuning
+// points; the defaults are the measured best on the gate matrix).
+#ifndef SBC_TMA_STAGES
+#define SBC_TMA_STAGES 6
+#endif
+#ifndef SBC_TMA_CTAS_PER_SM
+#define SBC_TMA_CTAS_PER_SM 3
+#endif
+constexpr int KStages = SBC_TMA_STAGES;
 constexpr int KTmaTileBytes = 64 * 128;
 constexpr int KTmaConsumers = 256;              // warps 0-7
 constexpr int KTmaThreads = KTmaConsumers + 32; // + the producer warp
@@ -992,7 +1000,7 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, i
 /// result) or CH_F16 / CH_BF16, CH_ON = 0, tiles of 32 A x 64 B cells. Both
 /// move one 8 KB box per tile through the same shared-memory layout.
 template <int WS, int CHAIN, int CH_ON>
-__global__ void __launch_bounds__(KTmaThreads, 3) k_tma_tile(const __grid_constant__ CUtensorMap tmap,
+__global__ void __launch_bounds__(KTmaThreads, SBC_TMA_CTAS_PER_SM) k_tma_tile(const __grid_constant__ CUtensorMap tmap,
                                                              const __grid_constant__ sbc_relocate d, TileOrder ord,
                                                              uint32_t tiles) {
   constexpr int TB = 64, VD = 8;
@@ -1514,7 +1522,10 @@ bool basic_ok(const sbc_relocate &d) {
 
 template <int WS, int WD, int CH>
 int launch_narrow(const sbc_relocate &d, int nb, int64_t per_batch, int64_t total, cudaStream_t s) {
-  const unsigned blocks = static_cast<unsigned>(grid_for(total, 256, 8));
+  // One item per thread (the grid-stride loop runs once): every load of the
+  // whole launch is issued in the first waves instead of a capped grid's
+  // threads walking several items each.
+  const unsigned blocks = static_cast<unsigned>((total + 255) / 256);
   const FastDiv pb = make_fastdiv(static_cast<uint32_t>(per_batch));
   const uint32_t n = static_cast<uint32_t>(total);
   switch (nb) {
@@ -1700,7 +1711,7 @@ int sbc_relocate_transpose(const sbc_relocate *desc, void *stream) {
     const int group = tma_32 && chain == CH_COPY ? 4 : 8; // rows per view group, as the kernel's GR
     if (encode_rows3d(&map, base, d.src_width, ext_a, ext_b, d.src_strides[1] * d.src_width, group)) {
       const int64_t tiles_b = ext_b / 64, tiles = (ext_a / tma_ta) * tiles_b;
-      const int64_t cap = static_cast<int64_t>(sm_count()) * 3;
+      const int64_t cap = static_cast<int64_t>(sm_count()) * SBC_TMA_CTAS_PER_SM;
       const unsigned blocks = static_cast<unsigned>(tiles < cap ? tiles : cap);
       TileOrder ord;
       ord.lg = tma_group_log2();
