@@ -920,12 +920,14 @@ __global__ void __launch_bounds__(256, 4) k_tile_s8(const __grid_constant__ sbc_
 __device__ int g_device_fault = 0;
 
 // Ring depth and resident CTAs per SM of k_tma_tile (compile-time tuning
-// points; the defaults are the measured best on the gate matrix).
+// points). Measured on the gate matrix (TB/s): 6 x 3 CTAs 5.00-5.03,
+// 8 x 3 5.00-5.05, 4 x 4 4.92-4.96, 12 x 2 5.08-5.09, 10 x 2 5.08 (default:
+// the same bytes in flight per SM as 12 x 2 with less shared memory).
 #ifndef SBC_TMA_STAGES
-#define SBC_TMA_STAGES 6
+#define SBC_TMA_STAGES 10
 #endif
 #ifndef SBC_TMA_CTAS_PER_SM
-#define SBC_TMA_CTAS_PER_SM 3
+#define SBC_TMA_CTAS_PER_SM 2
 #endif
 constexpr int KStages = SBC_TMA_STAGES;
 constexpr int KTmaTileBytes = 64 * 128;
