@@ -60,10 +60,10 @@ LLAMA7B = [("q", 4096, 4096), ("k", 4096, 4096), ("v", 4096, 4096), ("o", 4096, 
 # --config -> (matrix shapes, layers per step, workload name)
 MODELS = {"c5": (LLAMA70B, LAYERS, "llama70b_int8_fetch"), "c4": (LLAMA7B, 32, "llama7b_int8_fetch")}
 # DRAM bytes (read + write) per element of the gate launch, from one ncu
-# capture of `bench.py --kernel-case`: 235.2 MB + 412.3 MB over 28672 x 8192
+# capture of `bench.py --kernel-case`: 235.3 MB + 412.7 MB over 28672 x 8192
 # elements. Writes sit below the algorithmic 2 B/element because the last
 # dirty lines are still in L2 when the kernel ends.
-GATE_DRAM_BYTES_PER_ELEM = (235.236352e6 + 412.339456e6) / (28672 * 8192)
+GATE_DRAM_BYTES_PER_ELEM = (235.25888e6 + 412.66816e6) / (28672 * 8192)
 
 
 def _peaks():
