@@ -173,6 +173,13 @@ std::optional<TransferError> executeSourceRows(const DispatchTemplate &tmpl, Cud
                                                int64_t rowBegin, int64_t rowEnd, void *dst,
                                                const TransferOptions &options, Report &report);
 
+/// All source rows as `n` blocks (block j at `shards[j]`, rows
+/// [bounds[j], bounds[j + 1])), each in device memory of this GPU or a peer;
+/// the whole result is written to `dst`, in one launch where possible.
+std::optional<TransferError> executeSourceShards(const DispatchTemplate &tmpl, CudaBackend &backend,
+                                                 const void *const *shards, const int64_t *bounds, int n, void *dst,
+                                                 const TransferOptions &options, Report &report);
+
 /// Explicit consumer-sized group (reference Dispatch.h:177-214,
 /// prepareDispatchGroup :213): fresh views per member, one CUDA device, one
 /// caller-stream ordering and one completion for all members. Typed

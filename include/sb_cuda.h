@@ -112,6 +112,15 @@ typedef struct {
 int sbc_relocate_generic(const sbc_relocate *desc, void *stream);
 int sbc_relocate_contiguous(const sbc_relocate *desc, void *stream);
 int sbc_relocate_transpose(const sbc_relocate *desc, void *stream);
+/* One TMA tile launch over `n` (<= 8) separately stored blocks of source
+ * rows: `srcs[j]` holds the rows [row_bounds[j], row_bounds[j+1]) of axis 1
+ * (the source-row axis of a rank-2 transpose; device memory, this GPU's or a
+ * peer's), which together are the box's whole axis-1 range. `desc->src` is
+ * not read. SBC_EUNSUPPORTED when the box or a block does not fit the tile
+ * kernel (each block a multiple of 64 rows, TMA-aligned); the caller then
+ * launches per block. */
+int sbc_relocate_transpose_shards(const sbc_relocate *desc, const void *const *srcs, const int64_t *row_bounds,
+                                  int32_t n, void *stream);
 /* dst[i] = low `width` bytes of `bits`, i in [0, count). */
 int sbc_fill(void *dst, int64_t count, int32_t width, uint64_t bits, void *stream);
 /* Kernels launched by this library since load (instrumentation). */

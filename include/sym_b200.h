@@ -138,6 +138,16 @@ int sb_execute_source_rows(const sb_template *tmpl, sb_resources *resources, int
                            int64_t row_begin, int64_t row_end, void *dst, const sb_options *options, char *report,
                            size_t cap, sb_error *err);
 
+/* All of the source's rows as `n` consecutive blocks, block j at
+ * `srcs[j]` holding rows [row_bounds[j], row_bounds[j+1]) (row_bounds[0] = 0,
+ * row_bounds[n] = the source row count), each in device memory of this GPU or
+ * of a peer (sb_ipc_open): the whole result is written to `dst` on `device`,
+ * in ONE tile launch when the plan is a rank-2 transpose and the blocks fit
+ * the TMA tiles, else one launch per block. */
+int sb_execute_source_shards(const sb_template *tmpl, sb_resources *resources, int32_t device,
+                             const void *const *srcs, const int64_t *row_bounds, int32_t n, void *dst,
+                             const sb_options *options, char *report, size_t cap, sb_error *err);
+
 /* CUDA IPC between the processes of a multi-GPU job (one per GPU): the
  * 64-byte handle of the device allocation holding `device_ptr` and the
  * pointer's byte offset in it; the allocation's mapping into this process on

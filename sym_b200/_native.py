@@ -88,6 +88,8 @@ def lib():
         "sb_execute_h2d_static": (ctypes.c_int, [vp, vp, vp, vp, ep]),
         "sb_execute_source_rows": (ctypes.c_int, [vp, vp, i32, vp, i64, i64, vp, ctypes.POINTER(SbOptions),
                                                   ctypes.c_char_p, sz, ep]),
+        "sb_execute_source_shards": (ctypes.c_int, [vp, vp, i32, ctypes.POINTER(vp), ctypes.POINTER(i64), i32, vp,
+                                                    ctypes.POINTER(SbOptions), ctypes.c_char_p, sz, ep]),
         "sb_ipc_handle": (ctypes.c_int, [vp, ctypes.POINTER(ctypes.c_uint8), ctypes.POINTER(u64), ep]),
         "sb_ipc_open": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint8), i32, pp, ep]),
         "sb_ipc_close": (ctypes.c_int, [vp, ep]),

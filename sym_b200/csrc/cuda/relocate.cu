@@ -997,12 +997,23 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, i
                : "memory");
 }
 
+/// Tensor maps of the sources of one k_tma_tile launch: source j (a block of
+/// consecutive source rows, possibly in another GPU's memory) holds the
+/// b-tiles [tb_first[j], tb_first[j + 1]). One source in the common case;
+/// several when a multi-GPU fetch's shards are read in place.
+constexpr int kMaxTmaSources = 8;
+struct TmaSources {
+  CUtensorMap map[kMaxTmaSources];
+  uint32_t tb_first[kMaxTmaSources + 1];
+  int32_t n;
+};
+
 /// WS = 1: int8 source, CHAIN CH_DQ_F16 / CH_DQ_BF16 (f16/bf16 result), tiles
 /// of 128 A x 64 B cells. WS = 4: 32-bit source, CHAIN CH_COPY (32-bit
 /// result) or CH_F16 / CH_BF16, CH_ON = 0, tiles of 32 A x 64 B cells. Both
 /// move one 8 KB box per tile through the same shared-memory layout.
 template <int WS, int CHAIN, int CH_ON>
-__global__ void __launch_bounds__(KTmaThreads, SBC_TMA_CTAS_PER_SM) k_tma_tile(const __grid_constant__ CUtensorMap tmap,
+__global__ void __launch_bounds__(KTmaThreads, SBC_TMA_CTAS_PER_SM) k_tma_tile(const __grid_constant__ TmaSources srcs,
                                                              const __grid_constant__ sbc_relocate d, TileOrder ord,
                                                              uint32_t tiles) {
   constexpr int TB = 64, VD = 8;
@@ -1051,8 +1062,8 @@ __global__ void __launch_bounds__(KTmaThreads, SBC_TMA_CTAS_PER_SM) k_tma_tile(c
 
   if (t >= KTmaConsumers) { // ---- producer warp
     const int lane = t - KTmaConsumers;
-    if (lane == 0)
-      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap)) : "memory");
+    if (lane < srcs.n)
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&srcs.map[lane])) : "memory");
     // This lane's two parameter columns of a tile, loaded one tile ahead so
     // the global-load latency overlaps the wait for a free stage.
     float p_scale[2], p_bias[2];
@@ -1104,9 +1115,12 @@ __global__ void __launch_bounds__(KTmaThreads, SBC_TMA_CTAS_PER_SM) k_tma_tile(c
       if (lane == 0) {
         uint32_t ta, tb;
         tile_of(job, ord, ta, tb);
+        int j = 0; // the source holding b-tile tb
+        while (j + 1 < srcs.n && tb >= srcs.tb_first[j + 1])
+          ++j;
         mbar_expect_tx(&full[st], KTmaTileBytes); // lane 0's arrival
-        tma_load_3d(stage0 + st * KTmaTileBytes, &tmap, static_cast<int32_t>(ta * TA),
-                    static_cast<int32_t>(tb * (TB / GR)), 0, &full[st]);
+        tma_load_3d(stage0 + st * KTmaTileBytes, &srcs.map[j], static_cast<int32_t>(ta * TA),
+                    static_cast<int32_t>((tb - srcs.tb_first[j]) * (TB / GR)), 0, &full[st]);
       } else {
         mbar_arrive(&full[st]);
       }
@@ -1600,9 +1614,89 @@ int64_t box_count(const sbc_relocate &d) {
   return n;
 }
 
+/// The TMA tile kernel over `n` sources: source j starts at `bases[j]` and
+/// holds `rows[j]` consecutive rows of axis B (the source-row axis), in
+/// order, together the box's whole B extent. SBC_EUNSUPPORTED when the box or
+/// a source does not fit the kernel (the caller uses another kernel).
+int launch_tma(const sbc_relocate &d, int chain, int ch_on, const void *const *bases, const int64_t *rows, int n,
+               cudaStream_t st) {
+  if (d.rank != 2 || n < 1 || n > kMaxTmaSources || !tma_enabled())
+    return SBC_EUNSUPPORTED;
+  const int64_t ext_a = d.box_hi[0] - d.box_lo[0], ext_b = d.box_hi[1] - d.box_lo[1];
+  const bool tma_s8 = d.src_width == 1 && d.dst_width == 2 && (chain == CH_DQ_F16 || chain == CH_DQ_BF16);
+  const bool tma_32 = d.src_width == 4 && ch_on == 0 &&
+                      ((chain == CH_COPY && d.dst_width == 4) ||
+                       ((chain == CH_F16 || chain == CH_BF16) && d.dst_width == 2));
+  const int64_t tma_ta = 128 / d.src_width;
+  if (ch_on < 0 || !(tma_s8 || tma_32) || ext_a % tma_ta || ext_b % 64 ||
+      (ext_a / tma_ta) * (ext_b / 64) >= (int64_t(1) << 31))
+    return SBC_EUNSUPPORTED;
+  const int group = tma_32 && chain == CH_COPY ? 4 : 8; // rows per view group, as the kernel's GR
+  TmaSources srcs{};
+  srcs.n = n;
+  int64_t covered = 0;
+  for (int j = 0; j < n; ++j) {
+    if (rows[j] <= 0 || rows[j] % 64)
+      return SBC_EUNSUPPORTED;
+    srcs.tb_first[j] = static_cast<uint32_t>(covered / 64);
+    if (!encode_rows3d(&srcs.map[j], bases[j], d.src_width, ext_a, rows[j], d.src_strides[1] * d.src_width,
+                       group))
+      return SBC_EUNSUPPORTED;
+    covered += rows[j];
+  }
+  if (covered != ext_b)
+    return SBC_EUNSUPPORTED;
+  const int64_t tiles_b = ext_b / 64, tiles = (ext_a / tma_ta) * tiles_b;
+  srcs.tb_first[n] = static_cast<uint32_t>(tiles_b);
+  const int64_t cap = static_cast<int64_t>(sm_count()) * SBC_TMA_CTAS_PER_SM;
+  const unsigned blocks = static_cast<unsigned>(tiles < cap ? tiles : cap);
+  TileOrder ord;
+  ord.lg = tma_group_log2();
+  while (ord.lg > 0 && (ext_a / tma_ta) % (int64_t(1) << ord.lg))
+    --ord.lg;
+  ord.group = make_fastdiv(static_cast<uint32_t>(tiles_b << ord.lg));
+  const size_t smem = KStages * KTmaTileBytes + 1024;
+  const uint32_t nt = static_cast<uint32_t>(tiles);
+#define SBC_TMA(WS_, CH_, ON_)                                                                                 \
+  (cudaFuncSetAttribute(k_tma_tile<WS_, CH_, ON_>, cudaFuncAttributeMaxDynamicSharedMemorySize,                    \
+                        static_cast<int>(smem)),                                                                 \
+   k_tma_tile<WS_, CH_, ON_><<<blocks, KTmaThreads, smem, st>>>(srcs, d, ord, nt))
+  if (tma_32)
+    chain == CH_COPY ? SBC_TMA(4, CH_COPY, 0) : chain == CH_F16 ? SBC_TMA(4, CH_F16, 0) : SBC_TMA(4, CH_BF16, 0);
+  else if (chain == CH_DQ_F16)
+    ch_on == 0 ? SBC_TMA(1, CH_DQ_F16, 0) : ch_on == 1 ? SBC_TMA(1, CH_DQ_F16, 1) : SBC_TMA(1, CH_DQ_F16, 2);
+  else
+    ch_on == 0 ? SBC_TMA(1, CH_DQ_BF16, 0) : ch_on == 1 ? SBC_TMA(1, CH_DQ_BF16, 1) : SBC_TMA(1, CH_DQ_BF16, 2);
+#undef SBC_TMA
+  return launched(cudaSuccess);
+}
+
 } // namespace
 
 extern "C" {
+
+int sbc_relocate_transpose_shards(const sbc_relocate *desc, const void *const *srcs, const int64_t *row_bounds,
+                                  int32_t n, void *stream) {
+  if (!desc || !basic_ok(*desc) || !srcs || !row_bounds || n < 1)
+    return SBC_EINVAL;
+  const sbc_relocate &d = *desc;
+  if (d.rank != 2 || d.src_strides[0] != 1 || d.dst_strides[1] != 1 || n > kMaxTmaSources)
+    return SBC_EUNSUPPORTED;
+  const int chain = chain_of(d);
+  if (!chain_channels_ok(d, chain, true))
+    return SBC_EUNSUPPORTED;
+  // the shards tile the box's source rows exactly
+  if (row_bounds[0] != d.box_lo[1] - d.pad_lo[1] || row_bounds[n] != d.box_hi[1] - d.pad_lo[1])
+    return SBC_EUNSUPPORTED;
+  int64_t rows[kMaxTmaSources];
+  for (int j = 0; j < n; ++j)
+    rows[j] = row_bounds[j + 1] - row_bounds[j];
+  // the eligibility checks see the first block as the source
+  sbc_relocate e = d;
+  e.src = srcs[0];
+  e.src_offset = row_bounds[0] * d.src_strides[1];
+  return launch_tma(e, chain, tile_eligible(e), srcs, rows, n, static_cast<cudaStream_t>(stream));
+}
 
 int sbc_relocate_generic(const sbc_relocate *desc, void *stream) {
   if (!desc || !basic_ok(*desc))
@@ -1699,43 +1793,12 @@ int sbc_relocate_transpose(const sbc_relocate *desc, void *stream) {
   }
   const int ch_on = tile_eligible(d);
   const bool dq = chain == CH_DQ || chain == CH_DQ_F16 || chain == CH_DQ_BF16;
-  // TMA tiles: int8 -> f16/bf16 dequantize, or 32-bit copy / narrowing cast
-  const bool tma_s8 = d.src_width == 1 && d.dst_width == 2 && (chain == CH_DQ_F16 || chain == CH_DQ_BF16);
-  const bool tma_32 = d.src_width == 4 && ch_on == 0 &&
-                      ((chain == CH_COPY && d.dst_width == 4) ||
-                       ((chain == CH_F16 || chain == CH_BF16) && d.dst_width == 2));
-  const int64_t tma_ta = 128 / d.src_width;
-  if (ch_on >= 0 && d.rank == 2 && (tma_s8 || tma_32) && ext_a % tma_ta == 0 && ext_b % 64 == 0 &&
-      (ext_a / tma_ta) * (ext_b / 64) < (int64_t(1) << 31) && tma_enabled()) {
-    CUtensorMap map;
-    const uint8_t *base = static_cast<const uint8_t *>(d.src) +
-                          (d.box_lo[0] + d.box_lo[1] * d.src_strides[1] - d.src_offset) * d.src_width;
-    const int group = tma_32 && chain == CH_COPY ? 4 : 8; // rows per view group, as the kernel's GR
-    if (encode_rows3d(&map, base, d.src_width, ext_a, ext_b, d.src_strides[1] * d.src_width, group)) {
-      const int64_t tiles_b = ext_b / 64, tiles = (ext_a / tma_ta) * tiles_b;
-      const int64_t cap = static_cast<int64_t>(sm_count()) * SBC_TMA_CTAS_PER_SM;
-      const unsigned blocks = static_cast<unsigned>(tiles < cap ? tiles : cap);
-      TileOrder ord;
-      ord.lg = tma_group_log2();
-      while (ord.lg > 0 && (ext_a / tma_ta) % (int64_t(1) << ord.lg))
-        --ord.lg;
-      ord.group = make_fastdiv(static_cast<uint32_t>(tiles_b << ord.lg));
-      const size_t smem = KStages * KTmaTileBytes + 1024;
-      cudaStream_t st = static_cast<cudaStream_t>(stream);
-      const uint32_t nt = static_cast<uint32_t>(tiles);
-#define SBC_TMA(WS_, CH_, ON_)                                                                                 \
-  (cudaFuncSetAttribute(k_tma_tile<WS_, CH_, ON_>, cudaFuncAttributeMaxDynamicSharedMemorySize,                    \
-                        static_cast<int>(smem)),                                                                 \
-   k_tma_tile<WS_, CH_, ON_><<<blocks, KTmaThreads, smem, st>>>(map, d, ord, nt))
-      if (tma_32)
-        chain == CH_COPY ? SBC_TMA(4, CH_COPY, 0) : chain == CH_F16 ? SBC_TMA(4, CH_F16, 0) : SBC_TMA(4, CH_BF16, 0);
-      else if (chain == CH_DQ_F16)
-        ch_on == 0 ? SBC_TMA(1, CH_DQ_F16, 0) : ch_on == 1 ? SBC_TMA(1, CH_DQ_F16, 1) : SBC_TMA(1, CH_DQ_F16, 2);
-      else
-        ch_on == 0 ? SBC_TMA(1, CH_DQ_BF16, 0) : ch_on == 1 ? SBC_TMA(1, CH_DQ_BF16, 1) : SBC_TMA(1, CH_DQ_BF16, 2);
-#undef SBC_TMA
-      return launched(cudaSuccess);
-    }
+  {
+    const void *base = static_cast<const uint8_t *>(d.src) +
+                       (d.box_lo[0] + d.box_lo[1] * d.src_strides[1] - d.src_offset) * d.src_width;
+    const int rc = launch_tma(d, chain, ch_on, &base, &ext_b, 1, static_cast<cudaStream_t>(stream));
+    if (rc != SBC_EUNSUPPORTED)
+      return rc;
   }
   if (ch_on >= 0 && dq && d.src_width == 1 && ext_a >= 128 && ext_b * d.dst_width >= 128 &&
       ((ext_a + 127) / 128) * ((ext_b * d.dst_width + 127) / 128) * nbatch < (int64_t(1) << 31)) {

@@ -583,6 +583,29 @@ int sb_execute_source_rows(const sb_template *t, sb_resources *res, int32_t devi
   return 0;
 }
 
+int sb_execute_source_shards(const sb_template *t, sb_resources *res, int32_t device, const void *const *srcs,
+                             const int64_t *row_bounds, int32_t n, void *dst, const sb_options *opts, char *report,
+                             size_t cap, sb_error *err) {
+  const TransferOptions o = toOptions(opts);
+  dispatch::Report rep;
+  rep.implementation = t->t.selection.row.label();
+  rep.policy = t->t.selection.policy;
+  auto fn = [&](CudaBackend &b) {
+    return dispatch::executeSourceShards(t->t, b, srcs, row_bounds, n, dst, o, rep);
+  };
+  TransferOutcome out;
+  if (res) {
+    out = res->res.withContext(device, fn);
+  } else {
+    dispatch::Resources local(0, 0, 1);
+    out = local.withContext(device, fn);
+  }
+  putJson(reportJson(rep), report, cap);
+  if (out.error)
+    return setErr(err, out.error->code, out.error->message);
+  return 0;
+}
+
 int sb_ipc_handle(void *device_ptr, uint8_t handle[64], uint64_t *offset, sb_error *err) {
   size_t off = 0;
   const int rc = sbc_ipc_get_handle(device_ptr, handle, &off);

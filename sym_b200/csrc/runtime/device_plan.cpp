@@ -485,6 +485,56 @@ std::optional<TransferError> runSourceRows(const Lowered &l, CudaBackend &b, con
   return launch(l, b, d, st);
 }
 
+std::optional<TransferError> runSourceShards(const Lowered &l, CudaBackend &b, const void *const *shards,
+                                             const int64_t *bounds, int n, void *ddst, RunStats &st) {
+  if (!l.rowsChunkable || l.srcOuter < 0)
+    return terr("invalid_options", "the plan's source has no row axis (rows are not contiguous blocks)");
+  if (n < 1)
+    return terr("invalid_options", "no source shards");
+  const int64_t E = l.desc.extents[l.srcOuter];
+  if (bounds[0] != 0 || bounds[n] != E)
+    return terr("invalid_options", "source shards must cover rows [0, " + std::to_string(E) + ")");
+  for (int j = 0; j < n; ++j)
+    if (bounds[j + 1] < bounds[j])
+      return terr("invalid_options", "source shard bounds must not decrease");
+  // One tile launch over all shards when the plan is a rank-2 transpose whose
+  // source rows are axis 1 and the shards fit the TMA tiles.
+  if (l.family == Family::Transpose && l.desc.rank == 2 && l.srcOuter == 1 && n <= 8) {
+    std::vector<const void *> srcs;
+    std::vector<int64_t> rb;
+    for (int j = 0; j < n; ++j)
+      if (bounds[j + 1] > bounds[j]) {
+        srcs.push_back(shards[j]);
+        rb.push_back(bounds[j]);
+      }
+    rb.push_back(E);
+    sbc_relocate d = l.desc;
+    if (auto e = uploadParams(l, b, d))
+      return e;
+    if (auto e = zeroStatus(l, b, d))
+      return e;
+    d.dst = ddst;
+    const int rc = sbc_relocate_transpose_shards(&d, srcs.data(), rb.data(), static_cast<int32_t>(srcs.size()),
+                                                 b.computeStream());
+    if (rc == 0) {
+      ++st.launches;
+      ++b.kernelLaunches;
+      st.kernel = familyName(l.family);
+      st.route = "device";
+      return std::nullopt;
+    }
+    if (rc != SBC_EUNSUPPORTED) {
+      b.fail("tile kernel over shards", rc);
+      return terr("backend_failure", b.error());
+    }
+  }
+  for (int j = 0; j < n; ++j)
+    if (bounds[j + 1] > bounds[j])
+      if (auto e = runSourceRows(l, b, shards[j], bounds[j], bounds[j + 1], ddst, st))
+        return e;
+  return std::nullopt;
+}
+
 Route chooseRoute(const Lowered &l, CudaBackend &b, const void *hsrc, const TransferOptions &o) {
   if (o.route != Route::Auto)
     return o.route;

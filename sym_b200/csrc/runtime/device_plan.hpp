@@ -90,6 +90,14 @@ std::optional<TransferError> runD2H(const Lowered &l, CudaBackend &b, const void
 std::optional<TransferError> runSourceRows(const Lowered &l, CudaBackend &b, const void *rows, int64_t rowBegin,
                                            int64_t rowEnd, void *ddst, RunStats &stats);
 
+/// All of a plan's source rows, held as `n` consecutive blocks in device
+/// memory (this GPU's or peers'): block j is `shards[j]` with rows
+/// [bounds[j], bounds[j + 1]); bounds[0] = 0 and bounds[n] = the row count.
+/// One tile launch reads every block when the plan and the blocks fit the
+/// TMA tile kernel, else one launch per block.
+std::optional<TransferError> runSourceShards(const Lowered &l, CudaBackend &b, const void *const *shards,
+                                             const int64_t *bounds, int n, void *ddst, RunStats &stats);
+
 /// Route::Auto for a device-to-host execution: the DMA ring when the result
 /// splits into row chunks, else zero copy into pinned memory, else staged.
 Route chooseRouteD2H(const Lowered &l, void *hdst, const TransferOptions &options);

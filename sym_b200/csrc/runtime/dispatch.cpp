@@ -340,6 +340,30 @@ std::optional<TransferError> executeSourceRows(const DispatchTemplate &t, CudaBa
   return finish(t.lowered->needsStatus, t.lowered->classKey, b, o, false, Route::Auto, 0);
 }
 
+std::optional<TransferError> executeSourceShards(const DispatchTemplate &t, CudaBackend &b,
+                                                 const void *const *shards, const int64_t *bounds, int n, void *dst,
+                                                 const TransferOptions &o, Report &rep) {
+  if (!t.lowered)
+    return terr("implementation_unavailable", "template has no lowered program");
+  if (b.failed())
+    return terr("backend_failure", b.error());
+  if (!b.activate())
+    return terr("backend_failure", b.error());
+  if (o.hasCallerStream && !b.waitStream(o.callerStream))
+    return terr("backend_failure", b.error());
+  b200::RunStats st;
+  const uint64_t launches0 = b.kernelLaunches;
+  if (auto e = b200::runSourceShards(*t.lowered, b, shards, bounds, n, dst, st))
+    return e;
+  rep.executed = true;
+  rep.route = st.route;
+  rep.deviceKernel = st.kernel;
+  rep.kernelLaunches = b.kernelLaunches - launches0;
+  rep.sourceBytes = t.program.plan.sourceBytes;
+  rep.destinationBytes = t.program.plan.destinationBytes;
+  return finish(t.lowered->needsStatus, t.lowered->classKey, b, o, false, Route::Auto, 0);
+}
+
 std::variant<GroupRequest, TransferError> prepareDispatchGroup(const std::vector<GroupEntry> &entries) {
   if (entries.empty() || entries.size() > 256)
     return terr("invalid_options", "a group must contain between 1 and 256 members");

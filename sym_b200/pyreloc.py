@@ -446,6 +446,31 @@ def execute_source_rows(prepared: DispatchTemplate, source_ptr: int, row_begin: 
     return MappingProxyType(report)
 
 
+def execute_source_shards(prepared: DispatchTemplate, source_ptrs, row_bounds, destination_ptr: int, *,
+                          device: int, resources=None, caller_stream=None, async_completion=False):
+    """All source rows as consecutive blocks in device memory (this GPU's or
+    peers'): block j at ``source_ptrs[j]`` holds rows
+    ``[row_bounds[j], row_bounds[j + 1])``; writes the whole result to
+    ``destination_ptr``, in one tile launch where the plan allows."""
+    n = len(source_ptrs)
+    if len(row_bounds) != n + 1:
+        raise ValueError("row_bounds needs one more entry than source_ptrs")
+    ptrs = (ctypes.c_void_p * n)(*[int(p) for p in source_ptrs])
+    bounds = (ctypes.c_int64 * (n + 1))(*[int(b) for b in row_bounds])
+    opts = _options(4, "auto", 0, caller_stream, async_completion)
+    err = SbError()
+    buf = ctypes.create_string_buffer(8192)
+    rc = _native.lib().sb_execute_source_shards(prepared.ptr, resources.handle if resources is not None else None,
+                                                int(device), ptrs, bounds, n, ctypes.c_void_p(int(destination_ptr)),
+                                                ctypes.byref(opts), buf, 8192, ctypes.byref(err))
+    import json
+
+    report = json.loads(buf.value.decode())
+    if rc:
+        _raise_transfer(err)
+    return MappingProxyType(report)
+
+
 def ipc_handle(device_ptr: int):
     """``(handle, offset)``: the 64-byte CUDA IPC handle of the allocation
     holding ``device_ptr`` and the pointer's byte offset in it."""

@@ -408,14 +408,10 @@ class PeerShardedFetch:
                 ev = torch.cuda.Event()
                 ev.record(caller)
                 self._last[m] = ev
-            for j in range(self.world):
-                r0, r1 = self.bounds[m][j], self.bounds[m][j + 1]
-                if r1 <= r0:
-                    continue
-                src = self.bases[j] + self.offsets[j][parity][m]
-                pyreloc.execute_source_rows(tmpl, src, r0, r1, out.data_ptr(), device=self.device,
-                                            resources=self.res, caller_stream=caller.cuda_stream,
-                                            async_completion=True)
+            # one call (one tile launch where the shapes allow) reads every shard
+            pyreloc.execute_source_shards(tmpl, [self.bases[j] + self.offsets[j][parity][m] for j in range(self.world)],
+                                          self.bounds[m], out.data_ptr(), device=self.device, resources=self.res,
+                                          caller_stream=caller.cuda_stream, async_completion=True)
         return []
 
     def close(self):

@@ -288,3 +288,32 @@ def test_source_row_windows_assemble_the_result(out_f, in_f, cuts):
     assert np.array_equal(got, expected(blob, sym, params, q))
     with pytest.raises(pyreloc.TransferError):
         pyreloc.execute_source_rows(tmpl, shards[0].data_ptr(), 0, out_f + 1, out.data_ptr(), device=0)
+
+
+@pytest.mark.parametrize("out_f,in_f,cuts,launches", [
+    (512, 1024, [0, 64, 320, 512], 1),          # TMA tiles: one launch over all blocks
+    (3584 * 2, 512, [0, 2816, 5696, 7168], 1),  # uneven 64-row blocks
+    (300, 256, [0, 100, 300], 2),                # not 64-row blocks: one launch per block
+    (256, 512, [0, 128, 128, 256], 1),           # an empty block
+])
+def test_source_shards_one_launch(out_f, in_f, cuts, launches):
+    """All source rows as separately stored blocks (a multi-GPU fetch's
+    shards) produce the exact result through one call."""
+    import torch
+    from helpers import resources
+    from sym_b200 import pyreloc
+
+    blob = encode(recipe_c4())
+    q, scale = _c4_inputs(out_f, in_f, seed=23)
+    sym = {"out_features": out_f, "in_features": in_f}
+    params = {"scale": ("float32", [out_f], scale.tobytes())}
+    tmpl = pyreloc.prepare_dispatch_template(pyreloc.bind_typed(pyreloc.load_typed_plan(blob), sym, params))
+    out = torch.empty(in_f * out_f * 2, dtype=torch.uint8, device="cuda")
+    shards = [torch.from_numpy(q[b:e].copy()).cuda() if e > b else torch.empty(16, dtype=torch.int8, device="cuda")
+              for b, e in zip(cuts, cuts[1:])]
+    rep = pyreloc.execute_source_shards(tmpl, [s.data_ptr() for s in shards], cuts, out.data_ptr(), device=0,
+                                        resources=resources())
+    assert rep["kernel_launches"] == launches
+    assert np.array_equal(out.cpu().numpy(), expected(blob, sym, params, q))
+    with pytest.raises(pyreloc.TransferError):
+        pyreloc.execute_source_shards(tmpl, [shards[0].data_ptr()], [0, out_f - 1], out.data_ptr(), device=0)
