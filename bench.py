@@ -284,7 +284,7 @@ def run_ours(args):
         barrier()
     else:
         fetcher = ShardedLayerFetch(res, local, world, rank, chunk_bytes=args.chunk_bytes,
-                                    ring_slots=args.ring_slots)
+                                    ring_slots=args.ring_slots, route=args.route)
 
     def layer(l, host_source):
         mats = distinct[l % len(distinct)]
@@ -401,7 +401,7 @@ def run_ours(args):
                             "(peers' over NVLink, CUDA IPC)" if peer else
                             "result rows [k*in/N,(k+1)*in/N) + in-place NCCL all-gather" if world > 1 else "none",
                    "shard_weights": weights,
-                   "route": "dma_ring", "ring_slots": args.ring_slots, "chunk_bytes": args.chunk_bytes,
+                   "route": args.route, "ring_slots": args.ring_slots, "chunk_bytes": args.chunk_bytes,
                    "l2": "inputs larger than L2 (855 MB int8 per layer)"},
         "gbs_per_gpu": gbs_per_gpu, "pinned_h2d_ceiling_gbs": ceiling, "pinned_h2d_alone_gbs": alone,
         "pct_of_pinned_memcpy": 100.0 * gbs_per_gpu / ceiling if ceiling else None,
@@ -750,6 +750,8 @@ def main():
     parser.add_argument("--distinct-layers", type=int, default=2)
     parser.add_argument("--chunk-bytes", type=int, default=16 << 20)
     parser.add_argument("--ring-slots", type=int, default=4)
+    parser.add_argument("--route", default="dma_ring", choices=["dma_ring", "zero_copy"],
+                        help="host-source route of the result-row fetch (N=1 and --multi allgather)")
     parser.add_argument("--multi", default="peer", choices=["peer", "allgather"],
                         help="N>1: peer (int8 shards read over NVLink by every rank's kernel) or allgather "
                              "(f16 result rows all-gathered by NCCL)")

@@ -258,11 +258,11 @@ class ShardedLayerFetch:
     """
 
     def __init__(self, resources, device_index, world=1, rank=0, group=None, chunk_bytes=16 << 20,
-                 ring_slots=4):
+                 ring_slots=4, route="dma_ring"):
         self.res = resources
         self.device = device_index
         self.world, self.rank, self.group = world, rank, group
-        self.chunk_bytes, self.ring_slots = chunk_bytes, ring_slots
+        self.chunk_bytes, self.ring_slots, self.route = chunk_bytes, ring_slots, route
 
     def fetch(self, mats, outputs, host_source=True):
         """Enqueue every matrix (and its all-gather); returns collective handles."""
@@ -279,7 +279,7 @@ class ShardedLayerFetch:
             src = m["host"] if host_source else m["dev"]
             pyreloc.execute_rows(m["tmpl"], src.data_ptr(), shard.data_ptr(), b, e, device=self.device,
                                  host_source=host_source, resources=self.res, caller_stream=stream,
-                                 async_completion=True, route="dma_ring", chunk_size=self.chunk_bytes,
+                                 async_completion=True, route=self.route, chunk_size=self.chunk_bytes,
                                  n_buffers=self.ring_slots)
             if self.world > 1:
                 handles.append(dist.all_gather_into_tensor(out.view(-1), shard.reshape(-1), group=self.group,
