@@ -470,21 +470,60 @@ def _collect_symbols(w: _Writer, st: _State, src_shape, dst_extents):
     """Pre-assign the symbol table in first-use order of the wire sections."""
 
 
-def _layout_body(w: _Writer, st: _State, src_shape, src_dtype, dst_extents, dst_dtype, fused_fills):
+def _canonical_layout(st: _State):
+    """The layout in the exporter's canonical form (the reference's
+    PlanCanonicalize.cpp, canonicalizePlan): adjacent axes merge to a fixpoint
+    when they are neighbours in the view order (perm[k+1] == perm[k] + 1),
+    contiguous on the source side (stride_k == stride_{k+1} * extent_{k+1};
+    the row-major destination side then holds too) and neither carries a
+    pad. Returns (axes, perm, pads) with pad axes remapped; the logical
+    result and the value stages keep the unmerged dims."""
+    axes = [(_Axis(a.name, a.extent, a.stride)) for a in st.axes]
+    perm = list(st.perm)
+    pads = [dict(p) for p in st.pads]
+    changed = True
+    while changed:
+        changed = False
+        for k in range(len(axes) - 1):
+            if any(p["axis"] in (k, k + 1) for p in pads):
+                continue
+            if perm[k + 1] != perm[k] + 1:
+                continue
+            if not _equal(axes[k].stride, sx.mul(axes[k + 1].stride, axes[k + 1].extent)):
+                continue
+            axes[k] = _Axis(axes[k].name, sx.mul(axes[k].extent, axes[k + 1].extent), axes[k + 1].stride)
+            del axes[k + 1]
+            removed = perm[k] + 1
+            del perm[k + 1]
+            perm = [v - 1 if v > removed else v for v in perm]
+            for p in pads:
+                if p["axis"] > k:
+                    p["axis"] -= 1
+            changed = True
+            break
+    return axes, perm, pads
+
+
+def _layout_body(w: _Writer, st: _State, src_shape, src_dtype, dst_extents, dst_dtype, fused_fills, canon):
+    axes, perm, pads = canon
+    layout_extents = [a.extent for a in axes]
+    for p in pads:
+        k = p["axis"]
+        layout_extents[k] = sx.add(sx.add(layout_extents[k], p["lo"]), p["hi"])
     w.tensor(src_shape, src_dtype)
-    w.tensor(dst_extents, dst_dtype)
-    w.u32(len(st.perm))
-    for p in st.perm:
+    w.tensor(layout_extents, dst_dtype)
+    w.u32(len(perm))
+    for p in perm:
         w.u32(p)
-    dst_strides = sx.dense_strides(dst_extents)
-    w.u32(len(st.axes))
-    for a, ds in zip(st.axes, dst_strides):
-        w.string(a.name)
+    dst_strides = sx.dense_strides(layout_extents)
+    w.u32(len(axes))
+    for k, (a, ds) in enumerate(zip(axes, dst_strides)):
+        w.string(f"d{k}")  # positional names, as the exporter emits them
         w.expr(a.extent)
         w.expr(a.stride)
         w.expr(ds)
-    w.u32(len(st.pads))
-    for p, bits in zip(sorted(st.pads, key=lambda p: p["axis"]), fused_fills):
+    w.u32(len(pads))
+    for p, bits in zip(sorted(pads, key=lambda p: p["axis"]), fused_fills):
         w.u32(p["axis"])
         w.expr(p["lo"])
         w.expr(p["hi"])
@@ -495,18 +534,20 @@ def _layout_body(w: _Writer, st: _State, src_shape, src_dtype, dst_extents, dst_
         w.expr(e)
         w.i64(d)
     w.u32(0)  # alignment
-    w.u32(len(st.axes))
-    for a in st.axes:
+    w.u32(len(axes))
+    for a in axes:
         w.u8(1 if _const(a.stride) == 1 else 0)
-    symbolic_pad = any(_const(p["lo"]) is None or _const(p["hi"]) is None or _const(st.axes[p["axis"]].extent) is None
-                       for p in st.pads)
+    # a pad's range needs a check at bind time only when its widths are
+    # symbolic (their sign is unknown); the padded extent is built as
+    # extent + lo + hi, so it always matches
+    symbolic_pad = any(_const(p["lo"]) is None or _const(p["hi"]) is None for p in pads)
     w.u8(0)  # no_copy
     w.u8(1 if symbolic_pad else 0)
-    r = len(st.axes)
+    r = len(axes)
     w.u32(r)
     w.u32(r)
     inv = [0] * r
-    for k, p in enumerate(st.perm):
+    for k, p in enumerate(perm):
         inv[p] = k
     for k in range(r):
         w.expr(_Dim(inv[k]))
@@ -552,7 +593,8 @@ def encode(recipe: Recipe) -> bytes:
     if typed:
         body.tensor(src_shape, recipe.source.dtype)
         body.tensor(dst_extents, st.dtype)
-    _layout_body(body, st, src_shape, recipe.source.dtype, dst_extents, st.dtype, fused)
+    canon = _canonical_layout(st)
+    _layout_body(body, st, src_shape, recipe.source.dtype, dst_extents, st.dtype, fused, canon)
     if typed:
         body.u32(len(st.stages))
         for s in st.stages:
@@ -574,9 +616,10 @@ def encode(recipe: Recipe) -> bytes:
                 body.u8(1)
                 body.u32(len(st.axes))
                 body.expr(_Dim(s["channel"]))
+        # fills name the (merged) layout axes; merging keeps the pads' order
         body.u32(len(pads))
-        for p in pads:
-            body.u32(p["axis"])
+        for p, cp in zip(pads, sorted(canon[2], key=lambda p: p["axis"])):
+            body.u32(cp["axis"])
             body.u32(p["stage"])
             body.dtype(p["fill"][0])
             body.u64(p["fill"][1])

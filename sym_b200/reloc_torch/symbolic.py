@@ -97,24 +97,33 @@ def expression(value) -> Expr:
 
 
 def add(lhs, rhs) -> Expr:
+    """``lhs + rhs`` in the plan format's simplified form (the rules of the
+    reference's sym simplifier): constants fold, ``+ 0`` drops, and
+    ``(x + c1) + c2`` becomes ``x + (c1 + c2)``."""
     lhs, rhs = expression(lhs), expression(rhs)
     if isinstance(lhs, Const) and isinstance(rhs, Const):
         return Const(lhs.value + rhs.value)
-    if isinstance(lhs, Const) and lhs.value == 0:
-        return rhs
     if isinstance(rhs, Const) and rhs.value == 0:
         return lhs
+    if isinstance(lhs, Const) and lhs.value == 0:
+        return rhs
+    if isinstance(rhs, Const) and isinstance(lhs, Add) and isinstance(lhs.rhs, Const):
+        return add(lhs.lhs, Const(lhs.rhs.value + rhs.value))
     return Add(lhs, rhs)
 
 
 def mul(lhs, rhs) -> Expr:
+    """``lhs * rhs`` simplified likewise: constants fold, ``* 1`` drops and
+    ``(x * c1) * c2`` becomes ``x * (c1 * c2)``."""
     lhs, rhs = expression(lhs), expression(rhs)
     if isinstance(lhs, Const) and isinstance(rhs, Const):
         return Const(lhs.value * rhs.value)
-    if isinstance(lhs, Const) and lhs.value == 1:
-        return rhs
     if isinstance(rhs, Const) and rhs.value == 1:
         return lhs
+    if isinstance(lhs, Const) and lhs.value == 1:
+        return rhs
+    if isinstance(rhs, Const) and isinstance(lhs, Mul) and isinstance(lhs.rhs, Const):
+        return mul(lhs.lhs, Const(lhs.rhs.value * rhs.value))
     # (X floordiv k) * k with k constant stays as written; the encoder records
     # the divisibility that makes it equal X.
     return Mul(lhs, rhs)

@@ -1,17 +1,15 @@
 """The in-process plan encoder (replacement for the MLIR exporter) produces
 plans the reference decoder and binder accept and the reference executor runs
-to the reference's committed golden bits; for the reference corpus recipes it
-reproduces the committed blobs where the exporter did not canonicalize."""
+to the reference's committed golden bits, and for every reference corpus
+recipe it reproduces the exporter's committed blob byte for byte (the
+exporter's canonical form: merged adjacent axes, positional axis names,
+simplified expressions)."""
 import numpy as np
 import pytest
 
 from helpers import bits_to_bytes, corpus_params, encode, recipe_c1, recipe_c2, recipe_c3, recipe_c4, typed_corpus
 
 CASES = typed_corpus()
-# Fixtures whose committed blob the encoder reproduces byte for byte (the
-# others differ only by the exporter's axis canonicalization).
-BYTE_IDENTICAL = {"dequant_inline_zp_cast", "dequant_scale_witness", "dequant_zp127", "pad_then_quantize",
-                  "quantize_edges", "quantize_then_pad", "reciprocal_formation"}
 
 
 @pytest.mark.parametrize("case", CASES, ids=[c["name"] for c in CASES])
@@ -19,8 +17,7 @@ def test_corpus_recipes_execute_to_the_golden_bits(ref_lib, case):
     from sym_b200.reloc_torch import recipe as R
 
     blob = encode(R.from_json(case["recipe"]))
-    if case["name"] in BYTE_IDENTICAL:
-        assert blob.hex() == case["blob"]
+    assert blob.hex() == case["blob"]
     for b in case["bindings"]:
         prog = ref_lib.TypedProgram(blob, b["symbols"], corpus_params(case))
         src = np.frombuffer(bits_to_bytes(b["source"]["bits"], b["source"]["dtype"]), np.uint8)
