@@ -7,9 +7,10 @@ region's recipe once (in-process encoder), replaces the region's nodes by one
 call of a ``_Region`` and returns the rewritten graph's ``forward`` wrapped in
 a ``GraphCallable``. Per call a region
 
-* checks its inputs against the captured metadata (CPU, dense, dtype and
-  shape as captured, runtime parameters as declared; autograd off for inputs
-  that require grad) and otherwise runs the ORIGINAL region's nodes, so a
+* checks its inputs against the captured metadata (CPU, dense, dtype, rank,
+  every static extent as captured and every dynamic one bindable to its
+  symbol, runtime parameters as declared; autograd off for inputs that
+  require grad) and otherwise runs the ORIGINAL region's nodes, so a
   mismatched call never sees different semantics;
 * runs typed recipes through ``dispatch.prepare_typed_transfer`` /
   ``execute_typed_transfer`` and layout-only recipes through
@@ -27,6 +28,7 @@ from collections import Counter
 
 from .. import pyreloc
 from . import dispatch
+from . import symbolic as sx
 from .compiler import CompilerClient, UnsupportedRecipe
 from .fx_import import Exclusion, import_graph
 
@@ -49,10 +51,11 @@ class _Region:
         self.compiled = compiled
         self.original = original
         src = candidate.recipe.source
-        self.shape = tuple(int(e.value) for e in src.shape)
+        # None marks a dynamic extent (a plan symbol bound per call)
+        self.shape = tuple(int(e.value) if isinstance(e, sx.Const) else None for e in src.shape)
         self.dtype = getattr(torch, src.dtype)
         dst = candidate.recipe.destination
-        self.out_shape = tuple(int(e.value) for e in dst.shape)
+        self.out_extents = tuple(dst.shape)
         self.out_dtype = getattr(torch, dst.dtype)
         self.device = candidate.device  # index None: the current device at call time
         self.vector = {b.name: len(b.extents) == 1 for b in compiled.recipe.parameter_bindings}
@@ -63,13 +66,27 @@ class _Region:
 
         if not isinstance(src, torch.Tensor) or src.device.type != "cpu" or src.dtype != self.dtype:
             return False
-        if tuple(src.shape) != self.shape or not src.is_contiguous() or src.is_quantized:
+        if src.dim() != len(self.shape) or not src.is_contiguous() or src.is_quantized:
             return False
+        if any(want is not None and have != want for have, want in zip(src.shape, self.shape)):
+            return False
+        if src.numel() == 0:
+            return False
+        try:
+            bindings = self.compiled.source_symbols(tuple(src.shape))
+        except UnsupportedRecipe:
+            return False  # one symbol at two different sizes
+        declared = self.compiled.parameter_extents(bindings)
         if _needs_autograd((src, *params)):
             return False
-        for p in params:
+        for name, p in zip(self.candidate.parameters, params):
             if not isinstance(p, torch.Tensor) or p.device.type != "cpu" or p.dtype != torch.float32 \
                     or not p.is_contiguous():
+                return False
+            count = 1
+            for e in declared[name][1]:
+                count *= e
+            if p.numel() != count:
                 return False
         return True
 
@@ -93,8 +110,10 @@ class _Region:
     def _layout(self, src, device):
         import torch
 
-        bound = self.backend._bound(self.compiled)
-        out = torch.empty(self.out_shape, dtype=self.out_dtype, device=device)
+        bindings = self.compiled.source_symbols(tuple(src.shape))
+        bound = self.backend._bound(self.compiled, bindings)
+        out_shape = tuple(sx.expression(e).evaluate(bindings) for e in self.out_extents)
+        out = torch.empty(out_shape, dtype=self.out_dtype, device=device)
         es = src.element_size()
         sv = pyreloc.BufferView(src.data_ptr(), src.numel() * es, 0, [src.numel()], [1], es, "host", -1)
         dv = pyreloc.BufferView(out.data_ptr(), out.numel() * es, 0, [out.numel()], [1], es, "cuda",
@@ -146,11 +165,17 @@ class RelocBackend:
         if self._closed:
             raise RuntimeError("RelocBackend is closed")
 
-    def _bound(self, compiled):
-        key = id(compiled)
-        hit = self._bound_cache.get(key)
+    def _bound(self, compiled, bindings):
+        key = (id(compiled), tuple(sorted(bindings.items())))
+        with self._lock:
+            hit = self._bound_cache.get(key)
         if hit is None or hit[0] is not compiled:
-            hit = self._bound_cache[key] = (compiled, pyreloc.bind(compiled.decoded_plan, {}))
+            if len(self._bound_cache) >= 256:  # dynamic regions bind once per distinct size
+                with self._lock:
+                    self._bound_cache.clear()
+            hit = (compiled, pyreloc.bind(compiled.decoded_plan, bindings))
+            with self._lock:
+                self._bound_cache[key] = hit
         return hit[1]
 
     def stats(self):

@@ -28,7 +28,7 @@ import struct
 from dataclasses import dataclass
 
 from .recipe import BindingParam, Cast, Dequantize, Fill, InlineParam, Pad, Recipe, Reshape, TensorSpec, Transpose
-from .symbolic import Const
+from .symbolic import Const, Symbol, add, dense_strides, product
 
 
 @dataclass(frozen=True)
@@ -160,8 +160,11 @@ def _device_of(value):
 class _Walk:
     """Shape / stride / dtype / device state along a chain."""
 
-    def __init__(self, shape, dtype, inputs):
+    def __init__(self, shape, dtype, inputs, sym=None):
         self.shape = tuple(shape)
+        # Symbolic extents (dynamic dims of a Dynamo graph) or all constants;
+        # layout decisions use the example's concrete `shape`.
+        self.sym = tuple(sym) if sym is not None else tuple(Const(e) for e in self.shape)
         self.strides = _dense(self.shape)
         self.dtype = dtype
         self.device = "cpu"
@@ -179,9 +182,16 @@ class _Walk:
         if perm != tuple(range(rank)):
             self.ops.append(Transpose(perm))
         self.shape = tuple(self.shape[d] for d in perm)
+        self.sym = tuple(self.sym[d] for d in perm)
         self.strides = tuple(self.strides[d] for d in perm)
 
-    def reshape(self, target, need_dense=True):
+    @property
+    def symbolic(self):
+        return any(not isinstance(e, Const) for e in self.sym)
+
+    def reshape(self, target, need_dense=True, sym_target=None):
+        if self.symbolic and sym_target is None:
+            raise _Reject("symbolic_reshape")
         total = 1
         for e in self.shape:
             total *= e
@@ -201,9 +211,11 @@ class _Walk:
         if need_dense:
             _require(_is_dense(self.shape, self.strides), "non_dense_reshape")
         target = tuple(target)
-        if target != self.shape:
-            self.ops.append(Reshape(tuple(Const(e) for e in target)))
+        new_sym = tuple(sym_target) if sym_target is not None else tuple(Const(e) for e in target)
+        if new_sym != self.sym:
+            self.ops.append(Reshape(new_sym))
         self.shape = target
+        self.sym = new_sym
         self.strides = _dense(target)
 
     def squeeze(self, dims):
@@ -211,10 +223,13 @@ class _Walk:
         dims = range(rank) if dims is None else [d % rank for d in dims]
         keep = [i for i in range(rank) if not (i in dims and self.shape[i] == 1)]
         _require(keep, "rank_zero")
+        # a dynamic dim that is 1 in the example need not be 1 later
+        _require(all(isinstance(self.sym[i], Const) for i in range(rank) if i not in keep), "symbolic_squeeze")
         shape = tuple(self.shape[i] for i in keep)
         strides = tuple(self.strides[i] for i in keep)
         if shape != self.shape:
-            self.ops.append(Reshape(tuple(Const(e) for e in shape)))
+            self.sym = tuple(self.sym[i] for i in keep)
+            self.ops.append(Reshape(self.sym))
         self.shape, self.strides = shape, strides
 
     def unsqueeze(self, dim):
@@ -223,8 +238,9 @@ class _Walk:
         dim %= rank + 1
         inner = self.strides[dim] * self.shape[dim] if dim < rank else 1
         self.shape = self.shape[:dim] + (1,) + self.shape[dim:]
+        self.sym = self.sym[:dim] + (Const(1),) + self.sym[dim:]
         self.strides = self.strides[:dim] + (inner,) + self.strides[dim:]
-        self.ops.append(Reshape(tuple(Const(e) for e in self.shape)))
+        self.ops.append(Reshape(self.sym))
 
     def pad(self, widths, value):
         _require(len(widths) % 2 == 0 and len(widths) <= 2 * len(self.shape), "unsupported_padding")
@@ -236,6 +252,7 @@ class _Walk:
             if lo or hi:
                 self.ops.append(Pad(axis, Const(lo), Const(hi), fill))
                 self.shape = self.shape[:axis] + (self.shape[axis] + lo + hi,) + self.shape[axis + 1:]
+                self.sym = self.sym[:axis] + (add(add(self.sym[axis], lo), hi),) + self.sym[axis + 1:]
         self.strides = _dense(self.shape)
 
     # values ---------------------------------------------------------------
@@ -282,7 +299,7 @@ class _Walk:
         else:
             _require(len(axes) == 1 and shape[axes[0]] == self.shape[axes[0]], "unsupported_parameter")
             _require(tensor.dim() == 1 or tensor.numel() == self.shape[axes[0]], "unsupported_parameter")
-            self.ops[-1] = Dequantize("float32", BindingParam(name, "float32", (Const(self.shape[axes[0]]),)),
+            self.ops[-1] = Dequantize("float32", BindingParam(name, "float32", (self.sym[axes[0]],)),
                                       None, axes[0], "affine")
         _require(name not in self.parameters, "unsupported_parameter")
         self.parameters.append(name)
@@ -390,7 +407,8 @@ def _step(walk, node):
         inner = 1
         for e in walk.shape[start:end + 1]:
             inner *= e
-        walk.reshape(walk.shape[:start] + (inner,) + walk.shape[end + 1:])
+        walk.reshape(walk.shape[:start] + (inner,) + walk.shape[end + 1:],
+                     sym_target=walk.sym[:start] + (product(walk.sym[start:end + 1]),) + walk.sym[end + 1:])
     elif k == "squeeze":
         dims = node.args[1] if len(node.args) > 1 else node.kwargs.get("dim")
         dims = None if dims is None else (dims,) if type(dims) is int else tuple(dims)
@@ -459,6 +477,41 @@ def _member(node):
     return _kind(node) is not None
 
 
+def _symbolic_shape(root, example):
+    """Extents of a Dynamo placeholder: a Symbol for each dynamic dim (a bare
+    SymInt symbol in the node's example metadata, at least 2 in the example so
+    the captured layout decisions hold for every size), else a Const; None
+    when the graph is static or a dim is an expression."""
+    import torch
+
+    meta = root.meta.get("example_value")
+    if meta is None or not hasattr(meta, "shape"):
+        return None
+    out, dynamic = [], False
+    for d, e in zip(meta.shape, example.shape):
+        if isinstance(d, torch.SymInt):
+            name = str(d.node.expr)
+            if not name.isidentifier() or int(e) < 2:
+                return None
+            out.append(Symbol(name))
+            dynamic = True
+        else:
+            out.append(Const(int(d)))
+    return out if dynamic else None
+
+
+def _walk(members, src, dtype, inputs, sym):
+    walk = _Walk(src.shape, dtype, inputs, sym)
+    moves = 0
+    for m in members:
+        before = walk.device
+        _step(walk, m)
+        moves += walk.device != before
+    _require(moves == 1 and walk.device == "cuda", "same_device_transfer")
+    _require(_is_dense(walk.shape, walk.strides), "destination_layout")
+    return walk
+
+
 def import_graph(gm, example_inputs=None):
     """Discover replaceable regions of ``gm`` (read-only)."""
     import torch
@@ -505,18 +558,17 @@ def import_graph(gm, example_inputs=None):
                      "unsupported_symbolic_expr")
             dtype = _dtype_name(src.dtype)
             _require(dtype is not None, "unsupported_dtype")
-            walk = _Walk(src.shape, dtype, inputs)
-            moves = 0
-            for m in members:
-                before = walk.device
-                _step(walk, m)
-                moves += walk.device != before
-            _require(moves == 1 and walk.device == "cuda", "same_device_transfer")
-            _require(_is_dense(walk.shape, walk.strides), "destination_layout")
-            src_spec = TensorSpec(tuple(Const(e) for e in src.shape), tuple(Const(s) for s in _dense(src.shape)),
-                                  Const(0), dtype)
-            dst_spec = TensorSpec(tuple(Const(e) for e in walk.shape), tuple(Const(s) for s in _dense(walk.shape)),
-                                  Const(0), walk.dtype)
+            sym = _symbolic_shape(root, src)
+            try:
+                walk = _walk(members, src, dtype, inputs, sym)
+            except _Reject as error:
+                if sym is None or not error.reason.startswith("symbolic_"):
+                    raise
+                sym = None  # dynamic dims the chain cannot keep: capture the example's shape
+                walk = _walk(members, src, dtype, inputs, None)
+            src_sym = tuple(sym) if sym is not None else tuple(Const(e) for e in src.shape)
+            src_spec = TensorSpec(src_sym, dense_strides(src_sym), Const(0), dtype)
+            dst_spec = TensorSpec(walk.sym, dense_strides(walk.sym), Const(0), walk.dtype)
             recipe = Recipe(src_spec, tuple(walk.ops), dst_spec, "h2d")
             candidates.append(Candidate(root.name, members[-1].name, tuple(m.name for m in members), recipe,
                                         tuple(walk.parameters), walk.target_device))

@@ -116,3 +116,104 @@ def test_backend_rewrites_accepted_regions_only():
     backend.close()
     with pytest.raises(RuntimeError):
         fn(torch.zeros(16, 32, dtype=torch.int8), torch.ones(16), torch.zeros(8, 4))
+
+
+def _dynamo_graphs(fn, *args):
+    """The graphs Dynamo captures for ``fn`` with dynamic shapes (recorded by
+    a backend; the calls themselves fail on a host without a GPU)."""
+    import torch
+
+    graphs = []
+
+    def record(gm, example_inputs):
+        graphs.append((gm, list(example_inputs)))
+        return gm.forward
+
+    torch._dynamo.reset()
+    try:
+        torch.compile(fn, backend=record, dynamic=True)(*args)
+    except (RuntimeError, AssertionError):
+        pass
+    torch._dynamo.reset()
+    return graphs
+
+
+def test_dynamic_dims_become_plan_symbols():
+    import torch
+    from sym_b200.reloc_torch.compiler import CompilerClient
+    from sym_b200.reloc_torch.fx_import import import_graph
+    from sym_b200.reloc_torch.symbolic import Symbol
+
+    def f(q, s):
+        return (q.float() * s[:, None]).half().t().contiguous().cuda()
+
+    ((gm, ex),) = _dynamo_graphs(f, torch.zeros(16, 32, dtype=torch.int8), torch.ones(16))
+    (c,) = import_graph(gm, ex).candidates
+    rows, cols = c.recipe.source.shape
+    assert isinstance(rows, Symbol) and isinstance(cols, Symbol)
+    assert c.recipe.destination.shape == (cols, rows)
+    assert c.recipe.operations[0].scale.extents == (rows,)  # the scale's length is the row symbol
+    compiled = CompilerClient.from_environment().compile(c.recipe)
+    assert sorted(compiled.symbols) == sorted([rows.name, cols.name])
+    bindings = compiled.source_symbols((40, 24))
+    assert list(compiled.parameter_extents(bindings).values()) == [("float32", [40])]
+
+
+def test_dynamic_pad_and_flatten_keep_symbols():
+    import torch
+    import torch.nn.functional as F
+    from sym_b200.reloc_torch.fx_import import import_graph
+    from sym_b200.reloc_torch.symbolic import Add, Const, Mul, Symbol
+
+    ((gm, ex),) = _dynamo_graphs(lambda x: F.pad(x.permute(0, 2, 3, 1), (0, 1)).half().to("cuda"),
+                                 torch.zeros(2, 3, 5, 7))
+    (c,) = import_graph(gm, ex).candidates
+    n, ch, h, w = c.recipe.source.shape
+    assert all(isinstance(e, Symbol) for e in (n, ch, h, w))
+    assert c.recipe.destination.shape[:3] == (n, h, w) and c.recipe.destination.shape[3] == Add(ch, Const(1))
+
+    ((gm, ex),) = _dynamo_graphs(lambda x: x.flatten(1).t().contiguous().cuda(), torch.zeros(6, 4, 5))
+    (c,) = import_graph(gm, ex).candidates
+    a, b, d = c.recipe.source.shape
+    assert c.recipe.destination.shape == (Mul(b, d), a)
+
+
+def test_dynamic_reshape_captures_the_example_shape():
+    """A reshape whose target cannot follow the dynamic dims keeps the
+    example's sizes; the region then takes only that shape."""
+    import torch
+    from sym_b200.reloc_torch.backend import RelocBackend
+    from sym_b200.reloc_torch.fx_import import import_graph
+    from sym_b200.reloc_torch.symbolic import Const
+
+    ((gm, ex),) = _dynamo_graphs(lambda x: x.reshape(-1, 64).t().contiguous().cuda(), torch.zeros(1 << 12))
+    (c,) = import_graph(gm, ex).candidates
+    assert c.recipe.source.shape == (Const(4096),)
+    fn = RelocBackend()(gm, ex)
+    (region,) = fn.regions
+    assert region._eligible(torch.zeros(4096), ())
+    assert not region._eligible(torch.zeros(8192), ())
+
+
+def test_dynamic_region_checks_each_call():
+    import torch
+    from sym_b200.reloc_torch.backend import RelocBackend
+
+    def f(q, s):
+        return (q.float() * s[:, None]).half().t().contiguous().cuda()
+
+    ((gm, ex),) = _dynamo_graphs(f, torch.zeros(16, 32, dtype=torch.int8), torch.ones(16))
+    fn = RelocBackend()(gm, ex)
+    (region,) = fn.regions
+    assert region.shape == (None, None)
+    q = torch.zeros(40, 24, dtype=torch.int8)
+    assert region._eligible(q, (torch.ones(40),))
+    assert not region._eligible(q, (torch.ones(24),))          # scale length != rows
+    assert not region._eligible(q.float(), (torch.ones(40),))  # dtype
+    assert not region._eligible(q[:, :8], (torch.ones(40),))   # not dense
+    assert not region._eligible(torch.zeros(0, 24, dtype=torch.int8), (torch.ones(0),))
+
+    ((gm, ex),) = _dynamo_graphs(lambda x: x.t().contiguous().cuda(), torch.zeros(16, 16))
+    (region,) = RelocBackend()(gm, ex).regions
+    assert region._eligible(torch.zeros(24, 24), ())
+    assert not region._eligible(torch.zeros(24, 8), ())  # one symbol, two sizes

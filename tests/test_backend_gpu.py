@@ -1,20 +1,21 @@
 """RelocBackend end to end on the GPU: ``torch.compile(fn, backend=RelocBackend())``
 returns exactly what eager ``fn`` returns (bit for bit), the accepted regions
-run on the B200 kernels (kernel launches counted), and calls the replacement
-cannot take (inputs that need autograd, shapes captured symbolically) run the
-original ops."""
+run on the B200 kernels (kernel launches counted), graphs captured with
+dynamic shapes run one region over every size (the plan's symbols bound per
+call), and calls the replacement cannot take (inputs that need autograd) run
+the original ops."""
 import pytest
 
 pytestmark = pytest.mark.gpu
 
 
-def _compile(fn):
+def _compile(fn, dynamic=False):
     import torch
     from sym_b200.reloc_torch.backend import RelocBackend
 
     torch._dynamo.reset()
     backend = RelocBackend()
-    return torch.compile(fn, backend=backend, dynamic=False), backend
+    return torch.compile(fn, backend=backend, dynamic=dynamic), backend
 
 
 def _bits_equal(a, b):
@@ -100,3 +101,43 @@ def test_repeat_calls_and_new_values_stay_exact():
         q = torch.randint(-128, 128, (256, 512), dtype=torch.int8, generator=torch.Generator().manual_seed(seed))
         assert _bits_equal(fn(q), f(q))
     assert backend.stats()["executions"] >= 3
+
+
+def test_dynamic_shapes_bind_per_call():
+    """One dynamic capture serves every size: no recompile, each call exact."""
+    import torch
+    from sym_b200 import pyreloc
+
+    def f(q, s):
+        return (q.float() * s[:, None]).half().t().contiguous().cuda()
+
+    fn, backend = _compile(f, dynamic=True)
+    g = torch.Generator().manual_seed(1)
+    for rows, cols in ((256, 512), (96, 200), (1024, 4096), (33, 7)):
+        q = torch.randint(-128, 128, (rows, cols), dtype=torch.int8, generator=g)
+        s = torch.exp(torch.randn(rows, generator=g) * 0.5 - 5)
+        l0 = pyreloc.kernel_launches()
+        got = fn(q, s)
+        torch.cuda.synchronize()
+        assert pyreloc.kernel_launches() > l0
+        assert got.shape == (cols, rows) and _bits_equal(got, f(q, s))
+    st = backend.stats()
+    assert st["graphs"] == 1 and st["executions"] == 4 and st.get("fallbacks", 0) == 0
+
+
+@pytest.mark.parametrize("fn_name", ["pad", "flatten"])
+def test_dynamic_layout_and_pad_regions(fn_name):
+    import torch
+    import torch.nn.functional as F
+
+    fns = {
+        "pad": (lambda x: F.pad(x.permute(0, 2, 3, 1), (0, 1)).half().to("cuda"),
+                [(2, 3, 64, 64), (4, 3, 31, 17), (1, 5, 8, 9)]),
+        "flatten": (lambda x: x.flatten(1).t().contiguous().cuda(), [(6, 4, 5), (64, 32, 48), (3, 2, 1000)]),
+    }
+    f, shapes = fns[fn_name]
+    fn, backend = _compile(f, dynamic=True)
+    for shape in shapes:
+        x = torch.rand(shape)
+        assert _bits_equal(fn(x), f(x))
+    assert backend.stats()["executions"] >= 2
