@@ -350,14 +350,18 @@ def run_ours(args):
 
     for _ in range(3):
         gate_launch()
-    ka, kb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    reps = 10  # 705 MB per launch at N=1: larger than L2, so launches do not hit each other's lines
-    ka.record(compute_stream)
-    for _ in range(reps):
+    # 705 MB per launch at N=1: larger than L2, so launches do not hit each
+    # other's lines. Each launch between its own pair of events; median and p95.
+    reps = 20
+    marks = [torch.cuda.Event(enable_timing=True) for _ in range(reps + 1)]
+    marks[0].record(compute_stream)
+    for i in range(reps):
         gate_launch()
-    kb.record(compute_stream)
+        marks[i + 1].record(compute_stream)
     torch.cuda.synchronize(dev)
-    kernel_s = ka.elapsed_time(kb) * 1e-3 / reps
+    launch_s = sorted(marks[i].elapsed_time(marks[i + 1]) * 1e-3 for i in range(reps))
+    kernel_s = statistics.median(launch_s)
+    kernel_p95_s = launch_s[int(0.95 * (reps - 1) + 0.5)]
     gate_elems = gm["out"] * (ge - gb)
     kernel_bytes = gate_elems * 3 + gm["out"] * 4
     achieved_gbs = kernel_bytes / kernel_s / 1e9
@@ -412,6 +416,7 @@ def run_ours(args):
                      "kernel": f"k_tma_tile<int8, CH_DQ_F16, per-column scale> on gate [{gm['out']}, {gm['in']}], "
                                "this rank's rows",
                      "bytes_per_launch": kernel_bytes, "launch_ms": kernel_s * 1e3,
+                     "launch_ms_p95": kernel_p95_s * 1e3, "launches_timed": reps,
                      "bytes_per_launch_note": "int8 read + f16 write per element + 4 B per source-row scale",
                      "traffic_note": "ncu dram__bytes_read.sum + dram__bytes_write.sum of the full gate launch "
                                      "(--kernel-case), scaled by this rank's share of its elements"},
@@ -425,13 +430,34 @@ def run_ours(args):
     return 0
 
 
+def host_info():
+    """The host the CPU baseline ran on: logical CPUs, the CPUs this process
+    may use, the CPU model and the NUMA nodes."""
+    model = None
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    model = line.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    try:
+        nodes = sorted(n for n in os.listdir("/sys/devices/system/node") if n.startswith("node") and n[4:].isdigit())
+    except OSError:
+        nodes = []
+    return {"nproc": os.cpu_count(), "affinity": len(os.sched_getaffinity(0)), "cpu_model": model,
+            "numa_nodes": len(nodes) or None}
+
+
 def cpu_baseline(shapes):
-    """The reference CPU executor on one Llama-70B matrix pair (~10-20 s of CPU work)."""
+    """The reference CPU executor on one Llama-70B matrix pair (~10-20 s of
+    CPU work) with every usable host thread, and again with 8 threads (the
+    reference's own qualified setting)."""
     from helpers import encode, recipe_c4
     from oracle import ref
 
     threads = len(os.sched_getaffinity(0))
-    pool = ref.GatherPool(threads)
     blob = encode(recipe_c4())
     rng = np.random.default_rng(0)
     out_f, in_f = 8192, 8192
@@ -441,18 +467,23 @@ def cpu_baseline(shapes):
                          {"scale": ("float32", [out_f], scale.tobytes())})
     dst = np.empty(out_f * in_f * 2, np.uint8)
     src = q.reshape(-1).view(np.uint8)
-    p.execute_into(src, dst, pool=pool)
-    t0 = time.perf_counter()
-    n = 0
-    while time.perf_counter() - t0 < 8.0 and n < 20:
-        p.execute_into(src, dst, pool=pool)
-        n += 1
-    dt = (time.perf_counter() - t0) / n
     layer_elems = sum(o * i for _, o, i in shapes)
-    return {"value": (out_f * in_f / dt) / layer_elems, "unit": "layers/s", "cores": pool.threads,
-            "kind": "reference",
+
+    def rate(pool, seconds):
+        p.execute_into(src, dst, pool=pool)
+        t0, n = time.perf_counter(), 0
+        while time.perf_counter() - t0 < seconds and n < 20:
+            p.execute_into(src, dst, pool=pool)
+            n += 1
+        return (out_f * in_f / ((time.perf_counter() - t0) / n)) / layer_elems, n
+
+    pool = ref.GatherPool(threads)
+    value, n = rate(pool, 8.0)
+    value8, n8 = rate(ref.GatherPool(8), 4.0)
+    return {"value": value, "unit": "layers/s", "cores": pool.threads, "kind": "reference",
             "sample": f"q-projection [8192, 8192] int8 -> f16 [8192, 8192] x{n} via typed::executeHost, "
-                      "scaled to layers by element count"}
+                      "scaled to layers by element count",
+            "value_8_threads": value8, "runs_8_threads": n8, "host": host_info()}
 
 
 def run_kernel_case(args):
@@ -655,6 +686,7 @@ def run_config(args):
         times.append(a.elapsed_time(b) * 1e-3)
     launches = pyreloc.kernel_launches() - l0
     t_kernel = statistics.median(times)
+    t_p95 = sorted(times)[int(0.95 * (len(times) - 1) + 0.5)]
 
     # end to end through the public API: pinned host source -> device result
     # (d2h: device source -> pinned host result)
@@ -714,8 +746,8 @@ def run_config(args):
     print(json.dumps({
         "metric": f"{case['workload']} {case['unit']}", "value": case["unit_per_step"] / t_kernel,
         "unit": case["unit"], "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": t_kernel * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": case["dtype"], "data": "synthetic",
+        "ms_per_step": t_kernel * 1e3, "ms_per_step_p95": t_p95 * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": case["dtype"], "data": "synthetic",
         "config": {"workload": case["workload"], "shape": case["shape"],
                    "l2": "flushed (256 MB read) before each timed kernel launch; the e2e source crosses PCIe "
                          "every step"},
@@ -731,7 +763,8 @@ def run_config(args):
                      "bytes_per_launch_note": case["bytes_note"]},
         "gpu_launches": int(launches), "clocks": ck,
         "cpu_baseline": {"value": cpu_rate, "unit": case["unit"], "cores": threads, "kind": "reference",
-                         "sample": f"the whole input x{cpu_n}, reference executor host->host"},
+                         "sample": f"the whole input x{cpu_n}, reference executor host->host",
+                         "value_8_threads": _cpu_config(case, 8)[0], "host": host_info()},
     }))
     return 0
 

@@ -5,7 +5,7 @@
 recipe compiled once and bound for every matrix shape, ``fetch``,
 ``fetch_many`` (one transfer group), ``prepare_many``, ``prefetch`` (a
 bounded asynchronous window), per-device retained resources, ``reference``
-and ``close``.
+and ``close``, plus the offline helper ``quantize_per_channel``.
 Its default recipe is the reference's own (int8 ``[in, out]``, per-output-
 channel f32 scale on axis 1 -> dequantize -> transpose -> f32 ``[out, in]``);
 ``layout="out_in_f16"`` selects the BASELINE weight-streaming recipe (int8
@@ -69,6 +69,28 @@ def weight_recipe(layout="reference"):
                        Cast("float16", "ieee_rne"), Transpose((1, 0))),
                       spec((cols, rows), "float16"), "h2d")
     raise ValueError("layout must be 'reference' or 'out_in_f16'")
+
+
+def quantize_per_channel(weight, layout="reference"):
+    """Offline checkpoint preparation in PyTorch (reference
+    common.py:368-378): symmetric int8 with one f32 scale per output
+    channel, ``scale = amax|w| / 127`` (at least the smallest normal f32, so
+    an all-zero channel keeps a positive scale) and ``q = round(w / scale)``
+    clamped to [-127, 127].
+
+    ``layout="reference"``: ``weight`` is f32 ``[in, out]``, scales run along
+    axis 1 (``[out]``), the input of WeightFetcher's default recipe.
+    ``layout="out_in_f16"``: ``weight`` is ``[out, in]``, scales along axis 0
+    (``[out]``), the input of the f16 weight-streaming recipe."""
+    import torch
+
+    if layout not in ("reference", "out_in_f16"):
+        raise ValueError("layout must be 'reference' or 'out_in_f16'")
+    axis = 0 if layout == "reference" else 1  # the reduced (input-feature) axis
+    weight = weight.to(torch.float32)
+    scale = (weight.abs().amax(dim=axis) / 127.0).clamp_min(torch.finfo(torch.float32).tiny)
+    q = torch.round(weight / (scale if axis == 0 else scale[:, None])).clamp_(-127, 127).to(torch.int8)
+    return q.contiguous(), scale.contiguous()
 
 
 class WeightFetcher:

@@ -51,6 +51,52 @@ def test_weight_fetcher_f16_recipe(shape):
     assert torch.equal(got.view(torch.int16), want.view(torch.int16))
 
 
+def test_weight_fetcher_matches_pytorch_for_every_shape_with_one_artifact():
+    """One compiled recipe serves every matrix shape (reference
+    test_workload_common.py:186-203); the raw int8 crosses the wire."""
+    import torch
+    from sym_b200.workloads import Report, WeightFetcher, quantize_per_channel
+
+    report = Report()
+    generator = torch.Generator().manual_seed(1)
+    with WeightFetcher(report) as fetcher:
+        for rows, cols in ((64, 96), (96, 64), (128, 128)):
+            q, scale = quantize_per_channel(torch.randn(rows, cols, generator=generator))
+            got = fetcher.fetch(q, scale, "cuda:0")
+            want = WeightFetcher.reference(q, scale, "cuda:0")
+            assert got.shape == (cols, rows) and got.dtype == torch.float32
+            assert torch.equal(got.view(torch.int32), want.view(torch.int32))
+    assert fetcher.compiles == 1 and fetcher.shapes == {(64, 96), (96, 64), (128, 128)}
+    assert report.data["plan_compiles"] == 1
+    weights = report.data["bytes"]["weights"]
+    assert weights["transfers"] == 3 and weights["wire"] == weights["source"]
+    assert weights["destination"] == 4 * weights["source"]
+    assert sum(report.data["dispatches"].values()) == 3
+    assert all(k.startswith("b200_fused_h2d") for k in report.data["dispatches"])
+
+
+@pytest.mark.skipif("__import__('torch').cuda.device_count() < 2", reason="needs two GPUs")
+def test_weight_fetcher_reaches_a_device_that_is_not_current():
+    """Alternating destination devices keeps one warm owner per device and
+    leaves the current device alone (reference test_workload_common.py:206-225)."""
+    import torch
+    from sym_b200.workloads import Report, WeightFetcher, quantize_per_channel
+
+    report = Report()
+    fetcher = WeightFetcher(report, kind="expert_weights", layout="out_in_f16")
+    q, scale = quantize_per_channel(torch.randn(512, 256, generator=torch.Generator().manual_seed(2)),
+                                    "out_in_f16")
+    with torch.cuda.device(0), fetcher:
+        for device in ("cuda:0", "cuda:1", "cuda:0", "cuda:1"):
+            got = fetcher.fetch(q, scale, device)
+            assert torch.cuda.current_device() == 0 and got.device == torch.device(device)
+            want = WeightFetcher.reference(q, scale, device, layout="out_in_f16")
+            assert torch.equal(got.view(torch.int16), want.view(torch.int16))
+        stats = fetcher.resource_stats()
+        assert len(stats) == 2 and all(s["requests"] == 2 and s["contexts"] == 1 for s in stats.values())
+    assert report.data["bytes"]["expert_weights"]["transfers"] == 4
+
+
 def test_fetch_many_and_stream_ordering():
     """Outputs follow the caller's current stream: work queued on a side
     stream before the fetch is ordered before it."""
