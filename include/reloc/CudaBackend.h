@@ -43,7 +43,7 @@ public:
   /// Record completion of everything enqueued so far on the private streams;
   /// with `hasExternal`, order `external` (a null handle = the legacy default
   /// stream) after it.
-  bool signalStream(const void *external, bool hasExternal);
+  bool signalStream(const void *external, bool hasExternal, bool copyUsed = true);
   /// Block until all enqueued work completed.
   QueueCompletion quiesce();
 
@@ -75,20 +75,41 @@ public:
   uint64_t eventWaits = 0;
   uint64_t callerWaits = 0;
   uint64_t kernelLaunches = 0;
+  /// sbc_wait_launch_count() when this context last read the fault word.
+  uint64_t waitLaunchesChecked = 0;
   /// Set while a group runs: its members share one status word, cleared once
   /// before the first member instead of once per execution.
   bool keepStatus = false;
 
   /// Measured route choice per plan class: key -> seconds per byte of each
-  /// route (negative = not yet measured).
+  /// route, from its latest timed execution. A route counts as measured after
+  /// two samples (the first may include one-time ring allocation).
   struct RouteStats {
     double dmaSecondsPerByte = -1, zeroCopySecondsPerByte = -1;
+    uint32_t dmaSamples = 0, zeroCopySamples = 0;
+    bool known() const { return dmaSamples >= 2 && zeroCopySamples >= 2; }
+    uint32_t executions = 0; // auto-route executions since both were measured
+    bool probe = false;      // this timed execution re-measures the slower route
   };
   std::map<std::string, RouteStats> routeStats;
   std::mutex mutex; // one request at a time per context
 
+  /// Copy `bytes` of pageable (unregistered) host memory at `src` to device
+  /// memory `dst`, queued on the copy stream, through pinned bounce buffers:
+  /// host threads fill one buffer while the copy engine drains the previous
+  /// one. Returns when the last piece is queued (the host source may change
+  /// afterwards). The driver's own pageable path copies on one thread.
+  bool bounceH2D(void *dst, const void *src, size_t bytes);
+  uint64_t bouncedBytes = 0;
+
 private:
+  struct HostCopyPool;
+  static constexpr int kBounceBuffers = 3;
   CudaBackend() = default;
+  std::unique_ptr<HostCopyPool> pool_;
+  void *bounce_[kBounceBuffers] = {};
+  void *bounceFree_[kBounceBuffers] = {};
+  bool bounceUsed_[kBounceBuffers] = {};
   int device_ = -1;
   bool failed_ = false;
   std::string error_;

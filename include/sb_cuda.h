@@ -12,10 +12,12 @@
  *    cudaHostAlloc staging, cudaMemcpyAsync, events, cross-stream waits,
  *    pointer-attribute checks (libreloc/cuda/CudaBackend.cu:55-282);
  *  - every transform kernel of libreloc/cuda/CudaKernels.cu (launchers at
- *    libreloc/include/reloc/CudaKernels.h:25-122) by three fused families
+ *    libreloc/include/reloc/CudaKernels.h:25-122) by four fused families
  *    that take the whole bound layout plus the value-stage chain:
  *      sbc_relocate_generic    any rank <= 8 layout, pads, any channel map;
  *      sbc_relocate_contiguous rank-1 unit-stride runs (quantize/dequantize/casts);
+ *      sbc_relocate_runs       outer-axis permutations moving whole unit-stride
+ *                              rows ([B,S,H,D] -> [B,H,S,D]);
  *      sbc_relocate_transpose  (batched) 2-D transposes with pads, tiled in
  *                              shared memory (f32 transpose, NCHW->NHWC+pad+f16,
  *                              int8 [out,in] -> f16 [in,out] dequant).
@@ -111,6 +113,10 @@ typedef struct {
 /* ---- kernels (asynchronous on `stream`; NULL = the legacy default stream) */
 int sbc_relocate_generic(const sbc_relocate *desc, void *stream);
 int sbc_relocate_contiguous(const sbc_relocate *desc, void *stream);
+/* Rank >= 2 layouts whose last axis is unit-stride on both sides (outer axes
+ * permuted, outer pads, one parameter per tensor or per run);
+ * SBC_EUNSUPPORTED when the descriptor does not fit. */
+int sbc_relocate_runs(const sbc_relocate *desc, void *stream);
 int sbc_relocate_transpose(const sbc_relocate *desc, void *stream);
 /* One TMA tile launch over `n` (<= 8) separately stored blocks of source
  * rows: `srcs[j]` holds the rows [row_bounds[j], row_bounds[j+1]) of axis 1
@@ -125,6 +131,9 @@ int sbc_relocate_transpose_shards(const sbc_relocate *desc, const void *const *s
 int sbc_fill(void *dst, int64_t count, int32_t width, uint64_t bits, void *stream);
 /* Kernels launched by this library since load (instrumentation). */
 uint64_t sbc_launch_count(void);
+/* Launches since load of kernels with bounded waits, the only kernels that
+ * set the fault word: while it has not moved, the fault word is clear. */
+uint64_t sbc_wait_launch_count(void);
 /* The current device's kernel fault word, then cleared: 0 none, 2 a TMA copy
  * a kernel waited for did not land within the wait limit (the kernel left
  * early; its output is incomplete). Synchronizes with the device. */

@@ -28,6 +28,9 @@
 namespace {
 
 std::atomic<uint64_t> g_launches{0};
+// Launches of kernels with bounded waits (the only writers of the device
+// fault word): callers read the fault word only after one of these ran.
+std::atomic<uint64_t> g_wait_launches{0};
 
 // ---------------------------------------------------------------------------
 // Scalar stage arithmetic
@@ -458,6 +461,116 @@ __global__ void __launch_bounds__(256) k_narrow(const __grid_constant__ sbc_relo
 #pragma unroll
     for (int i = 0; i < RUN / SV; ++i)
       __stcs(dp + i, out.q[i]);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Runs: the last axis is unit-stride in both the source and the destination,
+// so each destination row of that axis is one contiguous run of the source
+// (leading axes permuted: [B,S,H,D] -> [B,H,S,D], swaps of outer axes).
+// The box is cut into units of U = 16 / max(WS, WD) elements of the last
+// axis; thread i takes unit i in destination order, so a warp's loads and
+// stores are contiguous spans within a run. A unit's row resolves its outer
+// coordinates with one magic-number division per outer axis; rows inside an
+// outer pad take the fill. Parameters: one per tensor, or one per run (a
+// channel on an outer axis).
+// ---------------------------------------------------------------------------
+
+struct RunsGeom {
+  FastDiv upr;                   // units per row of the last axis
+  FastDiv ext[SBC_MAX_RANK - 1]; // box extents of the outer axes
+};
+
+template <int WS, int WD, int CHAIN>
+__global__ void __launch_bounds__(256) k_runs(const __grid_constant__ sbc_relocate d, const __grid_constant__ RunsGeom g,
+                                               uint32_t nunits) {
+  using S = typename Word<WS>::T;
+  using D = typename Word<WD>::T;
+  constexpr int U = Units<WS, WD>::U;
+  using SU = typename Bytes<U * WS>::T;
+  using DU = typename Bytes<U * WD>::T;
+  constexpr bool kParam = CHAIN == CH_Q || CHAIN == CH_DQ || CHAIN == CH_DQ_F16 || CHAIN == CH_DQ_BF16;
+  const int last = d.rank - 1;
+  const S *src = static_cast<const S *>(d.src) + (d.box_lo[last] - d.pad_lo[last] - d.src_offset);
+  D *dst = static_cast<D *>(d.dst) + (d.box_lo[last] - d.dst_offset);
+  const sbc_stage &s = d.stages[0];
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < nunits; i += gridDim.x * blockDim.x) {
+    uint32_t row = fdiv(i, g.upr);
+    const int64_t j = static_cast<int64_t>(i - row * g.upr.d) * U;
+    int64_t so = 0, dg = 0;
+    int64_t coords[SBC_MAX_RANK - 1];
+    bool valid = true;
+#pragma unroll
+    for (int kk = 0; kk < SBC_MAX_RANK - 1; ++kk) {
+      const int k = SBC_MAX_RANK - 2 - kk; // innermost outer axis first
+      if (k >= last)
+        continue;
+      const uint32_t q = fdiv(row, g.ext[k]);
+      const int64_t c = d.box_lo[k] + (row - q * g.ext[k].d);
+      row = q;
+      coords[k] = c;
+      dg += c * d.dst_strides[k];
+      const int64_t v = c - d.pad_lo[k];
+      if (v < 0 || v >= d.extents[k])
+        valid = false;
+      else
+        so += v * d.src_strides[k];
+    }
+    union {
+      DU q;
+      D e[U];
+    } out;
+    DU *dp = reinterpret_cast<DU *>(dst + dg + j);
+    if (!valid) {
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        out.e[u] = static_cast<D>(d.fill_bits);
+      __stcs(dp, out.q);
+      continue;
+    }
+    union {
+      SU q;
+      S e[U];
+    } in;
+    in.q = __ldcs(reinterpret_cast<const SU *>(src + so + j));
+    float p = 0.0f;
+    int32_t zp = 0;
+    if constexpr (kParam) {
+      int64_t c = 0;
+      if (s.channel == SBC_CH_AXIS) {
+        c = coords[s.ch_axis] / s.ch_div;
+        if (s.ch_mod)
+          c %= s.ch_mod;
+      }
+      if (c >= s.channel_length) {
+        flag(d);
+        continue;
+      }
+      p = s.param[c];
+      zp = zp_of(s, c);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      uint32_t v = static_cast<uint32_t>(in.e[u]);
+      if constexpr (CHAIN == CH_F16)
+        v = narrow_f16(v);
+      else if constexpr (CHAIN == CH_BF16)
+        v = narrow_bf16(v);
+      else if constexpr (CHAIN == CH_W16)
+        v = widen_f16(v);
+      else if constexpr (CHAIN == CH_WB16)
+        v = widen_bf16(v);
+      else if constexpr (CHAIN == CH_Q)
+        v = quantize(v, p);
+      else if constexpr (CHAIN == CH_DQ)
+        v = dequantize(v, zp, p);
+      else if constexpr (CHAIN == CH_DQ_F16)
+        v = narrow_f16(dequantize(v, zp, p));
+      else if constexpr (CHAIN == CH_DQ_BF16)
+        v = narrow_bf16(dequantize(v, zp, p));
+      out.e[u] = static_cast<D>(v);
+    }
+    __stcs(dp, out.q);
   }
 }
 
@@ -1552,6 +1665,18 @@ int launch_narrow(const sbc_relocate &d, int nb, int64_t per_batch, int64_t tota
   return launched(cudaSuccess);
 }
 
+template <int WS, int WD, int CH> struct RunsLaunch {
+  static int run(const sbc_relocate &d, const RunsGeom &g, uint32_t nunits, cudaStream_t s) {
+    if constexpr (WS == 8 || WD == 8 || CH == CH_ANY) {
+      return SBC_EUNSUPPORTED;
+    } else {
+      const int64_t blocks = grid_for(nunits, 256, 8);
+      k_runs<WS, WD, CH><<<static_cast<unsigned>(blocks), 256, 0, s>>>(d, g, nunits);
+      return launched(cudaSuccess);
+    }
+  }
+};
+
 /// k_narrow when the box fits it (see the kernel); SBC_EUNSUPPORTED otherwise.
 int try_narrow(const sbc_relocate &d, int chain, cudaStream_t s) {
   const int ax_a = d.rank - 2, ax_b = d.rank - 1;
@@ -1668,6 +1793,7 @@ int launch_tma(const sbc_relocate &d, int chain, int ch_on, const void *const *b
   else
     ch_on == 0 ? SBC_TMA(1, CH_DQ_BF16, 0) : ch_on == 1 ? SBC_TMA(1, CH_DQ_BF16, 1) : SBC_TMA(1, CH_DQ_BF16, 2);
 #undef SBC_TMA
+  g_wait_launches.fetch_add(1, std::memory_order_relaxed);
   return launched(cudaSuccess);
 }
 
@@ -1711,6 +1837,52 @@ int sbc_relocate_generic(const sbc_relocate *desc, void *stream) {
     chain = desc->nstages == 0 && desc->src_width == desc->dst_width ? CH_COPY : -1;
   return dispatch<GenericLaunch>(desc->src_width, desc->dst_width, chain, *desc, total,
                                  static_cast<cudaStream_t>(stream));
+}
+
+int sbc_relocate_runs(const sbc_relocate *desc, void *stream) {
+  if (!desc || !basic_ok(*desc))
+    return SBC_EINVAL;
+  const sbc_relocate &d = *desc;
+  const int r = d.rank, last = r - 1;
+  if (r < 2 || d.src_strides[last] != 1 || d.dst_strides[last] != 1 || d.src_width == 8 || d.dst_width == 8)
+    return SBC_EUNSUPPORTED;
+  const int chain = chain_of(d);
+  if (chain == CH_ANY)
+    return SBC_EUNSUPPORTED;
+  if (chain == CH_Q || chain == CH_DQ || chain == CH_DQ_F16 || chain == CH_DQ_BF16) {
+    const sbc_stage &s = d.stages[0];
+    const bool outer_axis = s.channel == SBC_CH_AXIS && s.ch_axis < last && s.ch_div >= 1 && s.ch_mod >= 0;
+    if ((s.channel != SBC_CH_NONE && !outer_axis) || s.channel_length < 1)
+      return SBC_EUNSUPPORTED;
+  }
+  const int ws = d.src_width, wd = d.dst_width;
+  const int U = 16 / (ws > wd ? ws : wd);
+  // the last axis of the box lies in the valid source and splits into units
+  const int64_t run = d.box_hi[last] - d.box_lo[last];
+  if (d.box_lo[last] < d.pad_lo[last] || d.box_hi[last] > d.pad_lo[last] + d.extents[last] || run % U)
+    return SBC_EUNSUPPORTED;
+  int64_t rows = 1;
+  for (int k = 0; k < last; ++k) {
+    const int64_t e = d.box_hi[k] - d.box_lo[k];
+    if (d.src_strides[k] % U || d.dst_strides[k] % U || e >= (int64_t(1) << 31))
+      return SBC_EUNSUPPORTED;
+    rows *= e;
+  }
+  if (run == 0 || rows == 0)
+    return 0;
+  const int64_t upr = run / U, nunits = rows * upr;
+  if (upr >= (int64_t(1) << 31) || nunits >= (int64_t(1) << 31) - 256 * 8 * 1024) // 32-bit unit indices
+    return SBC_EUNSUPPORTED;
+  // every unit starts 16-byte aligned on the wide side (and U-element aligned on the other)
+  const uintptr_t sa = reinterpret_cast<uintptr_t>(d.src) + (d.box_lo[last] - d.pad_lo[last] - d.src_offset) * ws;
+  const uintptr_t da = reinterpret_cast<uintptr_t>(d.dst) + (d.box_lo[last] - d.dst_offset) * wd;
+  if (sa % (U * ws) || da % (U * wd))
+    return SBC_EUNSUPPORTED;
+  RunsGeom g;
+  g.upr = make_fastdiv(static_cast<uint32_t>(upr));
+  for (int k = 0; k < SBC_MAX_RANK - 1; ++k)
+    g.ext[k] = make_fastdiv(k < last ? static_cast<uint32_t>(d.box_hi[k] - d.box_lo[k]) : 1u);
+  return dispatch<RunsLaunch>(ws, wd, chain, d, g, static_cast<uint32_t>(nunits), static_cast<cudaStream_t>(stream));
 }
 
 int sbc_relocate_contiguous(const sbc_relocate *desc, void *stream) {
@@ -1875,6 +2047,8 @@ int sbc_fill(void *dst, int64_t count, int32_t width, uint64_t bits, void *strea
 }
 
 uint64_t sbc_launch_count(void) { return g_launches.load(); }
+
+uint64_t sbc_wait_launch_count(void) { return g_wait_launches.load(); }
 
 int sbc_device_fault(int *code) {
   int zero = 0;

@@ -4,7 +4,147 @@
 
 #include "sb_cuda.h"
 
+#include <algorithm>
+#include <atomic>
+#include <chrono>
+#include <condition_variable>
+#include <cstdlib>
+#include <cstring>
+#include <thread>
+
 namespace reloc {
+
+/// Worker threads that split one host memcpy with the calling thread. A
+/// bounce copy hands out one piece every few hundred microseconds, so both
+/// sides poll for up to kSpinUs before sleeping on a condition variable
+/// (waking a sleeping thread can cost more than a piece's copy).
+struct CudaBackend::HostCopyPool {
+  static constexpr int64_t kSpinUs = 200;
+
+  explicit HostCopyPool(int workers) {
+    for (int k = 1; k <= workers; ++k)
+      threads.emplace_back([this, k] { run(k); });
+  }
+  ~HostCopyPool() {
+    {
+      std::lock_guard<std::mutex> g(m);
+      stop.store(true);
+    }
+    wake.notify_all();
+    for (auto &t : threads)
+      t.join();
+  }
+  /// Copy [src, src + bytes) to dst with every thread; returns when done.
+  void copy(void *dst, const void *src, size_t bytes) {
+    const size_t parts = threads.size() + 1;
+    if (threads.empty() || bytes < (size_t(1) << 20)) {
+      std::memcpy(dst, src, bytes);
+      return;
+    }
+    dst_ = static_cast<uint8_t *>(dst);
+    src_ = static_cast<const uint8_t *>(src);
+    bytes_ = bytes;
+    part_ = ((bytes + parts - 1) / parts + 63) & ~size_t(63);
+    pending.store(static_cast<int>(threads.size()), std::memory_order_relaxed);
+    {
+      std::lock_guard<std::mutex> g(m);
+      generation.fetch_add(1, std::memory_order_release); // publishes the job fields
+    }
+    wake.notify_all();
+    std::memcpy(dst, src, std::min(part_, bytes));
+    if (!spinUntil([this] { return pending.load(std::memory_order_acquire) == 0; })) {
+      std::unique_lock<std::mutex> g(m);
+      finished.wait(g, [this] { return pending.load(std::memory_order_acquire) == 0; });
+    }
+  }
+
+private:
+  template <class Pred> static bool spinUntil(Pred ready) {
+    const auto t0 = std::chrono::steady_clock::now();
+    for (uint32_t i = 1;; ++i) {
+      if (ready())
+        return true;
+      if ((i & 63u) == 0 &&
+          std::chrono::steady_clock::now() - t0 > std::chrono::microseconds(kSpinUs))
+        return false;
+    }
+  }
+  void run(int k) {
+    uint64_t seen = 0;
+    for (;;) {
+      auto fresh = [&] { return stop.load(std::memory_order_relaxed) ||
+                                generation.load(std::memory_order_acquire) != seen; };
+      if (!spinUntil(fresh)) {
+        std::unique_lock<std::mutex> g(m);
+        wake.wait(g, fresh);
+      }
+      if (stop.load())
+        return;
+      seen = generation.load(std::memory_order_acquire);
+      const size_t lo = std::min(bytes_, part_ * static_cast<size_t>(k));
+      const size_t hi = std::min(bytes_, lo + part_);
+      if (hi > lo)
+        std::memcpy(dst_ + lo, src_ + lo, hi - lo);
+      if (pending.fetch_sub(1, std::memory_order_acq_rel) == 1) {
+        std::lock_guard<std::mutex> g(m);
+        finished.notify_one();
+      }
+    }
+  }
+  std::vector<std::thread> threads;
+  std::mutex m;
+  std::condition_variable wake, finished;
+  std::atomic<uint64_t> generation{0};
+  std::atomic<int> pending{0};
+  std::atomic<bool> stop{false};
+  uint8_t *dst_ = nullptr;
+  const uint8_t *src_ = nullptr;
+  size_t bytes_ = 0, part_ = 0;
+};
+
+namespace {
+/// Host threads that help with a pageable copy (SYM_B200_HOST_COPY_THREADS,
+/// default a quarter of the hardware threads, 1 to 4, plus the caller).
+int hostCopyWorkers() {
+  if (const char *v = std::getenv("SYM_B200_HOST_COPY_THREADS"))
+    return std::max(0, std::atoi(v) - 1);
+  const int hw = static_cast<int>(std::thread::hardware_concurrency());
+  return std::clamp(hw / 4, 1, 4);
+}
+} // namespace
+
+bool CudaBackend::bounceH2D(void *dst, const void *src, size_t bytes) {
+  constexpr size_t kPiece = size_t(8) << 20;
+  if (!bounce_[0]) {
+    for (int k = 0; k < kBounceBuffers; ++k) {
+      int rc;
+      if ((rc = sbc_malloc_host(&bounce_[k], kPiece, 0)))
+        return fail("cudaHostAlloc(bounce)", rc);
+      if ((rc = sbc_event_create(&bounceFree_[k], 0)))
+        return fail("cudaEventCreate", rc);
+    }
+  }
+  if (!pool_)
+    pool_.reset(new HostCopyPool(hostCopyWorkers()));
+  const auto *s = static_cast<const uint8_t *>(src);
+  auto *d = static_cast<uint8_t *>(dst);
+  for (size_t off = 0, piece = 0; off < bytes; ++piece) {
+    const size_t n = std::min(kPiece, bytes - off);
+    const int k = static_cast<int>(piece % kBounceBuffers);
+    int rc;
+    if (bounceUsed_[k] && (rc = sbc_event_synchronize(bounceFree_[k]))) // its last DMA has read it
+      return fail("bounce buffer wait", rc);
+    pool_->copy(bounce_[k], s + off, n);
+    if ((rc = sbc_memcpy_h2d_async(d + off, bounce_[k], n, copy_)) || (rc = sbc_event_record(bounceFree_[k], copy_)))
+      return fail("bounce upload", rc);
+    bounceUsed_[k] = true;
+    ++copyCalls;
+    ++eventRecords;
+    off += n;
+  }
+  bouncedBytes += bytes;
+  return true;
+}
 
 bool CudaBackend::fail(const std::string &what, int status) {
   if (!failed_) {
@@ -59,6 +199,12 @@ CudaBackend::~CudaBackend() {
     sbc_free_device(status_);
   if (statusHost_)
     sbc_free_host(statusHost_);
+  for (int k = 0; k < kBounceBuffers; ++k) {
+    if (bounce_[k])
+      sbc_free_host(bounce_[k]);
+    if (bounceFree_[k])
+      sbc_event_destroy(bounceFree_[k]);
+  }
   for (void *e : {done_, fence_, start_, stop_, stagingReady_, stagingFree_})
     if (e)
       sbc_event_destroy(e);
@@ -80,12 +226,15 @@ bool CudaBackend::waitStream(const void *external) {
   return true;
 }
 
-bool CudaBackend::signalStream(const void *external, bool hasExternal) {
+bool CudaBackend::signalStream(const void *external, bool hasExternal, bool copyUsed) {
   int rc;
-  if ((rc = sbc_event_record(fence_, copy_)) || (rc = sbc_stream_wait_event(compute_, fence_)) ||
-      (rc = sbc_event_record(done_, compute_)))
+  // Join the copy stream into the compute stream only when this execution
+  // queued copies there; `done` then covers both.
+  if (copyUsed && ((rc = sbc_event_record(fence_, copy_)) || (rc = sbc_stream_wait_event(compute_, fence_))))
     return fail("cudaEventRecord", rc);
-  eventRecords += 2;
+  if ((rc = sbc_event_record(done_, compute_)))
+    return fail("cudaEventRecord", rc);
+  eventRecords += copyUsed ? 2 : 1;
   // A null handle is the legacy default stream, a real caller stream.
   if (hasExternal && (rc = sbc_stream_wait_event(const_cast<void *>(external), done_)))
     return fail("cudaStreamWaitEvent(caller stream)", rc);

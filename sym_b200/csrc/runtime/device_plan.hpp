@@ -20,8 +20,11 @@
 namespace reloc {
 namespace b200 {
 
-enum class Family { Generic = 0, Contiguous = 1, Transpose = 2 };
+enum class Family { Generic = 0, Contiguous = 1, Transpose = 2, Runs = 3 };
 const char *familyName(Family f);
+/// Launch the family kernel for `d` on `stream`, falling back to the generic
+/// kernel when the family's kernel does not take the descriptor.
+int launchFamily(Family f, const sbc_relocate &d, void *stream);
 
 /// Device copies of a lowered program's parameter blob, one per device,
 /// uploaded on first use and freed with the program. A bound program's

@@ -204,8 +204,8 @@ Route routeOf(const Implementation &row, const TransferOptions &o) {
 /// learn the route timing.
 std::optional<TransferError> finish(bool needsStatus, const std::string &classKey, CudaBackend &b,
                                     const TransferOptions &o, bool timed, Route route, int64_t bytes,
-                                    void *completionEvent = nullptr) {
-  if (!b.signalStream(o.callerStream, o.hasCallerStream))
+                                    void *completionEvent = nullptr, bool copyUsed = true) {
+  if (!b.signalStream(o.callerStream, o.hasCallerStream, copyUsed))
     return terr("backend_failure", b.error());
   int rc;
   if (completionEvent) {
@@ -221,22 +221,31 @@ std::optional<TransferError> finish(bool needsStatus, const std::string &classKe
     b.fail("completion", rc);
     return terr("backend_failure", b.error());
   }
-  int fault = 0;
-  if ((rc = sbc_device_fault(&fault))) {
-    b.fail("fault word", rc);
-    return terr("backend_failure", b.error());
+  // The fault word is written only by kernels with bounded waits; reading it
+  // synchronizes with the device, so skip it while none has launched.
+  const uint64_t waits = sbc_wait_launch_count();
+  if (waits != b.waitLaunchesChecked) {
+    int fault = 0;
+    if ((rc = sbc_device_fault(&fault))) {
+      b.fail("fault word", rc);
+      return terr("backend_failure", b.error());
+    }
+    b.waitLaunchesChecked = waits;
+    if (fault)
+      return terr("backend_failure", "a kernel's bounded wait for a TMA copy ran out; the output is incomplete");
   }
-  if (fault)
-    return terr("backend_failure", "a kernel's bounded wait for a TMA copy ran out; the output is incomplete");
   if (timed) {
     float ms = 0;
     if (sbc_event_elapsed_ms(b.startEvent(), b.stopEvent(), &ms) == 0 && bytes > 0) {
       auto &s = b.routeStats[classKey];
       const double spb = (ms * 1e-3) / static_cast<double>(bytes);
-      if (route == Route::DmaRing)
+      if (route == Route::DmaRing) {
         s.dmaSecondsPerByte = spb;
-      else if (route == Route::ZeroCopy)
+        ++s.dmaSamples;
+      } else if (route == Route::ZeroCopy) {
         s.zeroCopySecondsPerByte = spb;
+        ++s.zeroCopySamples;
+      }
     }
   }
   if (needsStatus) {
@@ -307,13 +316,29 @@ std::optional<TransferError> executeDispatch(DispatchRequest &req, CudaBackend &
     return terr("backend_failure", b.error());
   if (o.hasCallerStream && !b.waitStream(o.callerStream))
     return terr("backend_failure", b.error());
-  // Auto mode learns each H2D route's cost per plan class from event timings.
-  const bool timed = routeOf(req.selected, o) == Route::Auto && !o.asyncCompletion &&
-                     req.direction == TransferDirection::HostToDevice;
+  // Auto mode learns each H2D route's cost per plan class from event
+  // timings: every execution until both routes are measured, then one in 64,
+  // alternating between the faster route and the slower one, so a cold first
+  // measurement (ring allocation, first touch) does not decide for good.
+  bool timed = false;
+  CudaBackend::RouteStats *rs = nullptr;
+  if (routeOf(req.selected, o) == Route::Auto && !o.asyncCompletion &&
+      req.direction == TransferDirection::HostToDevice) {
+    rs = &b.routeStats[req.lowered->classKey];
+    const bool known = rs->known();
+    const uint32_t n = known ? ++rs->executions : 0;
+    timed = !known || (n & 63u) == 0;
+    rs->probe = known && (n & 127u) == 64;
+  }
   Route route = Route::Auto;
-  if (auto e = launch(req, b, o, timed, route))
+  const uint64_t copies0 = b.copyCalls;
+  auto e = launch(req, b, o, timed, route);
+  if (rs)
+    rs->probe = false; // only this execution
+  if (e)
     return e;
-  return finish(req.lowered->needsStatus, req.lowered->classKey, b, o, timed, route, req.program.plan.sourceBytes);
+  return finish(req.lowered->needsStatus, req.lowered->classKey, b, o, timed, route, req.program.plan.sourceBytes,
+                nullptr, timed || b.copyCalls != copies0);
 }
 
 std::optional<TransferError> executeSourceRows(const DispatchTemplate &t, CudaBackend &b, const void *rows,

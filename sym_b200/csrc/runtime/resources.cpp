@@ -82,6 +82,7 @@ struct Completion::State {
   void *event = nullptr;
   int device = -1;
   bool finished = false;
+  uint64_t waitsBefore = 0; // sbc_wait_launch_count() before the work was enqueued
   TransferOutcome outcome;
   std::shared_ptr<void> owners; // buffers kept alive until completion
   ~State() {
@@ -94,6 +95,11 @@ struct Completion::State {
   /// Finalize after the event completed: the device's fault word.
   void finalizeLocked() {
     finished = true;
+    if (sbc_wait_launch_count() == waitsBefore) { // no kernel that writes the fault word ran
+      outcome.completion = TransferCompletion::Complete;
+      owners.reset();
+      return;
+    }
     int fault = 0;
     int dev = -1;
     sbc_get_device(&dev);
@@ -205,6 +211,7 @@ Resources::submit(GroupRequest &group, const TransferOptions &options, std::shar
       state->event = nullptr;
       return terr("backend_failure", std::string("cudaEventCreate: ") + sbc_error_string(rc));
     }
+    state->waitsBefore = sbc_wait_launch_count();
     return executeGroup(group, b, o, state->event);
   });
   if (out.error) {

@@ -72,9 +72,11 @@ class _Handle:
 
     def __del__(self):
         ptr = getattr(self, "_ptr", None)
-        if ptr and ptr.value and self._free and _native._lib is not None:
-            getattr(_native._lib, self._free)(ptr)
-            self._ptr = ctypes.c_void_p()
+        native = globals().get("_native")  # None once the interpreter tears modules down
+        lib = getattr(native, "_lib", None)
+        if ptr and ptr.value and self._free and lib is not None:
+            getattr(lib, self._free)(ptr)
+            ptr.value = None
 
 
 class PlanHandle(_Handle):
