@@ -550,7 +550,7 @@ def _config_case(name):
     of one config. `kernel_bytes` is the algorithmic HBM traffic of one
     device-resident execution; `unit_per_step` the amount of the config's
     unit that one step moves."""
-    from helpers import encode, recipe_c1, recipe_c2, recipe_c3
+    from helpers import encode, recipe_c1, recipe_c2, recipe_c3, recipe_tc
 
     rng = np.random.default_rng(0)
     if name == "c1":
@@ -567,6 +567,14 @@ def _config_case(name):
                 "dst_bytes": px * 8, "kernel_bytes": 20 * px, "unit": "images/s", "unit_per_step": 64,
                 "workload": "c2_nchw_to_nhwc_pad4_f16", "shape": [64, 3, 224, 224], "dtype": "f32->f16",
                 "bytes_note": "12 B read + 8 B write per pixel"}
+    if name == "tc":  # the reference latency table's transpose + cast (rows of 1024 move intact)
+        shape = (128, 128, 1024)
+        n = 128 * 128 * 1024
+        src = rng.uniform(-1.0, 1.0, shape).astype(np.float32)
+        return {"blob": encode(recipe_tc(shape)), "layout": False, "symbols": {}, "params": {}, "src": src,
+                "dst_bytes": 2 * n, "kernel_bytes": 6 * n, "unit": "GB/s", "unit_per_step": 4 * n / 1e9,
+                "workload": "transpose_cast_128x128x1024_f32_f16", "shape": list(shape), "dtype": "f32->f16",
+                "bytes_note": "4 B read + 2 B write per element"}
     if name == "c3q_d2h":  # KV-cache eviction: f32 on the GPU -> int8 in host memory
         case = _config_case("c3q")
         case.update(d2h=True, workload="c3q_d2h_quantize_evict")
@@ -886,9 +894,10 @@ def run_latency(args):
 def main():
     parser = argparse.ArgumentParser()
     parser.add_argument("--config", default="c5",
-                        choices=["c1", "c2", "c3q", "c3d", "c3q_d2h", "c4", "c5", "latency"],
+                        choices=["c1", "c2", "c3q", "c3d", "c3q_d2h", "c4", "c5", "tc", "latency"],
                         help="c5 (default): the headline Llama-70B fetch; c4: Llama-7B, 32 layers; "
-                             "c1-c3d: the other configs on one GPU; latency: typed H2D call latency")
+                             "c1-c3d: the other configs on one GPU; tc: the transpose + cast of the reference's "
+                             "latency table; latency: typed H2D call latency")
     parser.add_argument("--kernel-case", action="store_true",
                         help="profiling case: the hot kernel alone on one device-resident matrix")
     parser.add_argument("--gpus", type=int, default=1)

@@ -469,11 +469,14 @@ __global__ void __launch_bounds__(256) k_narrow(const __grid_constant__ sbc_relo
 // so each destination row of that axis is one contiguous run of the source
 // (leading axes permuted: [B,S,H,D] -> [B,H,S,D], swaps of outer axes).
 // The box is cut into units of U = 16 / max(WS, WD) elements of the last
-// axis; thread i takes unit i in destination order, so a warp's loads and
-// stores are contiguous spans within a run. A unit's row resolves its outer
-// coordinates with one magic-number division per outer axis; rows inside an
-// outer pad take the fill. Parameters: one per tensor, or one per run (a
-// channel on an outer axis).
+// axis, taken in destination order. With V > 1 (rows a multiple of 32 * V
+// units long) a warp takes a span of 32 * V consecutive units inside one
+// row: it resolves the row's outer coordinates (one magic-number division
+// per outer axis) and parameter once, then lane l moves units l, l + 32, ...
+// so every load and store instruction of the warp is one contiguous span.
+// With V == 1 each thread resolves its own unit's row. Rows inside an outer
+// pad take the fill. Parameters: one per tensor, or one per run (a channel
+// on an outer axis).
 // ---------------------------------------------------------------------------
 
 struct RunsGeom {
@@ -481,74 +484,81 @@ struct RunsGeom {
   FastDiv ext[SBC_MAX_RANK - 1]; // box extents of the outer axes
 };
 
-template <int WS, int WD, int CHAIN>
-__global__ void __launch_bounds__(256) k_runs(const __grid_constant__ sbc_relocate d, const __grid_constant__ RunsGeom g,
-                                               uint32_t nunits) {
+/// Two f32 bit patterns narrowed to f16 (RNE) with one packed conversion,
+/// x0 in the low half; NaNs keep narrow_f16's payload rule.
+__device__ __forceinline__ uint32_t narrow2_f16(uint32_t x0, uint32_t x1) {
+  if (max(x0 & 0x7fffffffu, x1 & 0x7fffffffu) > 0x7f800000u)
+    return narrow_f16(x0) | (narrow_f16(x1) << 16);
+  const __half2 h = __floats2half2_rn(__uint_as_float(x0), __uint_as_float(x1));
+  return static_cast<uint32_t>(__half_as_ushort(__low2half(h))) |
+         (static_cast<uint32_t>(__half_as_ushort(__high2half(h))) << 16);
+}
+
+/// Row `row` of the box's outer axes: source and destination element offsets
+/// of its first cell, validity (false inside an outer pad) and the stage-0
+/// parameter (and zero point) of the run. False return: channel out of range.
+template <int CHAIN>
+__device__ __forceinline__ bool runs_row(const sbc_relocate &d, const RunsGeom &g, uint32_t row, int64_t &so,
+                                         int64_t &dg, bool &valid, float &p, int32_t &zp) {
+  constexpr bool kParam = CHAIN == CH_Q || CHAIN == CH_DQ || CHAIN == CH_DQ_F16 || CHAIN == CH_DQ_BF16;
+  const int last = d.rank - 1;
+  int64_t coords[SBC_MAX_RANK - 1];
+  so = 0;
+  dg = 0;
+  valid = true;
+#pragma unroll
+  for (int kk = 0; kk < SBC_MAX_RANK - 1; ++kk) {
+    const int k = SBC_MAX_RANK - 2 - kk; // innermost outer axis first
+    if (k >= last)
+      continue;
+    const uint32_t q = fdiv(row, g.ext[k]);
+    const int64_t c = d.box_lo[k] + (row - q * g.ext[k].d);
+    row = q;
+    coords[k] = c;
+    dg += c * d.dst_strides[k];
+    const int64_t v = c - d.pad_lo[k];
+    if (v < 0 || v >= d.extents[k])
+      valid = false;
+    else
+      so += v * d.src_strides[k];
+  }
+  if constexpr (kParam) {
+    const sbc_stage &s = d.stages[0];
+    int64_t c = 0;
+    if (s.channel == SBC_CH_AXIS) {
+      c = coords[s.ch_axis] / s.ch_div;
+      if (s.ch_mod)
+        c %= s.ch_mod;
+    }
+    if (c >= s.channel_length)
+      return false;
+    p = s.param[c];
+    zp = zp_of(s, c);
+  }
+  return true;
+}
+
+/// Convert one unit (U source cells) and store it at `dp`.
+template <int WS, int WD, int CHAIN, typename SU, typename DU>
+__device__ __forceinline__ void runs_unit(const SU &src, DU *dp, float p, int32_t zp) {
   using S = typename Word<WS>::T;
   using D = typename Word<WD>::T;
   constexpr int U = Units<WS, WD>::U;
-  using SU = typename Bytes<U * WS>::T;
-  using DU = typename Bytes<U * WD>::T;
-  constexpr bool kParam = CHAIN == CH_Q || CHAIN == CH_DQ || CHAIN == CH_DQ_F16 || CHAIN == CH_DQ_BF16;
-  const int last = d.rank - 1;
-  const S *src = static_cast<const S *>(d.src) + (d.box_lo[last] - d.pad_lo[last] - d.src_offset);
-  D *dst = static_cast<D *>(d.dst) + (d.box_lo[last] - d.dst_offset);
-  const sbc_stage &s = d.stages[0];
-  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < nunits; i += gridDim.x * blockDim.x) {
-    uint32_t row = fdiv(i, g.upr);
-    const int64_t j = static_cast<int64_t>(i - row * g.upr.d) * U;
-    int64_t so = 0, dg = 0;
-    int64_t coords[SBC_MAX_RANK - 1];
-    bool valid = true;
+  union {
+    SU q;
+    S e[U];
+  } in;
+  in.q = src;
+  union {
+    DU q;
+    D e[U];
+    uint32_t w[(U * WD + 3) / 4];
+  } out;
+  if constexpr (CHAIN == CH_F16 && WS == 4 && WD == 2) {
 #pragma unroll
-    for (int kk = 0; kk < SBC_MAX_RANK - 1; ++kk) {
-      const int k = SBC_MAX_RANK - 2 - kk; // innermost outer axis first
-      if (k >= last)
-        continue;
-      const uint32_t q = fdiv(row, g.ext[k]);
-      const int64_t c = d.box_lo[k] + (row - q * g.ext[k].d);
-      row = q;
-      coords[k] = c;
-      dg += c * d.dst_strides[k];
-      const int64_t v = c - d.pad_lo[k];
-      if (v < 0 || v >= d.extents[k])
-        valid = false;
-      else
-        so += v * d.src_strides[k];
-    }
-    union {
-      DU q;
-      D e[U];
-    } out;
-    DU *dp = reinterpret_cast<DU *>(dst + dg + j);
-    if (!valid) {
-#pragma unroll
-      for (int u = 0; u < U; ++u)
-        out.e[u] = static_cast<D>(d.fill_bits);
-      __stcs(dp, out.q);
-      continue;
-    }
-    union {
-      SU q;
-      S e[U];
-    } in;
-    in.q = __ldcs(reinterpret_cast<const SU *>(src + so + j));
-    float p = 0.0f;
-    int32_t zp = 0;
-    if constexpr (kParam) {
-      int64_t c = 0;
-      if (s.channel == SBC_CH_AXIS) {
-        c = coords[s.ch_axis] / s.ch_div;
-        if (s.ch_mod)
-          c %= s.ch_mod;
-      }
-      if (c >= s.channel_length) {
-        flag(d);
-        continue;
-      }
-      p = s.param[c];
-      zp = zp_of(s, c);
-    }
+    for (int u = 0; u < U; u += 2)
+      out.w[u / 2] = narrow2_f16(in.e[u], in.e[u + 1]);
+  } else {
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       uint32_t v = static_cast<uint32_t>(in.e[u]);
@@ -570,7 +580,86 @@ __global__ void __launch_bounds__(256) k_runs(const __grid_constant__ sbc_reloca
         v = narrow_bf16(dequantize(v, zp, p));
       out.e[u] = static_cast<D>(v);
     }
-    __stcs(dp, out.q);
+  }
+  __stcs(dp, out.q);
+}
+
+template <int WS, int WD, int CHAIN, int V>
+__global__ void __launch_bounds__(256) k_runs(const __grid_constant__ sbc_relocate d, const __grid_constant__ RunsGeom g,
+                                               uint32_t nunits) {
+  using S = typename Word<WS>::T;
+  using D = typename Word<WD>::T;
+  constexpr int U = Units<WS, WD>::U;
+  using SU = typename Bytes<U * WS>::T;
+  using DU = typename Bytes<U * WD>::T;
+  const int last = d.rank - 1;
+  const S *src = static_cast<const S *>(d.src) + (d.box_lo[last] - d.pad_lo[last] - d.src_offset);
+  D *dst = static_cast<D *>(d.dst) + (d.box_lo[last] - d.dst_offset);
+  if constexpr (V == 1) {
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < nunits; i += gridDim.x * blockDim.x) {
+      const uint32_t row = fdiv(i, g.upr);
+      const int64_t j = static_cast<int64_t>(i - row * g.upr.d) * U;
+      int64_t so, dg;
+      bool valid;
+      float p = 0.0f;
+      int32_t zp = 0;
+      if (!runs_row<CHAIN>(d, g, row, so, dg, valid, p, zp)) {
+        flag(d);
+        continue;
+      }
+      DU *dp = reinterpret_cast<DU *>(dst + dg + j);
+      if (!valid) {
+        union {
+          DU q;
+          D e[U];
+        } out;
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+          out.e[u] = static_cast<D>(d.fill_bits);
+        __stcs(dp, out.q);
+        continue;
+      }
+      runs_unit<WS, WD, CHAIN>(__ldcs(reinterpret_cast<const SU *>(src + so + j)), dp, p, zp);
+    }
+  } else {
+    const int lane = threadIdx.x & 31;
+    const uint32_t nspans = nunits / (32 * V); // host: rows are whole spans
+    const uint32_t warps = gridDim.x * (blockDim.x / 32);
+    for (uint32_t sp = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5); sp < nspans; sp += warps) {
+      const uint32_t u0 = sp * (32 * V);
+      const uint32_t row = fdiv(u0, g.upr);
+      const int64_t j0 = static_cast<int64_t>(u0 - row * g.upr.d + lane) * U;
+      int64_t so, dg;
+      bool valid;
+      float p = 0.0f;
+      int32_t zp = 0;
+      if (!runs_row<CHAIN>(d, g, row, so, dg, valid, p, zp)) {
+        flag(d);
+        continue;
+      }
+      DU *dp = reinterpret_cast<DU *>(dst + dg + j0);
+      if (!valid) {
+        union {
+          DU q;
+          D e[U];
+        } out;
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+          out.e[u] = static_cast<D>(d.fill_bits);
+#pragma unroll
+        for (int v = 0; v < V; ++v)
+          __stcs(dp + v * 32, out.q);
+        continue;
+      }
+      const SU *sp_ = reinterpret_cast<const SU *>(src + so + j0);
+      SU in[V];
+#pragma unroll
+      for (int v = 0; v < V; ++v)
+        in[v] = __ldcs(sp_ + v * 32);
+#pragma unroll
+      for (int v = 0; v < V; ++v)
+        runs_unit<WS, WD, CHAIN>(in[v], dp + v * 32, p, zp);
+    }
   }
 }
 
@@ -1670,8 +1759,17 @@ template <int WS, int WD, int CH> struct RunsLaunch {
     if constexpr (WS == 8 || WD == 8 || CH == CH_ANY) {
       return SBC_EUNSUPPORTED;
     } else {
-      const int64_t blocks = grid_for(nunits, 256, 8);
-      k_runs<WS, WD, CH><<<static_cast<unsigned>(blocks), 256, 0, s>>>(d, g, nunits);
+      const uint32_t upr = g.upr.d;
+      if (upr % 128 == 0) { // spans of 32 x 4 units inside a row
+        const int64_t blocks = grid_for(nunits / 128 * 32, 256, 8);
+        k_runs<WS, WD, CH, 4><<<static_cast<unsigned>(blocks), 256, 0, s>>>(d, g, nunits);
+      } else if (upr % 64 == 0) {
+        const int64_t blocks = grid_for(nunits / 64 * 32, 256, 8);
+        k_runs<WS, WD, CH, 2><<<static_cast<unsigned>(blocks), 256, 0, s>>>(d, g, nunits);
+      } else {
+        const int64_t blocks = grid_for(nunits, 256, 8);
+        k_runs<WS, WD, CH, 1><<<static_cast<unsigned>(blocks), 256, 0, s>>>(d, g, nunits);
+      }
       return launched(cudaSuccess);
     }
   }

@@ -82,6 +82,18 @@ def recipe_c3(direction="quantize", scale_bits=0x3D4CCCCD, hidden=4096):
     return R.Recipe(src, ops, dst, "h2d")
 
 
+def recipe_tc(shape=(128, 128, 1024)):
+    """The reference typed-H2D latency table's transpose + cast: f32
+    [A, B, C] -> swap axes 0/1 -> f16 [B, A, C] (rows of C move intact)."""
+    from sym_b200.reloc_torch import recipe as R
+    from sym_b200.reloc_torch import symbolic as S
+
+    a, b, c = (S.Const(x) for x in shape)
+    src = R.TensorSpec((a, b, c), S.dense_strides((a, b, c)), S.Const(0), "float32")
+    dst = R.TensorSpec((b, a, c), S.dense_strides((b, a, c)), S.Const(0), "float16")
+    return R.Recipe(src, (R.Transpose((1, 0, 2)), R.Cast("float16", "ieee_rne")), dst, "h2d")
+
+
 def recipe_c4(out_dtype="float16"):
     """C4/C5: int8 [out, in] + per-row f32 scale -> dequantize (axis 0) ->
     cast f16 -> transpose -> f16 [in, out]; out/in symbolic, scale a binding."""

@@ -202,7 +202,11 @@ def _runs_recipe(shape, perm, op, pad=None, src_dtype="float32"):
     ((2, 3, 4, 64), (1, 0, 2, 3), "f16", (0, 1, 2)),
     ((2, 3, 4, 64), (0, 2, 1, 3), "quantize", (2, 2, 0)),
     ((2, 3, 30), (1, 0, 2), "f16", None),          # rows not a whole number of vectors: generic kernel
-    ((128, 128, 1024), (1, 0, 2), "f16", None),    # the transpose + cast latency case
+    ((128, 128, 1024), (1, 0, 2), "f16", None),    # the transpose + cast latency case (warp spans of 4)
+    ((4, 6, 256), (1, 0, 2), "f16", None),         # warp spans of 2 units per lane
+    ((2, 3, 512), (1, 0, 2), "bf16", (0, 1, 1)),   # spans over an outer pad
+    ((2, 16, 8, 512), (0, 2, 1, 3), "dequantize_axis1", None),  # a per-run scale with spans
+    ((6, 4, 128), (1, 0, 2), "quantize", None),
 ])
 def test_outer_permutation_runs(shape, perm, op, pad):
     """Permutations that move whole unit-stride rows (attention-style
