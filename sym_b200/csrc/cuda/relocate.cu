@@ -390,15 +390,96 @@ template <int BYTES> struct StoreVec { using T = uint4; };
 template <> struct StoreVec<8> { using T = uint2; };
 template <> struct StoreVec<4> { using T = uint32_t; };
 
+/// Two f32 bit patterns narrowed to f16 (RNE) with one packed conversion,
+/// x0 in the low half; NaNs keep narrow_f16's payload rule.
+__device__ __forceinline__ uint32_t narrow2_f16(uint32_t x0, uint32_t x1) {
+  if (max(x0 & 0x7fffffffu, x1 & 0x7fffffffu) > 0x7f800000u)
+    return narrow_f16(x0) | (narrow_f16(x1) << 16);
+  const __half2 h = __floats2half2_rn(__uint_as_float(x0), __uint_as_float(x1));
+  return static_cast<uint32_t>(__half_as_ushort(__low2half(h))) |
+         (static_cast<uint32_t>(__half_as_ushort(__high2half(h))) << 16);
+}
+
+/// One k_narrow item: VA source cells of axis A from each of the NB planes
+/// (16-byte loads already issued into `in`; pad planes take the fill),
+/// converted and stored as one contiguous run of VA x NB cells at `dp`.
 template <int WS, int WD, int CHAIN, int NB>
-__global__ void __launch_bounds__(256) k_narrow(const __grid_constant__ sbc_relocate d, FastDiv per_batch,
-                                                 uint32_t total) {
+__device__ __forceinline__ void narrow_item(const uint4 (&in)[NB], const bool (&valid)[NB], uint8_t *dp,
+                                            uint32_t fill, float p0, int32_t zp0) {
   using S = typename Word<WS>::T;
   using D = typename Word<WD>::T;
   constexpr int VA = 16 / WS;
-  constexpr int RUN = VA * NB * WD; // bytes a thread writes
+  constexpr int RUN = VA * NB * WD;
   constexpr int SV = RUN % 16 == 0 ? 16 : RUN % 8 == 0 ? 8 : 4;
   using ST = typename StoreVec<SV>::T;
+  union {
+    ST q[RUN / SV];
+    D e[VA * NB];
+    uint32_t w[(RUN + 3) / 4];
+  } out;
+  if constexpr (CHAIN == CH_F16 && WS == 4 && WD == 2 && NB % 2 == 0) {
+    // channel pairs (j, j + 1) of one cell: one packed conversion
+#pragma unroll
+    for (int j = 0; j < NB; j += 2) {
+      const uint4 x = in[j], y = in[j + 1];
+      const uint32_t xs[4] = {x.x, x.y, x.z, x.w}, ys[4] = {y.x, y.y, y.z, y.w};
+#pragma unroll
+      for (int i = 0; i < VA; ++i) {
+        uint32_t w;
+        if (valid[j] && valid[j + 1])
+          w = narrow2_f16(xs[i], ys[i]);
+        else if (valid[j])
+          w = narrow_f16(xs[i]) | (fill << 16);
+        else if (valid[j + 1])
+          w = fill | (narrow_f16(ys[i]) << 16);
+        else
+          w = fill | (fill << 16);
+        out.w[(i * NB + j) / 2] = w;
+      }
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < NB; ++j) {
+      union {
+        uint4 q;
+        S e[VA];
+      } v;
+      v.q = in[j];
+#pragma unroll
+      for (int i = 0; i < VA; ++i) {
+        uint32_t x = static_cast<uint32_t>(v.e[i]);
+        if constexpr (CHAIN == CH_F16)
+          x = narrow_f16(x);
+        else if constexpr (CHAIN == CH_BF16)
+          x = narrow_bf16(x);
+        else if constexpr (CHAIN == CH_W16)
+          x = widen_f16(x);
+        else if constexpr (CHAIN == CH_WB16)
+          x = widen_bf16(x);
+        else if constexpr (CHAIN == CH_Q)
+          x = quantize(x, p0);
+        else if constexpr (CHAIN == CH_DQ)
+          x = dequantize(x, zp0, p0);
+        out.e[i * NB + j] = static_cast<D>(valid[j] ? x : fill);
+      }
+    }
+  }
+  ST *sp = reinterpret_cast<ST *>(dp);
+#pragma unroll
+  for (int i = 0; i < RUN / SV; ++i)
+    __stcs(sp + i, out.q[i]);
+}
+
+/// V == 1: one item per thread (each resolves its own batch index). V > 1
+/// (the host checks that a batch holds a whole number of 32 * V items): a
+/// warp takes 32 * V consecutive items of one batch, resolves the batch and
+/// the base offsets once, and lane l takes items l, l + 32, ..., issuing all
+/// of its 16-byte loads before the first conversion.
+template <int WS, int WD, int CHAIN, int NB, int V>
+__global__ void __launch_bounds__(256) k_narrow(const __grid_constant__ sbc_relocate d, FastDiv per_batch,
+                                                 uint32_t total) {
+  using S = typename Word<WS>::T;
+  constexpr int VA = 16 / WS;
   const int ax_a = d.rank - 2, ax_b = d.rank - 1;
   const int64_t Sb = d.src_strides[ax_b];
   const int64_t lo_b = d.pad_lo[ax_b], hi_b = d.pad_lo[ax_b] + d.extents[ax_b];
@@ -412,55 +493,52 @@ __global__ void __launch_bounds__(256) k_narrow(const __grid_constant__ sbc_relo
     p0 = s.param[0];
     zp0 = zp_of(s, 0);
   }
-  for (uint32_t g = blockIdx.x * blockDim.x + threadIdx.x; g < total; g += gridDim.x * blockDim.x) {
+  const uint32_t fill = static_cast<uint32_t>(static_cast<typename Word<WD>::T>(d.fill_bits));
+  bool valid[NB];
+#pragma unroll
+  for (int j = 0; j < NB; ++j)
+    valid[j] = b0 + j >= lo_b && b0 + j < hi_b;
+  // element offsets of item g's first source cell (plane b0) and destination cell
+  auto bases = [&](uint32_t g, int64_t &sbase, int64_t &dbase) {
     const uint32_t n = d.rank == 3 ? fdiv(g, per_batch) : 0; // total < 2^31 (host-checked)
     const int64_t a = d.box_lo[ax_a] + static_cast<int64_t>(g - n * per_batch.d) * VA;
-    int64_t sbase = (a - d.pad_lo[ax_a]) - d.src_offset;
-    int64_t dbase = a * d.dst_strides[ax_a] + b0 - d.dst_offset;
+    sbase = (a - d.pad_lo[ax_a]) - d.src_offset + (b0 - lo_b) * Sb;
+    dbase = a * NB + b0 - d.dst_offset; // dst_strides[ax_a] == NB (host-checked)
     if (d.rank == 3) {
       sbase += (d.box_lo[0] + n - d.pad_lo[0]) * d.src_strides[0];
       dbase += (d.box_lo[0] + n) * d.dst_strides[0];
     }
-    union {
-      ST q[RUN / SV];
-      D e[VA * NB];
-    } out;
+  };
+  if constexpr (V == 1) {
+    for (uint32_t g = blockIdx.x * blockDim.x + threadIdx.x; g < total; g += gridDim.x * blockDim.x) {
+      int64_t sbase, dbase;
+      bases(g, sbase, dbase);
+      uint4 in[NB] = {};
 #pragma unroll
-    for (int j = 0; j < NB; ++j) {
-      const int64_t b = b0 + j;
-      if (b >= lo_b && b < hi_b) {
-        union {
-          uint4 q;
-          S e[VA];
-        } in;
-        in.q = __ldcs(reinterpret_cast<const uint4 *>(src + sbase + (b - lo_b) * Sb));
-#pragma unroll
-        for (int i = 0; i < VA; ++i) {
-          uint32_t v = static_cast<uint32_t>(in.e[i]);
-          if constexpr (CHAIN == CH_F16)
-            v = narrow_f16(v);
-          else if constexpr (CHAIN == CH_BF16)
-            v = narrow_bf16(v);
-          else if constexpr (CHAIN == CH_W16)
-            v = widen_f16(v);
-          else if constexpr (CHAIN == CH_WB16)
-            v = widen_bf16(v);
-          else if constexpr (CHAIN == CH_Q)
-            v = quantize(v, p0);
-          else if constexpr (CHAIN == CH_DQ)
-            v = dequantize(v, zp0, p0);
-          out.e[i * NB + j] = static_cast<D>(v);
-        }
-      } else {
-#pragma unroll
-        for (int i = 0; i < VA; ++i)
-          out.e[i * NB + j] = static_cast<D>(d.fill_bits);
-      }
+      for (int j = 0; j < NB; ++j)
+        if (valid[j])
+          in[j] = __ldcs(reinterpret_cast<const uint4 *>(src + sbase + j * Sb));
+      narrow_item<WS, WD, CHAIN, NB>(in, valid, dst + dbase * WD, fill, p0, zp0);
     }
-    ST *dp = reinterpret_cast<ST *>(dst + dbase * WD);
+  } else {
+    const int lane = threadIdx.x & 31;
+    const uint32_t nspans = total / (32 * V);
+    const uint32_t warps = gridDim.x * (blockDim.x / 32);
+    for (uint32_t sp = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5); sp < nspans; sp += warps) {
+      int64_t sbase, dbase;
+      bases(sp * (32 * V), sbase, dbase);
+      uint4 in[V][NB] = {};
 #pragma unroll
-    for (int i = 0; i < RUN / SV; ++i)
-      __stcs(dp + i, out.q[i]);
+      for (int v = 0; v < V; ++v)
+#pragma unroll
+        for (int j = 0; j < NB; ++j)
+          if (valid[j])
+            in[v][j] = __ldcs(reinterpret_cast<const uint4 *>(src + sbase + j * Sb + (v * 32 + lane) * VA));
+#pragma unroll
+      for (int v = 0; v < V; ++v)
+        narrow_item<WS, WD, CHAIN, NB>(in[v], valid, dst + (dbase + (v * 32 + lane) * VA * NB) * WD, fill, p0,
+                                       zp0);
+    }
   }
 }
 
@@ -483,16 +561,6 @@ struct RunsGeom {
   FastDiv upr;                   // units per row of the last axis
   FastDiv ext[SBC_MAX_RANK - 1]; // box extents of the outer axes
 };
-
-/// Two f32 bit patterns narrowed to f16 (RNE) with one packed conversion,
-/// x0 in the low half; NaNs keep narrow_f16's payload rule.
-__device__ __forceinline__ uint32_t narrow2_f16(uint32_t x0, uint32_t x1) {
-  if (max(x0 & 0x7fffffffu, x1 & 0x7fffffffu) > 0x7f800000u)
-    return narrow_f16(x0) | (narrow_f16(x1) << 16);
-  const __half2 h = __floats2half2_rn(__uint_as_float(x0), __uint_as_float(x1));
-  return static_cast<uint32_t>(__half_as_ushort(__low2half(h))) |
-         (static_cast<uint32_t>(__half_as_ushort(__high2half(h))) << 16);
-}
 
 /// Row `row` of the box's outer axes: source and destination element offsets
 /// of its first cell, validity (false inside an outer pad) and the stage-0
@@ -1738,19 +1806,44 @@ bool basic_ok(const sbc_relocate &d) {
   return true;
 }
 
+// Widest warp span of k_narrow (items per lane). Measured on C2 (f32 NCHW
+// [64,3,224,224] -> f16 NHWC, pad 3 -> 4): one item per thread 17.4 us,
+// residency-capped spans of 2 14.3-15.4 us, spans of 4 (89 registers,
+// 2 blocks per SM) 16.4-17.3 us.
+#ifndef SBC_NARROW_VMAX
+#define SBC_NARROW_VMAX 2
+#endif
+
+
 template <int WS, int WD, int CH>
 int launch_narrow(const sbc_relocate &d, int nb, int64_t per_batch, int64_t total, cudaStream_t s) {
-  // One item per thread (the grid-stride loop runs once): every load of the
-  // whole launch is issued in the first waves instead of a capped grid's
-  // threads walking several items each.
-  const unsigned blocks = static_cast<unsigned>((total + 255) / 256);
   const FastDiv pb = make_fastdiv(static_cast<uint32_t>(per_batch));
   const uint32_t n = static_cast<uint32_t>(total);
+  // Warp spans of 32 x V items when a batch holds whole spans (all of a
+  // lane's loads first; the grid is what stays resident, warps loop over
+  // spans); otherwise one item per thread.
+  constexpr int VMAX = SBC_NARROW_VMAX;
+  const int v = VMAX >= 4 && per_batch % 128 == 0 ? 4 : VMAX >= 2 && per_batch % 64 == 0 ? 2 : 1;
+  auto grid = [&](auto kernel) -> unsigned {
+    if (v == 1)
+      return static_cast<unsigned>((total + 255) / 256);
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, 256, 0) != cudaSuccess || per_sm < 1)
+      per_sm = 1;
+    const int64_t want = (total / (32 * v) + 7) / 8, cap = static_cast<int64_t>(sm_count()) * per_sm;
+    return static_cast<unsigned>(want < cap ? want : cap);
+  };
+#define SBC_NARROW(NB_, V_)                                                                                  \
+  k_narrow<WS, WD, CH, NB_, V_><<<grid(k_narrow<WS, WD, CH, NB_, V_>), 256, 0, s>>>(d, pb, n)
+#define SBC_NARROW_V(NB_)                                                                                    \
+  (v == 4 ? SBC_NARROW(NB_, 4) : v == 2 ? SBC_NARROW(NB_, 2) : SBC_NARROW(NB_, 1))
   switch (nb) {
-  case 2: k_narrow<WS, WD, CH, 2><<<blocks, 256, 0, s>>>(d, pb, n); break;
-  case 3: k_narrow<WS, WD, CH, 3><<<blocks, 256, 0, s>>>(d, pb, n); break;
-  default: k_narrow<WS, WD, CH, 4><<<blocks, 256, 0, s>>>(d, pb, n); break;
+  case 2: SBC_NARROW_V(2); break;
+  case 3: SBC_NARROW_V(3); break;
+  default: SBC_NARROW_V(4); break;
   }
+#undef SBC_NARROW_V
+#undef SBC_NARROW
   return launched(cudaSuccess);
 }
 
