@@ -318,8 +318,9 @@ std::optional<TransferError> executeDispatch(DispatchRequest &req, CudaBackend &
     return terr("backend_failure", b.error());
   // Auto mode learns each H2D route's cost per plan class from event
   // timings: every execution until both routes are measured, then one in 64,
-  // alternating between the faster route and the slower one, so a cold first
-  // measurement (ring allocation, first touch) does not decide for good.
+  // and the slower route is measured again after 4, 16 and then every 128
+  // executions, so a cold early sample (ring allocation, first touch of the
+  // source, a link leaving its idle state) does not decide for good.
   bool timed = false;
   CudaBackend::RouteStats *rs = nullptr;
   if (routeOf(req.selected, o) == Route::Auto && !o.asyncCompletion &&
@@ -327,8 +328,8 @@ std::optional<TransferError> executeDispatch(DispatchRequest &req, CudaBackend &
     rs = &b.routeStats[req.lowered->classKey];
     const bool known = rs->known();
     const uint32_t n = known ? ++rs->executions : 0;
-    timed = !known || (n & 63u) == 0;
-    rs->probe = known && (n & 127u) == 64;
+    rs->probe = known && (n == 4 || n == 16 || (n & 127u) == 64);
+    timed = !known || rs->probe || (n & 63u) == 0;
   }
   Route route = Route::Auto;
   const uint64_t copies0 = b.copyCalls;
