@@ -8,6 +8,7 @@
 #define SYM_B200_RELOC_CUDABACKEND_H
 
 #include <cstddef>
+#include <climits>
 #include <cstdint>
 #include <map>
 #include <memory>
@@ -70,6 +71,22 @@ public:
   void *stopEvent() const { return stop_; }
 
   size_t deviceBytes() const;
+  /// Scratch budget of this context (the owner's limits divided among its
+  /// contexts): `liveLimit` caps the device scratch an execution may hold
+  /// (0 = unlimited); scratch beyond `retainedLimit` is released when a
+  /// blocking execution's lease ends.
+  size_t liveLimit = 0;
+  size_t retainedLimit = SIZE_MAX;
+  /// Bytes a ring slot may take for `slots` slots under the live limit (and,
+  /// when `retained`, also the retained limit), after the other scratch.
+  size_t ringSlotBudget(int slots, bool retained) const;
+  /// Release ring and staging scratch until at most `keep` bytes remain
+  /// (waits for queued work first). Returns whether anything was released.
+  bool trim(size_t keep);
+  size_t peakDeviceBytes = 0;
+  uint64_t trims = 0;
+  size_t ringBytes() const { return ring_.size() * slotBytes_; }
+  size_t stagingCapacity() const { return stagingBytes_; }
   uint64_t copyCalls = 0;
   uint64_t eventRecords = 0;
   uint64_t eventWaits = 0;

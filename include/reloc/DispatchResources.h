@@ -54,11 +54,14 @@ struct ResourceStats {
   bool closed = false, quarantined = false;
   size_t retainedLimit = 0, liveLimit = 0;
   unsigned contextLimit = 0;
+  size_t peakLiveBytes = 0; // sum over contexts of each one's peak scratch
+  uint64_t releases = 0;    // scratch releases at lease end (over the retained quota)
+  uint64_t evictions = 0;   // contexts retired to admit one for another device
 };
 
 class Resources {
 public:
-  explicit Resources(size_t maxRetainedBytes = size_t(256) << 20, size_t maxLiveBytes = 0, unsigned maxContexts = 8);
+  explicit Resources(size_t maxRetainedBytes = size_t(64) << 20, size_t maxLiveBytes = 0, unsigned maxContexts = 1);
   ~Resources();
   Resources(const Resources &) = delete;
   Resources &operator=(const Resources &) = delete;
@@ -75,7 +78,13 @@ public:
   std::variant<std::shared_ptr<Completion>, TransferError> submit(GroupRequest &group, const TransferOptions &options,
                                                                   std::shared_ptr<void> owners);
   /// Run `fn` with the leased context of `device` (window/device executions).
-  TransferOutcome withContext(int device, const std::function<std::optional<TransferError>(CudaBackend &)> &fn);
+  /// With `releaseAfter` (blocking work), scratch beyond the context's
+  /// retained quota is released before the lease ends. Each context holds
+  /// an equal share of the owner's retained and live limits; a nonzero live
+  /// limit caps the scratch one execution may hold (insufficient_capacity
+  /// when a plan cannot run within it), zero leaves it unlimited.
+  TransferOutcome withContext(int device, const std::function<std::optional<TransferError>(CudaBackend &)> &fn,
+                              bool releaseAfter = true);
 
   ResourceStats stats() const;
   std::optional<TransferError> clear();
@@ -85,10 +94,14 @@ private:
   struct Slot {
     std::unique_ptr<CudaBackend> backend;
     std::mutex lease;
+    uint64_t lastUse = 0;
   };
-  std::optional<TransferError> acquire(int device, Slot *&slot);
+  /// The context of `device`; at the context limit the least recently used
+  /// context is retired (its scratch is freed once its current lease ends).
+  std::optional<TransferError> acquire(int device, std::shared_ptr<Slot> &slot);
   mutable std::mutex mutex_;
-  std::map<int, std::unique_ptr<Slot>> slots_;
+  std::map<int, std::shared_ptr<Slot>> slots_;
+  uint64_t clock_ = 0, evictions_ = 0;
   size_t maxRetained_, maxLive_;
   unsigned maxContexts_;
   bool closed_ = false, quarantined_ = false;

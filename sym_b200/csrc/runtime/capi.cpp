@@ -549,7 +549,7 @@ int sb_execute_rows(const sb_template *t, sb_resources *res, int32_t device, con
   };
   TransferOutcome out;
   if (res) {
-    out = res->res.withContext(device, fn);
+    out = res->res.withContext(device, fn, !o.asyncCompletion);
   } else {
     dispatch::Resources local(0, 0, 1);
     out = local.withContext(device, fn);
@@ -572,7 +572,7 @@ int sb_execute_source_rows(const sb_template *t, sb_resources *res, int32_t devi
   };
   TransferOutcome out;
   if (res) {
-    out = res->res.withContext(device, fn);
+    out = res->res.withContext(device, fn, !o.asyncCompletion);
   } else {
     dispatch::Resources local(0, 0, 1);
     out = local.withContext(device, fn);
@@ -595,7 +595,7 @@ int sb_execute_source_shards(const sb_template *t, sb_resources *res, int32_t de
   };
   TransferOutcome out;
   if (res) {
-    out = res->res.withContext(device, fn);
+    out = res->res.withContext(device, fn, !o.asyncCompletion);
   } else {
     dispatch::Resources local(0, 0, 1);
     out = local.withContext(device, fn);
@@ -666,17 +666,21 @@ int sb_resources_stats(const sb_resources *r, char *json, size_t cap) {
      << ",\"caller_waits\":" << s.callerWaits << ",\"kernel_launches\":" << s.kernelLaunches
      << ",\"closed\":" << (s.closed ? "true" : "false") << ",\"quarantined\":" << (s.quarantined ? "true" : "false")
      << ",\"retained_limit\":" << s.retainedLimit << ",\"live_limit\":" << s.liveLimit
-     << ",\"context_limit\":" << s.contextLimit << "}";
+     << ",\"context_limit\":" << s.contextLimit << ",\"peak_live_bytes\":" << s.peakLiveBytes
+     << ",\"releases\":" << s.releases << "}";
   return putJson(os.str(), json, cap);
 }
 
 int sb_resources_streams(sb_resources *r, int32_t device, void **copy_stream, void **compute_stream,
                          sb_error *err) {
-  auto out = r->res.withContext(device, [&](CudaBackend &b) -> std::optional<TransferError> {
-    *copy_stream = b.copyStream();
-    *compute_stream = b.computeStream();
-    return std::nullopt;
-  });
+  auto out = r->res.withContext(
+      device,
+      [&](CudaBackend &b) -> std::optional<TransferError> {
+        *copy_stream = b.copyStream();
+        *compute_stream = b.computeStream();
+        return std::nullopt;
+      },
+      false); // a query: queued work stays as it is
   if (out.error)
     return setErr(err, out.error->code, out.error->message);
   return 0;

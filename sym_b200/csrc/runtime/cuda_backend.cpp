@@ -183,6 +183,8 @@ std::unique_ptr<CudaBackend> CudaBackend::create(int device, std::string &error)
 CudaBackend::~CudaBackend() {
   if (device_ < 0)
     return;
+  int current = -1; // restored below: retiring a context leaves the caller's device alone
+  sbc_get_device(&current);
   sbc_set_device(device_);
   quiesce();
   for (void *p : ring_)
@@ -212,6 +214,8 @@ CudaBackend::~CudaBackend() {
     sbc_stream_destroy(copy_);
   if (compute_)
     sbc_stream_destroy(compute_);
+  if (current >= 0 && current != device_)
+    sbc_set_device(current);
 }
 
 bool CudaBackend::waitStream(const void *external) {
@@ -279,6 +283,7 @@ bool CudaBackend::ensureRing(int slots, size_t bytes) {
     }
   }
   slotBytes_ = want;
+  peakDeviceBytes = std::max(peakDeviceBytes, deviceBytes());
   return true;
 }
 
@@ -296,6 +301,7 @@ void *CudaBackend::staging(size_t bytes) {
     return nullptr;
   }
   stagingBytes_ = bytes;
+  peakDeviceBytes = std::max(peakDeviceBytes, deviceBytes());
   return staging_;
 }
 
@@ -315,9 +321,37 @@ void *CudaBackend::params(size_t bytes) {
     return nullptr;
   }
   paramBytes_ = bytes;
+  peakDeviceBytes = std::max(peakDeviceBytes, deviceBytes());
   return params_;
 }
 
 size_t CudaBackend::deviceBytes() const { return ring_.size() * slotBytes_ + stagingBytes_ + paramBytes_ + 16; }
+
+size_t CudaBackend::ringSlotBudget(int slots, bool retained) const {
+  size_t limit = liveLimit ? liveLimit : SIZE_MAX;
+  if (retained && retainedLimit < limit)
+    limit = retainedLimit;
+  if (limit == SIZE_MAX)
+    return SIZE_MAX;
+  const size_t other = stagingBytes_ + paramBytes_ + 16;
+  return limit > other ? (limit - other) / static_cast<size_t>(slots > 0 ? slots : 1) : 0;
+}
+
+bool CudaBackend::trim(size_t keep) {
+  if (deviceBytes() <= keep)
+    return false;
+  quiesce();
+  for (void *p : ring_)
+    sbc_free_device(p);
+  ring_.clear();
+  slotBytes_ = 0;
+  if (deviceBytes() > keep && staging_) {
+    sbc_free_device(staging_);
+    staging_ = nullptr;
+    stagingBytes_ = 0;
+  }
+  ++trims;
+  return true;
+}
 
 } // namespace reloc

@@ -48,6 +48,47 @@ constexpr size_t kMaxChunkBytes = size_t(64) << 20;
 
 } // namespace
 
+namespace {
+
+/// The staging buffer for `bytes` within the context's live scratch budget:
+/// ring scratch is released first when both do not fit.
+std::variant<void *, TransferError> budgetedStaging(CudaBackend &b, size_t bytes) {
+  bytes = bytes ? bytes : 16;
+  if (b.liveLimit && bytes > b.stagingCapacity()) {
+    if (bytes + 16 > b.liveLimit)
+      return terr("insufficient_capacity", "a staging buffer of " + std::to_string(bytes) +
+                                               " bytes exceeds the context's live scratch budget of " +
+                                               std::to_string(b.liveLimit) + " bytes");
+    if (b.deviceBytes() - b.stagingCapacity() + bytes > b.liveLimit)
+      b.trim(b.deviceBytes() - b.ringBytes()); // drop the ring, keep the rest
+  }
+  void *p = b.staging(bytes);
+  if (!p)
+    return terr("backend_failure", b.error());
+  return p;
+}
+
+/// The ring-slot size for chunks of `rowBytes`-byte rows: at most `target`,
+/// within the live budget (a hard limit: insufficient_capacity when not even
+/// one row fits) and, for default chunk sizes, within the retained budget
+/// when that still allows default-sized chunks (a smaller retained budget
+/// keeps the chunk size, and the ring is released when the lease ends).
+std::variant<size_t, TransferError> budgetedChunk(const CudaBackend &b, int slots, size_t target, int64_t rowBytes,
+                                                  bool defaultSize) {
+  const size_t row = static_cast<size_t>(rowBytes);
+  const size_t hard = b.ringSlotBudget(slots, false);
+  if (hard < row)
+    return terr("insufficient_capacity", "the context's live scratch budget of " + std::to_string(b.liveLimit) +
+                                             " bytes holds no ring of " + std::to_string(slots) + " slots of one " +
+                                             std::to_string(row) + "-byte row");
+  const size_t soft = b.ringSlotBudget(slots, true);
+  if (defaultSize && soft >= kDefaultChunkBytes)
+    target = std::min(target, soft);
+  return std::min(target, hard);
+}
+
+} // namespace
+
 const char *familyName(Family f) {
   switch (f) {
   case Family::Contiguous: return "contiguous";
@@ -408,17 +449,26 @@ std::optional<TransferError> runD2H(const Lowered &l, CudaBackend &b, const void
   const bool rows = route != Route::Staged && d2hRows(l);
   const int64_t rowBytes = rows ? l.desc.dst_strides[0] * wd : std::max<int64_t>(dstBytes, 1);
   const int64_t nrows = rows ? l.padded[0] : 1;
-  const size_t target = o.chunkSizeOverride ? o.chunkSizeOverride : kDefaultChunkBytes;
+  const int slots = rows ? std::max(2, o.nBuffers) : 1;
+  size_t target = o.chunkSizeOverride ? o.chunkSizeOverride : kDefaultChunkBytes;
+  if (rows) {
+    auto t = budgetedChunk(b, slots, target, rowBytes, !o.chunkSizeOverride);
+    if (auto *e = std::get_if<TransferError>(&t))
+      return *e;
+    target = std::get<size_t>(t);
+  }
   int64_t rowsPer = rows ? std::max<int64_t>(1, static_cast<int64_t>(target) / rowBytes) : 1;
   if (rowsPer >= 64)
     rowsPer -= rowsPer % 64; // whole kernel tiles per chunk
-  const int slots = rows ? std::max(2, o.nBuffers) : 1;
   void *stage = nullptr;
   if (rows) {
     if (!b.ensureRing(slots, static_cast<size_t>(rowsPer * rowBytes)))
       return terr("backend_failure", b.error());
-  } else if (!(stage = b.staging(static_cast<size_t>(rowBytes)))) {
-    return terr("backend_failure", b.error());
+  } else {
+    auto sg = budgetedStaging(b, static_cast<size_t>(rowBytes));
+    if (auto *e = std::get_if<TransferError>(&sg))
+      return *e;
+    stage = std::get<void *>(sg);
   }
   auto slotOf = [&](int k) { return rows ? b.slot(k) : stage; };
   auto readyOf = [&](int k) { return rows ? b.slotReady(k) : b.stagingReady(); };
@@ -630,9 +680,10 @@ std::optional<TransferError> runH2D(const Lowered &l, CudaBackend &b, const void
 
   if (mode == Mode::Whole) {
     const size_t bytes = static_cast<size_t>(l.srcElements) * ws;
-    void *stage = b.staging(bytes ? bytes : 16);
-    if (!stage)
-      return terr("backend_failure", b.error());
+    auto sg = budgetedStaging(b, bytes);
+    if (auto *e = std::get_if<TransferError>(&sg))
+      return *e;
+    void *stage = std::get<void *>(sg);
     int rc;
     if ((rc = sbc_stream_wait_event(b.copyStream(), b.stagingFree())) || (rc = upload(stage, hsrc, bytes)) ||
         (rc = sbc_event_record(b.stagingReady(), b.copyStream())) ||
@@ -678,18 +729,32 @@ std::optional<TransferError> runH2D(const Lowered &l, CudaBackend &b, const void
   // chunks, 1.318 ms in 32 MiB ones), and the kernels are fast enough that
   // the pipeline's tail (the last chunk's kernel) stays short.
   const size_t validBytes = static_cast<size_t>(std::max<int64_t>(V1 - V0, 0)) * static_cast<size_t>(rowBytes);
-  const size_t target = o.chunkSizeOverride ? o.chunkSizeOverride
-                                            : std::clamp(validBytes / 4, kDefaultChunkBytes, kMaxChunkBytes);
-  int64_t rowsPer = std::max<int64_t>(1, static_cast<int64_t>(target) / rowBytes);
-  // Chunk boundaries on a multiple of 64 rows keep every chunk's destination
-  // box 16-byte aligned and made of whole kernel tiles.
-  if (rowsPer >= 64)
-    rowsPer -= rowsPer % 64;
-  const int slots = std::max(2, o.nBuffers);
-  if (mode == Mode::Whole || route == Route::Staged)
+  size_t target = o.chunkSizeOverride ? o.chunkSizeOverride
+                                      : std::clamp(validBytes / 4, kDefaultChunkBytes, kMaxChunkBytes);
+  // Staged: the valid rows in one piece, in the staging buffer.
+  const bool single = route == Route::Staged;
+  const int slots = single ? 1 : std::max(2, o.nBuffers);
+  void *stage = nullptr;
+  int64_t rowsPer;
+  if (single) {
     rowsPer = std::max<int64_t>(1, V1 - V0);
-  if (!b.ensureRing(slots, static_cast<size_t>(rowsPer * rowBytes)))
-    return terr("backend_failure", b.error());
+    auto sg = budgetedStaging(b, static_cast<size_t>(rowsPer * rowBytes));
+    if (auto *e = std::get_if<TransferError>(&sg))
+      return *e;
+    stage = std::get<void *>(sg);
+  } else {
+    auto t = budgetedChunk(b, slots, target, rowBytes, !o.chunkSizeOverride);
+    if (auto *e = std::get_if<TransferError>(&t))
+      return *e;
+    target = std::get<size_t>(t);
+    rowsPer = std::max<int64_t>(1, static_cast<int64_t>(target) / rowBytes);
+    // Chunk boundaries on a multiple of 64 rows keep every chunk's
+    // destination box 16-byte aligned and made of whole kernel tiles.
+    if (rowsPer >= 64)
+      rowsPer -= rowsPer % 64;
+    if (!b.ensureRing(slots, static_cast<size_t>(rowsPer * rowBytes)))
+      return terr("backend_failure", b.error());
+  }
   st.route = route == Route::Staged ? "staged" : "dma_ring";
   st.buffers = static_cast<size_t>(slots);
   st.chunkBytes = static_cast<size_t>(rowsPer * rowBytes);
@@ -704,9 +769,11 @@ std::optional<TransferError> runH2D(const Lowered &l, CudaBackend &b, const void
   for (int64_t r0 = V0; r0 < V1; r0 += rowsPer, ++i) {
     const int64_t r1 = std::min(r0 + rowsPer, V1);
     const int s = static_cast<int>(i % slots);
-    void *slot = b.slot(s);
+    void *slot = single ? stage : b.slot(s);
+    void *slotFree = single ? b.stagingFree() : b.slotFree(s);
+    void *slotReady = single ? b.stagingReady() : b.slotReady(s);
     int rc;
-    if ((rc = sbc_stream_wait_event(b.copyStream(), b.slotFree(s)))) {
+    if ((rc = sbc_stream_wait_event(b.copyStream(), slotFree))) {
       b.fail("ring wait", rc);
       return terr("backend_failure", b.error());
     }
@@ -720,8 +787,8 @@ std::optional<TransferError> runH2D(const Lowered &l, CudaBackend &b, const void
       rc = sbc_memcpy_h2d_2d_async(slot, static_cast<size_t>(rowBytes), src, static_cast<size_t>(S1 * ws),
                                    static_cast<size_t>((c1 - c0) * ws), static_cast<size_t>(v1 - v0), b.copyStream());
     }
-    if (rc || (rc = sbc_event_record(b.slotReady(s), b.copyStream())) ||
-        (rc = sbc_stream_wait_event(b.computeStream(), b.slotReady(s)))) {
+    if (rc || (rc = sbc_event_record(slotReady, b.copyStream())) ||
+        (rc = sbc_stream_wait_event(b.computeStream(), slotReady))) {
       b.fail("ring upload", rc);
       return terr("backend_failure", b.error());
     }
@@ -742,7 +809,7 @@ std::optional<TransferError> runH2D(const Lowered &l, CudaBackend &b, const void
     }
     if (auto e = launch(l, b, d, st))
       return e;
-    if ((rc = sbc_event_record(b.slotFree(s), b.computeStream()))) {
+    if ((rc = sbc_event_record(slotFree, b.computeStream()))) {
       b.fail("ring release", rc);
       return terr("backend_failure", b.error());
     }

@@ -3,6 +3,8 @@
 
 #include "sb_cuda.h"
 
+#include <algorithm>
+
 namespace reloc {
 namespace dispatch {
 namespace {
@@ -14,7 +16,8 @@ Resources::Resources(size_t maxRetainedBytes, size_t maxLiveBytes, unsigned maxC
 
 Resources::~Resources() { close(); }
 
-std::optional<TransferError> Resources::acquire(int device, Slot *&slot) {
+std::optional<TransferError> Resources::acquire(int device, std::shared_ptr<Slot> &slot) {
+  std::shared_ptr<Slot> retired; // destroyed (drained, freed) outside the lock
   std::lock_guard<std::mutex> g(mutex_);
   if (closed_)
     return terr("resources_closed", "typed resources are closed");
@@ -24,27 +27,43 @@ std::optional<TransferError> Resources::acquire(int device, Slot *&slot) {
   auto it = slots_.find(device);
   if (it != slots_.end()) {
     ++hits_;
-    slot = it->second.get();
+    it->second->lastUse = ++clock_;
+    slot = it->second;
     return std::nullopt;
   }
-  if (slots_.size() >= maxContexts_)
-    return terr("invalid_options", "context limit reached (" + std::to_string(maxContexts_) + ")");
+  if (slots_.size() >= maxContexts_) {
+    auto victim = slots_.begin();
+    for (auto v = slots_.begin(); v != slots_.end(); ++v)
+      if (v->second->lastUse < victim->second->lastUse)
+        victim = v;
+    retired = std::move(victim->second); // a lease in progress keeps it alive until it ends
+    slots_.erase(victim);
+    ++evictions_;
+  }
   std::string err;
   auto b = CudaBackend::create(device, err);
   if (!b)
     return terr("backend_failure", err);
-  auto s = std::make_unique<Slot>();
+  // The owner's scratch limits divided into fixed per-context quotas (the
+  // first contexts take the remainder).
+  const size_t k = slots_.size();
+  auto quota = [&](size_t limit) { return limit / maxContexts_ + (k < limit % maxContexts_ ? 1 : 0); };
+  b->retainedLimit = quota(maxRetained_);
+  b->liveLimit = maxLive_ ? std::max<size_t>(quota(maxLive_), 1) : 0;
+  auto s = std::make_shared<Slot>();
   s->backend = std::move(b);
-  slot = s.get();
+  s->lastUse = ++clock_;
+  slot = s;
   slots_[device] = std::move(s);
   ++created_;
   return std::nullopt;
 }
 
 TransferOutcome Resources::withContext(int device,
-                                       const std::function<std::optional<TransferError>(CudaBackend &)> &fn) {
+                                       const std::function<std::optional<TransferError>(CudaBackend &)> &fn,
+                                       bool releaseAfter) {
   TransferOutcome out;
-  Slot *slot = nullptr;
+  std::shared_ptr<Slot> slot;
   if (auto e = acquire(device, slot)) {
     out.error = e;
     return out;
@@ -52,6 +71,10 @@ TransferOutcome Resources::withContext(int device,
   std::lock_guard<std::mutex> lease(slot->lease); // FIFO per context
   out.error = fn(*slot->backend);
   out.completion = TransferCompletion::Complete;
+  // Idle scratch beyond the retained quota is released at the end of a
+  // blocking lease (its work has completed, so nothing waits on it).
+  if (releaseAfter && !slot->backend->failed())
+    slot->backend->trim(slot->backend->retainedLimit);
   if (out.error && slot->backend->failed()) {
     // A failed CUDA call leaves completion unknown: retire the context.
     if (slot->backend->quiesce() != QueueCompletion::Complete) {
@@ -65,7 +88,8 @@ TransferOutcome Resources::withContext(int device,
 
 TransferOutcome Resources::execute(DispatchRequest &request, int device, int /*streams*/,
                                    const TransferOptions &options, std::shared_ptr<void> owners) {
-  TransferOutcome out = withContext(device, [&](CudaBackend &b) { return executeDispatch(request, b, options); });
+  TransferOutcome out = withContext(
+      device, [&](CudaBackend &b) { return executeDispatch(request, b, options); }, !options.asyncCompletion);
   if (out.completion == TransferCompletion::Unknown) {
     std::lock_guard<std::mutex> g(mutex_);
     quarantinedOwners_.push_back(std::move(owners)); // keep buffers alive for good
@@ -184,8 +208,9 @@ TransferOutcome Resources::execute(GroupRequest &group, const TransferOptions &o
     out.error = terr("already_executed", "dispatch groups are single-use");
     return out;
   }
-  TransferOutcome out =
-      withContext(group.device, [&](CudaBackend &b) { return executeGroup(group, b, options, nullptr); });
+  TransferOutcome out = withContext(
+      group.device, [&](CudaBackend &b) { return executeGroup(group, b, options, nullptr); },
+      !options.asyncCompletion);
   if (out.completion == TransferCompletion::Unknown) {
     std::lock_guard<std::mutex> g(mutex_);
     quarantinedOwners_.push_back(std::move(owners));
@@ -213,7 +238,7 @@ Resources::submit(GroupRequest &group, const TransferOptions &options, std::shar
     }
     state->waitsBefore = sbc_wait_launch_count();
     return executeGroup(group, b, o, state->event);
-  });
+  }, false);
   if (out.error) {
     if (out.completion == TransferCompletion::Unknown) {
       std::lock_guard<std::mutex> g(mutex_);
@@ -240,12 +265,15 @@ ResourceStats Resources::stats() const {
   for (const auto &kv : slots_) {
     const CudaBackend &b = *kv.second->backend;
     s.deviceBytes += b.deviceBytes();
+    s.peakLiveBytes += b.peakDeviceBytes;
+    s.releases += b.trims;
     s.copyCalls += b.copyCalls;
     s.eventRecords += b.eventRecords;
     s.eventWaits += b.eventWaits;
     s.callerWaits += b.callerWaits;
     s.kernelLaunches += b.kernelLaunches;
   }
+  s.evictions = evictions_;
   s.retainedBytes = s.deviceBytes;
   return s;
 }

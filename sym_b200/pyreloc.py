@@ -520,8 +520,8 @@ class DispatchResources:
     """Typed contexts: per-device streams, HBM ring and parameter buffers,
     retained across calls (reference ``pyreloc.DispatchResources``)."""
 
-    def __init__(self, *, max_retained_bytes=256 << 20, max_live_bytes=0, max_background_workers=64,
-                 max_streams=8, max_contexts=8, max_contexts_per_device=1, acquire_timeout_ms=None):
+    def __init__(self, *, max_retained_bytes=64 << 20, max_live_bytes=0, max_background_workers=64,
+                 max_streams=8, max_contexts=1, max_contexts_per_device=1, acquire_timeout_ms=None):
         out = ctypes.c_void_p()
         err = SbError()
         _native.lib().sb_resources_create(int(max_retained_bytes), int(max_live_bytes or 0), int(max_contexts),

@@ -15,7 +15,7 @@ class TransferResources:
     def __init__(self, *, max_retained_bytes=256 << 20, max_contexts=4, max_contexts_per_device=2,
                  max_background_workers=64, max_live_staging_bytes=None, acquire_timeout_ms=None,
                  max_typed_retained_bytes=64 << 20, max_typed_live_bytes=0, max_typed_streams=8,
-                 max_typed_background_workers=64, max_typed_contexts=8, max_typed_contexts_per_device=1,
+                 max_typed_background_workers=64, max_typed_contexts=1, max_typed_contexts_per_device=1,
                  typed_acquire_timeout_ms=None):
         from .. import pyreloc
 

@@ -91,3 +91,49 @@ def test_every_16_bit_pattern_widens_like_the_reference(family, op):
     got, rep = run_typed_gpu(blob, {}, {}, patterns)
     assert got.tobytes() == expected(blob, {}, {}, patterns).tobytes()
     assert rep["device_kernel"] == family
+
+
+def _quantize_2d(rows, cols):
+    """f32 [rows, cols] -> transpose -> s8 with scale 0.05 (the SIMT tile family)."""
+    from sym_b200.reloc_torch import recipe as R
+    from sym_b200.reloc_torch import symbolic as S
+
+    shape = (S.Const(rows), S.Const(cols))
+    out = (S.Const(cols), S.Const(rows))
+    q = R.Quantize("int8", R.InlineParam("float32", (), (0x3D4CCCCD,)), None, None, "symmetric_rne")
+    return R.Recipe(R.TensorSpec(shape, S.dense_strides(shape), S.Const(0), "float32"), (R.Transpose((1, 0)), q),
+                    R.TensorSpec(out, S.dense_strides(out), S.Const(0), "int8"), "h2d")
+
+
+@pytest.mark.parametrize("family", ["contiguous", "tile", "narrow", "runs", "generic"])
+def test_quantize_bits_in_every_family(family):
+    """Symmetric RNE quantize (scale 0.05: multiply by the host-formed
+    reciprocal 20.0f, clamp, round half to even; NaN -> -128) of random 32-bit
+    patterns and the boundaries (ties at +-2.5 / 20, the clamp limits,
+    infinities, NaNs) in each family."""
+    from helpers import recipe_c3
+
+    if family == "contiguous":
+        recipe, shape, symbols = recipe_c3("quantize"), (2, 129, 4096), {"B": 2, "S": 129}
+    elif family == "tile":
+        recipe, shape, symbols = _quantize_2d(512, 768), (512, 768), {}
+    elif family == "narrow":
+        recipe, shape, symbols = _channels_last(4, 3, 4096, 1, "quantize"), (4, 3, 4096, 1), {}
+    elif family == "runs":
+        recipe, shape, symbols = _runs_recipe((16, 32, 512), (1, 0, 2), "quantize"), (16, 32, 512), {}
+    else:
+        recipe, shape, symbols = _runs_recipe((8, 32, 30), (1, 0, 2), "quantize"), (8, 32, 30), {}
+    blob = encode(recipe)
+    n = int(np.prod(shape))
+    x = _f32_bits(n, seed=22)
+    edges = (np.array([-2.5, -1.5, -0.5, 0.5, 1.5, 2.5, -6.4, 6.4, 6.35, 6.45, -6.45, 6.425, -6.425],
+                      np.float32) / np.float32(20.0))
+    edges = np.concatenate([edges, np.array([127.0, 128.0, -128.0, -129.0, 6.4, -6.4], np.float32),
+                            np.array([0x7FC00000, 0xFFC00001, 0x7F800000, 0xFF800000], np.uint32).view(np.float32)])
+    x[100:100 + edges.size] = edges
+    x[1000:1000 + edges.size] = edges[::-1]
+    # half of the elements in a human range, where rounding decides the result
+    rng = np.random.default_rng(23)
+    x[n // 2:] = (rng.standard_normal(n - n // 2) * 3.0).astype(np.float32)
+    out, rep = run_typed_gpu(blob, symbols, {}, x)
+    assert out.tobytes() == expected(blob, symbols, {}, x).tobytes()
