@@ -80,8 +80,12 @@ class _Region:
         if _needs_autograd((src, *params)):
             return False
         for name, p in zip(self.candidate.parameters, params):
-            if not isinstance(p, torch.Tensor) or p.device.type != "cpu" or p.dtype != torch.float32 \
-                    or not p.is_contiguous():
+            if not isinstance(p, torch.Tensor) or p.device.type != "cpu" or not p.is_contiguous():
+                return False
+            # f32 scales; integer zero points (the snapshot narrows them to int32, range-checked)
+            want = (torch.float32,) if declared[name][0] == "float32" else (torch.int32, torch.int64, torch.int16,
+                                                                            torch.int8)
+            if p.dtype not in want:
                 return False
             count = 1
             for e in declared[name][1]:

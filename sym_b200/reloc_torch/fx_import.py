@@ -88,14 +88,49 @@ def _is_dense(shape, strides):
     return all(e == 1 or s == d for e, s, d in zip(shape, strides, _dense(shape)))
 
 
-def _kind(node):
-    """The op family of an FX node, or None."""
+_FUNCTION_KINDS = None
+
+
+def _function_kinds():
+    """call_function targets -> op family: Torch functions (Dynamo graphs),
+    their ATen overloads (AOT / export graphs) and the decomposed
+    dequantize ops of ``torch.ops.quantized_decomposed`` when that library
+    is registered (reference reloc_torch/compat.py:538-586)."""
+    global _FUNCTION_KINDS
+    if _FUNCTION_KINDS is not None:
+        return _FUNCTION_KINDS
     import torch
     import torch.nn.functional as F
 
+    aten = torch.ops.aten
+    kinds = {torch.permute: "permute", torch.transpose: "transpose", torch.t: "t", torch.reshape: "view",
+             torch.flatten: "flatten", torch.squeeze: "squeeze", torch.unsqueeze: "unsqueeze", torch.clone: "clone",
+             F.pad: "pad", torch._C._nn.pad: "pad", operator.mul: "mul", torch.mul: "mul",
+             aten.permute.default: "permute", aten.transpose.int: "transpose", aten.t.default: "t",
+             aten.view.default: "view", aten.reshape.default: "view", aten._unsafe_view.default: "view",
+             aten.squeeze.default: "squeeze", aten.squeeze.dim: "squeeze", aten.squeeze.dims: "squeeze",
+             aten.unsqueeze.default: "unsqueeze", aten.flatten.using_ints: "flatten", aten.clone.default: "clone",
+             aten.constant_pad_nd.default: "constant_pad", aten._to_copy.default: "to", aten.to.dtype: "to",
+             aten.to.device: "to"}
+    try:
+        qd = torch.ops.quantized_decomposed
+        for op, kind in ((qd.dequantize_per_tensor, "dequantize_tensor"),
+                         (qd.dequantize_per_channel, "dequantize_channel")):
+            kinds[op] = kind
+            for name in op.overloads():
+                kinds[getattr(op, name)] = kind
+    except (AttributeError, RuntimeError):
+        pass  # the library is not registered: no graph can hold its ops
+    _FUNCTION_KINDS = kinds
+    return kinds
+
+
+def _kind(node):
+    """The op family of an FX node, or None."""
     if node.op == "call_method":
         t = node.target
-        if t in ("permute", "transpose", "t", "reshape", "view", "flatten", "squeeze", "unsqueeze", "contiguous"):
+        if t in ("permute", "transpose", "t", "reshape", "view", "flatten", "squeeze", "unsqueeze", "contiguous",
+                 "clone"):
             return "view" if t == "reshape" else t
         if t in ("to", "cuda"):
             return "to"
@@ -105,11 +140,13 @@ def _kind(node):
             return "mul"
         return None
     if node.op == "call_function":
-        t = node.target
-        table = {torch.permute: "permute", torch.transpose: "transpose", torch.t: "t", torch.reshape: "view",
-                 torch.flatten: "flatten", torch.squeeze: "squeeze", torch.unsqueeze: "unsqueeze",
-                 F.pad: "pad", torch._C._nn.pad: "pad", operator.mul: "mul", torch.mul: "mul"}
-        return table.get(t)
+        kinds = _function_kinds()
+        kind = kinds.get(node.target)
+        if kind is None and "quantized_decomposed" in str(node.target):
+            global _FUNCTION_KINDS
+            _FUNCTION_KINDS = None  # the library was registered after the first lookup
+            kind = _function_kinds().get(node.target)
+        return kind
     return None
 
 
@@ -304,6 +341,64 @@ class _Walk:
         _require(name not in self.parameters, "unsupported_parameter")
         self.parameters.append(name)
 
+    def _tensor_parameter(self, operand, dtypes, numel):
+        """The name of a runtime parameter tensor (an input of the graph)."""
+        _require(hasattr(operand, "op"), "unsupported_parameter")
+        name, _ = _parameter_source(operand, self.inputs)
+        _require(name is not None and operand.op in ("placeholder", "get_attr"), "unsupported_parameter")
+        tensor = self.inputs[name]
+        _require(str(tensor.dtype) in dtypes and tensor.device.type == "cpu", "parameter_dtype_unsupported")
+        _require(tensor.numel() == numel and tensor.dim() <= 1, "unsupported_parameter")
+        _require(name not in self.parameters, "unsupported_parameter")
+        self.parameters.append(name)
+        return name
+
+    def dequantize(self, node, per_channel):
+        """``quantized_decomposed.dequantize_per_tensor`` /
+        ``dequantize_per_channel`` of an int8 tensor: ``(q - zp) * scale`` in
+        f32 (the decomposition computes exactly this: an exact integer
+        difference, then one multiply by the f32 scale), then the optional
+        ``out_dtype`` narrowing."""
+        import torch
+
+        args = list(node.args) + [None] * 7
+        _require(self.dtype == "int8" and args[6 if per_channel else 5] == torch.int8,
+                 "typed_transform_unavailable")
+        ints = ("torch.int32", "torch.int64", "torch.int16", "torch.int8")
+        if per_channel:
+            axis = args[3]
+            _require(type(axis) is int, "unsupported_parameter")
+            rank = len(self.shape)
+            _require(-rank <= axis < rank, "unsupported_parameter")
+            axis %= rank
+            extent = self.shape[axis]
+            scale = BindingParam(self._tensor_parameter(args[1], ("torch.float32",), extent), "float32",
+                                 (self.sym[axis],))
+            zp = None
+            if args[2] is not None:
+                zp = BindingParam(self._tensor_parameter(args[2], ints, extent), "int32", (self.sym[axis],))
+        else:
+            axis = None
+            value = args[1]
+            if isinstance(value, (int, float)) and not isinstance(value, bool):
+                bits = struct.unpack("<I", struct.pack("<f", float(value)))[0]
+                scale = InlineParam("float32", (), (bits,))
+            else:
+                scale = BindingParam(self._tensor_parameter(value, ("torch.float32",), 1), "float32", ())
+            value = args[2]
+            if type(value) is int:
+                _require(-(1 << 31) <= value < (1 << 31), "unsupported_parameter")
+                zp = InlineParam("int32", (), (value & 0xFFFFFFFF,)) if value else None
+            else:
+                zp = BindingParam(self._tensor_parameter(value, ints, 1), "int32", ())
+        self.ops.append(Dequantize("float32", scale, zp, axis, "affine"))
+        self.dtype = "float32"
+        out_dtype = node.kwargs.get("out_dtype")
+        if out_dtype is not None:
+            name = _dtype_name(out_dtype)
+            _require(name in ("float32", "float16", "bfloat16"), "typed_transform_unavailable")
+            self.cast(name)
+
     def move(self, device):
         _require(device.type == "cuda" and self.device == "cpu", "unsupported_device")
         self.device = "cuda"
@@ -423,6 +518,20 @@ def _step(walk, node):
         fmt = node.kwargs.get("memory_format", torch.contiguous_format)
         _require(fmt == torch.contiguous_format, "unsupported_memory_format")
         walk.strides = _dense(walk.shape)
+    elif k == "clone":
+        # preserve_format keeps a dense permuted layout's strides; the
+        # destination check at the end of the chain still requires a dense result
+        fmt = node.kwargs.get("memory_format", torch.preserve_format)
+        _require(fmt in (torch.preserve_format, torch.contiguous_format), "unsupported_memory_format")
+        if fmt == torch.contiguous_format:
+            walk.strides = _dense(walk.shape)
+    elif k == "constant_pad":
+        widths = node.args[1] if len(node.args) > 1 else node.kwargs.get("pad")
+        value = node.args[2] if len(node.args) > 2 else node.kwargs.get("value", 0)
+        _require(isinstance(widths, (tuple, list)), "unsupported_padding")
+        walk.pad(tuple(widths), 0 if value is None else value)
+    elif k in ("dequantize_tensor", "dequantize_channel"):
+        walk.dequantize(node, per_channel=k == "dequantize_channel")
     elif k == "pad":
         widths = node.args[1] if len(node.args) > 1 else node.kwargs.get("pad")
         mode = node.args[2] if len(node.args) > 2 else node.kwargs.get("mode", "constant")

@@ -217,3 +217,68 @@ def test_dynamic_region_checks_each_call():
     (region,) = RelocBackend()(gm, ex).regions
     assert region._eligible(torch.zeros(24, 24), ())
     assert not region._eligible(torch.zeros(24, 8), ())  # one symbol, two sizes
+
+
+def test_decomposed_dequantize_ops_become_typed_recipes():
+    """``quantized_decomposed.dequantize_per_channel`` / ``_per_tensor`` (the
+    reference importer's audited dequantize operators): tensor scales and
+    zero points become runtime parameters, Python scalars exact inline bits,
+    ``out_dtype`` a narrowing cast."""
+    import torch
+    import torch.ao.quantization.fx._decomposed  # noqa: F401  (registers the ops)
+    from sym_b200.reloc_torch.fx_import import import_graph
+    from sym_b200.reloc_torch.recipe import BindingParam, InlineParam
+
+    qd = torch.ops.quantized_decomposed
+
+    def per_channel(q, s, z):
+        return qd.dequantize_per_channel(q, s, z, 0, -128, 127, torch.int8).half().t().contiguous().cuda()
+
+    ((gm, ex),) = _dynamo_graphs(per_channel, torch.zeros(16, 32, dtype=torch.int8), torch.ones(16),
+                                 torch.zeros(16, dtype=torch.int64))
+    (c,) = import_graph(gm, ex).candidates
+    dq = c.recipe.operations[0]
+    assert _ops(c) == ["Dequantize", "Cast", "Transpose"] and dq.axis == 0 and len(c.parameters) == 2
+    assert isinstance(dq.scale, BindingParam) and dq.zero_point.dtype == "int32"
+
+    ((gm, ex),) = _dynamo_graphs(lambda q: qd.dequantize_per_tensor(q, 0.05, -3, -128, 127, torch.int8).cuda(),
+                                 torch.zeros(8, 4, dtype=torch.int8))
+    (c,) = import_graph(gm, ex).candidates
+    dq = c.recipe.operations[0]
+    assert dq.scale == InlineParam("float32", (), (0x3D4CCCCD,))
+    assert dq.zero_point == InlineParam("int32", (), (0xFFFFFFFD,)) and not c.parameters
+
+    ((gm, ex),) = _dynamo_graphs(
+        lambda q, s: qd.dequantize_per_channel(q, s, None, 1, -128, 127, torch.int8, out_dtype=torch.bfloat16).cuda(),
+        torch.zeros(8, 4, dtype=torch.int8), torch.ones(4))
+    (c,) = import_graph(gm, ex).candidates
+    assert _ops(c) == ["Dequantize", "Cast"] and c.recipe.operations[0].zero_point is None
+    assert c.recipe.destination.dtype == "bfloat16"
+
+
+def test_aten_level_graphs_are_imported():
+    """Graphs of ATen overloads (AOT / export level) map to the same recipes."""
+    import torch
+    import torch.fx as fx
+    from sym_b200.reloc_torch.fx_import import import_graph
+
+    aten = torch.ops.aten
+    g = fx.Graph()
+    x = g.placeholder("x")
+    p = g.call_function(aten.permute.default, (x, [1, 0]))
+    c = g.call_function(aten.clone.default, (p,), {"memory_format": torch.contiguous_format})
+    pad = g.call_function(aten.constant_pad_nd.default, (c, [0, 2], 0.0))
+    out = g.call_function(aten._to_copy.default, (pad,), {"dtype": torch.float16, "device": torch.device("cuda")})
+    g.output(out)
+    (cand,) = import_graph(fx.GraphModule(torch.nn.Module(), g), (torch.zeros(8, 4),)).candidates
+    assert _ops(cand) == ["Transpose", "Pad", "Cast"]
+    assert [e.value for e in cand.recipe.destination.shape] == [4, 10]
+
+    # a preserved-format clone of a transposed view is not dense: rejected
+    g = fx.Graph()
+    x = g.placeholder("x")
+    t = g.call_function(aten.t.default, (x,))
+    c = g.call_function(aten.clone.default, (t,))
+    g.output(g.call_function(aten._to_copy.default, (c,), {"device": torch.device("cuda")}))
+    r = import_graph(fx.GraphModule(torch.nn.Module(), g), (torch.zeros(8, 4),))
+    assert not r.candidates and [e.reason for e in r.exclusions] == ["destination_layout"]

@@ -141,3 +141,37 @@ def test_dynamic_layout_and_pad_regions(fn_name):
         x = torch.rand(shape)
         assert _bits_equal(fn(x), f(x))
     assert backend.stats()["executions"] >= 2
+
+
+@pytest.mark.parametrize("case", ["per_channel_zp_f16_t", "per_tensor_inline", "per_channel_bf16_out",
+                                  "per_tensor_tensor_params"])
+def test_decomposed_dequantize_regions_match_eager(case):
+    """Weight-dequant graphs written with ``quantized_decomposed`` ops run as
+    one fused transfer each, bit for bit the eager result."""
+    import torch
+    import torch.ao.quantization.fx._decomposed  # noqa: F401
+    from sym_b200 import pyreloc
+
+    qd = torch.ops.quantized_decomposed
+    g = torch.Generator().manual_seed(7)
+    q = torch.randint(-128, 128, (512, 768), dtype=torch.int8, generator=g)
+    s0 = torch.exp(torch.randn(512, generator=g) * 0.5 - 5)
+    s1 = torch.exp(torch.randn(768, generator=g) * 0.5 - 5)
+    z0 = torch.randint(-20, 20, (512,), dtype=torch.int64, generator=g)
+    fns = {
+        "per_channel_zp_f16_t": (lambda q, s, z: qd.dequantize_per_channel(q, s, z, 0, -128, 127, torch.int8)
+                                 .half().t().contiguous().cuda(), (q, s0, z0)),
+        "per_tensor_inline": (lambda q: qd.dequantize_per_tensor(q, 0.0123, -7, -128, 127, torch.int8).cuda(), (q,)),
+        "per_channel_bf16_out": (lambda q, s: qd.dequantize_per_channel(q, s, None, 1, -128, 127, torch.int8,
+                                                                        out_dtype=torch.bfloat16).cuda(), (q, s1)),
+        "per_tensor_tensor_params": (lambda q, s, z: qd.dequantize_per_tensor.tensor(q, s, z, -128, 127,
+                                                                                     torch.int8).cuda(),
+                                     (q, torch.tensor(0.031), torch.tensor(5))),
+    }
+    f, args = fns[case]
+    fn, backend = _compile(f)
+    l0 = pyreloc.kernel_launches()
+    got = fn(*args)
+    torch.cuda.synchronize()
+    assert pyreloc.kernel_launches() > l0 and backend.stats()["executions"] >= 1, backend.stats()
+    assert _bits_equal(got, f(*args))
