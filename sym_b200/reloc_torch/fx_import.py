@@ -28,7 +28,7 @@ import struct
 from dataclasses import dataclass
 
 from .recipe import BindingParam, Cast, Dequantize, Fill, InlineParam, Pad, Recipe, Reshape, TensorSpec, Transpose
-from .symbolic import Const, Symbol, add, dense_strides, product
+from .symbolic import Const, Symbol, add, dense_strides, product, product_key
 
 
 @dataclass(frozen=True)
@@ -209,6 +209,7 @@ class _Walk:
         self.ops = []
         self.parameters = []  # parameter node names in declaration order
         self.inputs = inputs  # node name -> example tensor
+        self.scalars = {}  # SymInt placeholder name -> (example value, Symbol)
 
     # layout -------------------------------------------------------------
     def permute(self, perm):
@@ -472,6 +473,54 @@ def _operand(node):
     return _tensor_arg(node)
 
 
+def _quotient(total, known):
+    """``product(total) / product(known)`` as a product expression when the
+    known factors cancel exactly (symbols and the constant), else None."""
+    t, k = product_key(total), product_key(known)
+    if t is None or k is None or k[0] == 0 or t[0] % k[0]:
+        return None
+    atoms = list(t[1])
+    for a in k[1]:
+        if a not in atoms:
+            return None
+        atoms.remove(a)
+    return product([Const(t[0] // k[0]), *atoms])
+
+
+def _view(walk, node):
+    """view / reshape: integer targets, -1, and (dynamic graphs) SymInt
+    placeholders as target extents. With dynamic dims the target's extents
+    must multiply to the source's symbolically; a -1 is the exact quotient
+    of the two products (else the chain keeps the example's sizes)."""
+    rest = list(node.args[1:])
+    if len(rest) == 1 and isinstance(rest[0], (tuple, list)):
+        rest = list(rest[0])
+    for key in ("shape", "size"):
+        if key in node.kwargs:
+            rest = list(node.kwargs[key])
+    concrete, sym = [], []
+    for v in rest:
+        if type(v) is int:
+            concrete.append(v)
+            sym.append(Const(v) if v >= 0 else None)
+        elif hasattr(v, "op") and v.name in walk.scalars:
+            concrete.append(walk.scalars[v.name][0])
+            sym.append(walk.scalars[v.name][1])
+        else:
+            raise _Reject("unsupported_symbolic_expr")
+    if not walk.symbolic and all(isinstance(e, Const) or e is None for e in sym):
+        walk.reshape(concrete)
+        return
+    _require(concrete.count(-1) <= 1, "unsupported_reshape")
+    if -1 in concrete:
+        i = concrete.index(-1)
+        q = _quotient(walk.sym, [e for e in sym if e is not None])
+        _require(q is not None, "symbolic_reshape")
+        sym[i] = q
+    _require(product_key(sym) == product_key(walk.sym), "symbolic_reshape")
+    walk.reshape(concrete, sym_target=tuple(sym))
+
+
 def _step(walk, node):
     """Apply one member node to the walk state."""
     import torch
@@ -491,7 +540,7 @@ def _step(walk, node):
         _require(len(walk.shape) <= 2, "unsupported_permutation")
         walk.permute((1, 0) if len(walk.shape) == 2 else (0,))
     elif k == "view":
-        walk.reshape(_varargs(node, "unsupported_symbolic_expr"))
+        _view(walk, node)
     elif k == "flatten":
         rank = len(walk.shape)
         start = node.args[1] if len(node.args) > 1 else node.kwargs.get("start_dim", 0)
@@ -600,6 +649,9 @@ def _symbolic_shape(root, example):
     for d, e in zip(meta.shape, example.shape):
         if isinstance(d, torch.SymInt):
             name = str(d.node.expr)
+            if name.isdigit():  # a dim the capture specialized
+                out.append(Const(int(name)))
+                continue
             if not name.isidentifier() or int(e) < 2:
                 return None
             out.append(Symbol(name))
@@ -609,8 +661,10 @@ def _symbolic_shape(root, example):
     return out if dynamic else None
 
 
-def _walk(members, src, dtype, inputs, sym):
+def _walk(members, src, dtype, inputs, sym, scalars=None):
     walk = _Walk(src.shape, dtype, inputs, sym)
+    # SymInt view targets: symbols in a symbolic walk, the example's sizes in a static one
+    walk.scalars = {k: (v, e if sym is not None else Const(v)) for k, (v, e) in (scalars or {}).items()}
     moves = 0
     for m in members:
         before = walk.device
@@ -626,13 +680,19 @@ def import_graph(gm, example_inputs=None):
     import torch
 
     nodes = list(gm.graph.nodes)
-    inputs = {}
+    inputs, scalars = {}, {}
     examples = iter(example_inputs or ())
     for n in nodes:
         if n.op == "placeholder":
             value = next(examples, None)
             if isinstance(value, torch.Tensor):
                 inputs[n.name] = value
+            meta = n.meta.get("example_value")
+            if isinstance(meta, torch.SymInt):
+                hint = value.node.hint if isinstance(value, torch.SymInt) else value
+                name = str(meta.node.expr)
+                if type(hint) is int and name.isidentifier():
+                    scalars[n.name] = (hint, Symbol(name))
         elif n.op == "get_attr":
             try:
                 value = operator.attrgetter(n.target)(gm)
@@ -669,7 +729,7 @@ def import_graph(gm, example_inputs=None):
             _require(dtype is not None, "unsupported_dtype")
             sym = _symbolic_shape(root, src)
             try:
-                walk = _walk(members, src, dtype, inputs, sym)
+                walk = _walk(members, src, dtype, inputs, sym, scalars)
             except _Reject as error:
                 if sym is None or not error.reason.startswith("symbolic_"):
                     raise

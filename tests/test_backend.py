@@ -282,3 +282,29 @@ def test_aten_level_graphs_are_imported():
     g.output(g.call_function(aten._to_copy.default, (c,), {"device": torch.device("cuda")}))
     r = import_graph(fx.GraphModule(torch.nn.Module(), g), (torch.zeros(8, 4),))
     assert not r.candidates and [e.reason for e in r.exclusions] == ["destination_layout"]
+
+
+def test_dynamic_view_targets_follow_the_symbols():
+    """``x.view(x.shape[0], x.shape[1], 16, 64)`` and ``x.view(-1)`` in a
+    dynamic capture: SymInt targets and exact -1 quotients keep the plan
+    symbolic; ``reshape(-1, 64)`` (a quotient that is not exact) keeps the
+    example's sizes."""
+    import torch
+    from sym_b200.reloc_torch.fx_import import import_graph
+    from sym_b200.reloc_torch.symbolic import Const, Mul, Symbol
+
+    ((gm, ex),) = _dynamo_graphs(lambda x: x.view(x.shape[0], x.shape[1], 16, 64).transpose(1, 2).contiguous().cuda(),
+                                 torch.zeros(4, 8, 1024))
+    (c,) = import_graph(gm, ex).candidates
+    b, s, h = c.recipe.source.shape
+    assert isinstance(b, Symbol) and isinstance(s, Symbol) and h == Const(1024)
+    assert c.recipe.destination.shape == (b, Const(16), s, Const(64))
+
+    ((gm, ex),) = _dynamo_graphs(lambda x: x.view(-1).cuda(), torch.zeros(4, 8))
+    (c,) = import_graph(gm, ex).candidates
+    a, b = c.recipe.source.shape
+    assert c.recipe.destination.shape in ((Mul(a, b),), (Mul(b, a),))
+
+    ((gm, ex),) = _dynamo_graphs(lambda x: x.reshape(-1, 64).t().contiguous().cuda(), torch.zeros(4, 8, 1024))
+    (c,) = import_graph(gm, ex).candidates
+    assert all(isinstance(e, Const) for e in c.recipe.source.shape)

@@ -175,3 +175,24 @@ def test_decomposed_dequantize_regions_match_eager(case):
     torch.cuda.synchronize()
     assert pyreloc.kernel_launches() > l0 and backend.stats()["executions"] >= 1, backend.stats()
     assert _bits_equal(got, f(*args))
+
+
+@pytest.mark.parametrize("fn_name", ["heads", "flatten_rest"])
+def test_dynamic_view_targets_run_for_every_size(fn_name):
+    """Symbolic view targets (SymInt extents, exact -1 quotients) keep one
+    plan for every size."""
+    import torch
+
+    fns = {
+        "heads": (lambda x: x.view(x.shape[0], x.shape[1], 16, 64).transpose(1, 2).contiguous().half().cuda(),
+                  [(2, 8, 1024), (3, 40, 1024), (5, 7, 1024)]),
+        "flatten_rest": (lambda x: x.view(x.shape[0], -1).t().contiguous().cuda(),
+                         [(4, 8, 6), (9, 5, 7), (16, 32, 3)]),
+    }
+    f, shapes = fns[fn_name]
+    fn, backend = _compile(f, dynamic=True)
+    for shape in shapes:
+        x = torch.randn(shape)
+        assert _bits_equal(fn(x), f(x))
+    st = backend.stats()
+    assert st["executions"] >= 2 and st.get("fallbacks", 0) == 0, st
