@@ -94,10 +94,13 @@ class _Region:
                 return False
         return True
 
-    def __call__(self, src, *params):
+    def __call__(self, src, *inputs):
+        # inputs: the runtime parameters, then the scalar graph inputs the
+        # original nodes read (SymInt sizes; the plan binds them from src)
+        params = inputs[:len(self.candidate.parameters)]
         if not self._eligible(src, params):
             self.backend._count("fallbacks")
-            return self.original(src, *params)
+            return self.original(src, *inputs)
         self.backend._count("executions")
         import torch
 
@@ -215,10 +218,23 @@ class RelocBackend:
             members = [by_name[m] for m in cand.members]
             root = by_name[cand.source]
             params = [by_name[p] for p in cand.parameters]
-            region = _Region(self, cand, compiled, _extract(rewritten, root, members, params))
+            member_set = set(members)
+            extras = []  # scalar graph inputs the members read (SymInt sizes)
+            for m in members:
+                for n in m.all_input_nodes:
+                    if n not in member_set and n is not root and n not in params and n not in extras \
+                            and n.op == "placeholder":
+                        extras.append(n)
+            try:
+                original = _extract(rewritten, root, members, params + extras)
+            except UnsupportedRecipe as error:
+                with self._lock:
+                    self._exclusions.append(Exclusion(cand.tail, error.reason))
+                continue
+            region = _Region(self, cand, compiled, original)
             tail = members[-1]
             with graph.inserting_before(tail):
-                call = graph.call_function(region, (root, *params))
+                call = graph.call_function(region, (root, *params, *extras))
             tail.replace_all_uses_with(call)
             for m in reversed(members):
                 graph.erase_node(m)
@@ -231,8 +247,9 @@ class RelocBackend:
 
 
 def _extract(gm, root, members, params):
-    """The region's original nodes as a standalone callable ``(src, *params)``
-    (node_copy keeps the exact call targets and arguments)."""
+    """The region's original nodes as a standalone callable ``(src, *inputs)``
+    (node_copy keeps the exact call targets and arguments); ``params`` are
+    the other graph inputs the members read, in call order."""
     from torch.fx import Graph, GraphModule
 
     graph = Graph()
