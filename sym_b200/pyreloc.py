@@ -11,6 +11,7 @@ runs in the fused sm_100a kernels; there is no CPU execution entry point.
 from __future__ import annotations
 
 import ctypes
+import threading
 from dataclasses import dataclass, field
 from types import MappingProxyType
 
@@ -314,19 +315,15 @@ class BufferView:
     device: int = -1
 
     def native(self) -> SbView:
-        v = SbView()
-        v.base = int(self.base)
-        v.capacity_bytes = int(self.capacity_bytes)
-        v.offset_bytes = int(self.offset_bytes)
-        v.kind = 1 if self.kind == "cuda" else 0
-        v.device = int(self.device)
-        if len(self.extents) > 8:
+        rank = len(self.extents)
+        if rank > 8:
             raise TransferError("invalid_view", "views have at most 8 dimensions")
-        v.rank = len(self.extents)
-        v.element_size = int(self.element_size)
-        for i, (e, s) in enumerate(zip(self.extents, self.strides)):
-            v.extents[i] = int(e)
-            v.strides[i] = int(s)
+        v = SbView(int(self.base), int(self.capacity_bytes), int(self.offset_bytes), 1 if self.kind == "cuda" else 0,
+                   int(self.device), rank, int(self.element_size))
+        pairs = list(zip(self.extents, self.strides))
+        if pairs:
+            v.extents[:len(pairs)] = [int(e) for e, _ in pairs]
+            v.strides[:len(pairs)] = [int(x) for _, x in pairs]
         return v
 
 
@@ -339,9 +336,9 @@ class DispatchRequest(_Handle):
         super().__init__(ptr)
         self.template = template
         self.consumed = False
-        self.report = MappingProxyType({"implementation": template.selection["implementation"],
-                                        "policy": template.selection["policy"],
-                                        "placement_reason": template.selection["placement_reason"]})
+        sel = template._info["selection"]
+        self.report = MappingProxyType({"implementation": sel["implementation"], "policy": sel["policy"],
+                                        "placement_reason": sel["placement_reason"]})
 
 
 def prepare_dispatch_from_template(prepared: DispatchTemplate, source: BufferView, destination: BufferView):
@@ -374,6 +371,18 @@ def _options(n_buffers=4, route="auto", chunk_size=0, caller_stream=None, async_
     return o
 
 
+_TLS = threading.local()
+
+
+def _call_scratch():
+    """This thread's error record and report buffer for execute calls (the
+    native call fills them; reused so each call does not allocate 8 KiB)."""
+    scratch = getattr(_TLS, "scratch", None)
+    if scratch is None:
+        scratch = _TLS.scratch = (SbError(), ctypes.create_string_buffer(8192))
+    return scratch
+
+
 def execute_dispatch(request: DispatchRequest, *, caller_stream=None, n_buffers=4, n_streams=2, gather_threads=None,
                      gather_pool=None, pinning="pinned", min_pinned_bytes=None, direct_dense_upload=True,
                      pipeline=True, chunk_size=0, resources=None, owners=(), route="auto",
@@ -389,8 +398,7 @@ def execute_dispatch(request: DispatchRequest, *, caller_stream=None, n_buffers=
         raise TransferError("already_executed", "dispatch requests are single-use")
     request.consumed = True
     opts = _options(n_buffers, route, chunk_size, caller_stream, async_completion)
-    err = SbError()
-    buf = ctypes.create_string_buffer(8192)
+    err, buf = _call_scratch()
     native_res = resources.handle if resources is not None else None
     _keep = owners
     rc = _native.lib().sb_execute_dispatch(request.ptr, native_res, ctypes.byref(opts), buf, 8192,

@@ -659,6 +659,20 @@ class CompiledRecipe:
             out[p.name] = (p.dtype, [sx.expression(e).evaluate(bindings) for e in p.extents])
         return out
 
+    def bind_shape(self, shape):
+        """(symbol bindings, declared parameter extents) of a source shape,
+        cached per shape (the per-call hot path of typed transfers)."""
+        cache = self.__dict__.setdefault("_shape_cache", {})
+        hit = cache.get(shape)
+        if hit is None:
+            bindings = self.source_symbols(shape)
+            hit = (bindings, self.parameter_extents(bindings))
+            if len(cache) >= 256:
+                cache.clear()
+            cache[shape] = hit
+        bindings, declared = hit
+        return dict(bindings), {k: (d, list(e)) for k, (d, e) in declared.items()}
+
     def source_symbols(self, shape):
         """Bind symbols from a concrete source shape (each symbol must appear
         as a bare source extent)."""

@@ -34,6 +34,18 @@ def dtype_name(dtype):
     return name
 
 
+def _current_stream(device):
+    """The raw handle of the current CUDA stream of ``device`` (the cheap
+    accessor when this Torch build has it)."""
+    import torch
+
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    raw = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+    if raw is not None:
+        return raw(index)
+    return torch.cuda.current_stream(index).cuda_stream
+
+
 def storage_span(tensor):
     """Allocation base, capacity and the byte offset of element 0."""
     storage = tensor.untyped_storage()
@@ -90,7 +102,6 @@ class PreparedTypedTransfer:
     source_view: object
     parameters: dict
     snapshots: dict
-    capability: dict
     selected: dict
     consumed: bool = False
     direction: str = "h2d"
@@ -100,9 +111,16 @@ class PreparedTypedTransfer:
     def __post_init__(self):
         self._storage = storage_snapshot(self.source)
 
+    @property
+    def capability(self):
+        """The capability table of the selected template (a fresh copy)."""
+        return self.template.capability
+
     def recheck(self):
         if storage_snapshot(self.source) != self._storage:
             raise RuntimeError("stale typed transfer: source storage or metadata changed after preflight")
+        if not self.parameters:
+            return
         declared = self.compiled.parameter_extents(self.bindings)
         for name, value in self.parameters.items():
             if _parameter_snapshot(name, value, declared[name]) != self.snapshots[name]:
@@ -153,8 +171,7 @@ def prepare_typed_transfer(compiled, source, device, *, parameters=None, policy=
                                                 f"{compiled.recipe.source.dtype}")
     if not source.is_contiguous():
         raise UnsupportedRecipe("non_dense_source", "typed transfers take dense row-major sources")
-    bindings = compiled.source_symbols(tuple(source.shape))
-    declared = compiled.parameter_extents(bindings)
+    bindings, declared = compiled.bind_shape(tuple(source.shape))
     parameters = dict(parameters or {})
     missing, extra = sorted(set(declared) - set(parameters)), sorted(set(parameters) - set(declared))
     if missing or extra:
@@ -184,10 +201,9 @@ def prepare_typed_transfer(compiled, source, device, *, parameters=None, policy=
     if direction == "d2h":
         return PreparedTypedTransfer(compiled, source, bindings, bound, template, torch.device("cpu"),
                                      storage_view(source, "cuda", index), parameters, snapshots,
-                                     template.capability, dict(template.selection), direction="d2h")
+                                     template.selection, direction="d2h")
     return PreparedTypedTransfer(compiled, source, bindings, bound, template, torch.device("cuda", index),
-                                 storage_view(source, "host", -1), parameters, snapshots, template.capability,
-                                 dict(template.selection))
+                                 storage_view(source, "host", -1), parameters, snapshots, template.selection)
 
 
 def execute_typed_transfer(request, *, n_buffers=4, n_streams=2, gather_threads=None, gather_pool=None,
@@ -221,7 +237,7 @@ def execute_typed_transfer(request, *, n_buffers=4, n_streams=2, gather_threads=
         except pyreloc.TransferError as error:
             raise RuntimeError(f"typed dispatch rejected at execution: {error}") from error
         request.consumed = True
-        stream = torch.cuda.current_stream(request.source.device if d2h else request.device).cuda_stream
+        stream = _current_stream(request.source.device if d2h else request.device)
         try:
             report = pyreloc.execute_dispatch(
                 native, caller_stream=stream, n_buffers=n_buffers, chunk_size=chunk_size or 0,
