@@ -667,7 +667,7 @@ int sb_resources_stats(const sb_resources *r, char *json, size_t cap) {
      << ",\"closed\":" << (s.closed ? "true" : "false") << ",\"quarantined\":" << (s.quarantined ? "true" : "false")
      << ",\"retained_limit\":" << s.retainedLimit << ",\"live_limit\":" << s.liveLimit
      << ",\"context_limit\":" << s.contextLimit << ",\"peak_live_bytes\":" << s.peakLiveBytes
-     << ",\"releases\":" << s.releases << "}";
+     << ",\"releases\":" << s.releases << ",\"evictions\":" << s.evictions << "}";
   return putJson(os.str(), json, cap);
 }
 

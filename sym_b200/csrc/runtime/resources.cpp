@@ -63,6 +63,19 @@ TransferOutcome Resources::withContext(int device,
                                        const std::function<std::optional<TransferError>(CudaBackend &)> &fn,
                                        bool releaseAfter) {
   TransferOutcome out;
+  // The work runs with the context's device current; the caller's current
+  // device is put back afterwards (callers may target a GPU that is not
+  // their current one).
+  int callerDevice = -1;
+  sbc_get_device(&callerDevice);
+  struct Restore {
+    int device;
+    ~Restore() {
+      int now = -1;
+      if (device >= 0 && sbc_get_device(&now) == 0 && now != device)
+        sbc_set_device(device);
+    }
+  } restore{callerDevice};
   std::shared_ptr<Slot> slot;
   if (auto e = acquire(device, slot)) {
     out.error = e;
