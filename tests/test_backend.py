@@ -308,3 +308,19 @@ def test_dynamic_view_targets_follow_the_symbols():
     ((gm, ex),) = _dynamo_graphs(lambda x: x.reshape(-1, 64).t().contiguous().cuda(), torch.zeros(4, 8, 1024))
     (c,) = import_graph(gm, ex).candidates
     assert all(isinstance(e, Const) for e in c.recipe.source.shape)
+
+
+def test_bind_shape_caches_without_sharing_state():
+    """The per-shape binding cache of a compiled recipe returns the same
+    bindings and parameter extents as binding afresh, as copies."""
+    from sym_b200.workloads import weight_recipe
+    from sym_b200.reloc_torch.compiler import CompilerClient
+
+    compiled = CompilerClient.from_environment().compile(weight_recipe("out_in_f16"))
+    for shape in ((64, 96), (96, 64), (64, 96)):
+        bindings, declared = compiled.bind_shape(shape)
+        assert bindings == compiled.source_symbols(shape)
+        assert declared == compiled.parameter_extents(bindings)
+        bindings["s0"] = -1
+        declared["scale"][1].append(7)
+    assert compiled.bind_shape((64, 96)) == ({"s0": 64, "s1": 96}, {"scale": ("float32", [64])})
