@@ -86,6 +86,11 @@ public:
   TransferOutcome withContext(int device, const std::function<std::optional<TransferError>(CudaBackend &)> &fn,
                               bool releaseAfter = true);
 
+  /// Bound the wait for a context another call holds (reference
+  /// typed_acquire_timeout_ms): after `ms` milliseconds (0: at once) the call
+  /// fails with acquire_timeout; a negative value waits without limit.
+  void setAcquireTimeout(int64_t ms) { acquireTimeoutMs_ = ms; }
+
   ResourceStats stats() const;
   std::optional<TransferError> clear();
   std::optional<TransferError> close();
@@ -93,9 +98,10 @@ public:
 private:
   struct Slot {
     std::unique_ptr<CudaBackend> backend;
-    std::mutex lease;
+    std::timed_mutex lease;
     uint64_t lastUse = 0;
   };
+  int64_t acquireTimeoutMs_ = -1; // < 0: wait for a leased context without limit
   /// The context of `device`; at the context limit the least recently used
   /// context is retired (its scratch is freed once its current lease ends).
   std::optional<TransferError> acquire(int device, std::shared_ptr<Slot> &slot);

@@ -227,6 +227,11 @@ int sb_resources_stats(const sb_resources *resources, char *json, size_t cap);
  * `device`, created on first use; for callers that time or order work on them. */
 int sb_resources_streams(sb_resources *resources, int32_t device, void **copy_stream, void **compute_stream,
                          sb_error *err);
+/* Bound the wait for a context that another call holds (reference
+ * DispatchResources acquireTimeoutMs, DispatchResources.h:70): after `ms`
+ * milliseconds (0: at once) the call fails with acquire_timeout; a negative
+ * value waits without limit (the default). */
+void sb_resources_set_acquire_timeout(sb_resources *resources, int64_t ms);
 int sb_resources_clear(sb_resources *resources, sb_error *err);
 int sb_resources_close(sb_resources *resources, sb_error *err);
 void sb_resources_free(sb_resources *resources);

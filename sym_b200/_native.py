@@ -97,6 +97,7 @@ def lib():
         "sb_resources_stats": (ctypes.c_int, [vp, ctypes.c_char_p, sz]),
         "sb_resources_streams": (ctypes.c_int, [vp, i32, pp, pp, ep]),
         "sb_resources_clear": (ctypes.c_int, [vp, ep]),
+        "sb_resources_set_acquire_timeout": (None, [vp, ctypes.c_int64]),
         "sb_resources_close": (ctypes.c_int, [vp, ep]),
         "sb_resources_free": (None, [vp]),
         "sb_prepare_dispatch_group": (ctypes.c_int, [ctypes.POINTER(SbGroupEntry), sz, pp, ep]),

@@ -686,6 +686,8 @@ int sb_resources_streams(sb_resources *r, int32_t device, void **copy_stream, vo
   return 0;
 }
 
+void sb_resources_set_acquire_timeout(sb_resources *r, int64_t ms) { r->res.setAcquireTimeout(ms); }
+
 int sb_resources_clear(sb_resources *r, sb_error *err) {
   if (auto e = r->res.clear())
     return setErr(err, e->code, e->message);

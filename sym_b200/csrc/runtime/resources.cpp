@@ -4,6 +4,7 @@
 #include "sb_cuda.h"
 
 #include <algorithm>
+#include <chrono>
 
 namespace reloc {
 namespace dispatch {
@@ -81,7 +82,13 @@ TransferOutcome Resources::withContext(int device,
     out.error = e;
     return out;
   }
-  std::lock_guard<std::mutex> lease(slot->lease); // FIFO per context
+  std::unique_lock<std::timed_mutex> lease(slot->lease, std::defer_lock); // one call at a time per context
+  if (acquireTimeoutMs_ < 0) {
+    lease.lock();
+  } else if (!lease.try_lock_for(std::chrono::milliseconds(acquireTimeoutMs_))) {
+    out.error = terr("acquire_timeout", "typed context admission timed out");
+    return out;
+  }
   out.error = fn(*slot->backend);
   out.completion = TransferCompletion::Complete;
   // Idle scratch beyond the retained quota is released at the end of a
@@ -296,7 +303,7 @@ std::optional<TransferError> Resources::clear() {
   if (quarantined_)
     return terr("completion_unknown", "quarantined resources are never released");
   for (auto &kv : slots_)
-    std::lock_guard<std::mutex> lease(kv.second->lease);
+    std::lock_guard<std::timed_mutex> lease(kv.second->lease);
   slots_.clear();
   return std::nullopt;
 }

@@ -532,10 +532,14 @@ class DispatchResources:
                  max_streams=8, max_contexts=1, max_contexts_per_device=1, acquire_timeout_ms=None):
         out = ctypes.c_void_p()
         err = SbError()
+        if acquire_timeout_ms is not None and int(acquire_timeout_ms) < 0:
+            raise ValueError("acquire_timeout_ms must be None or non-negative")
         _native.lib().sb_resources_create(int(max_retained_bytes), int(max_live_bytes or 0), int(max_contexts),
                                           ctypes.byref(out), ctypes.byref(err))
         self.handle = out
         self._closed = False
+        if acquire_timeout_ms is not None:
+            _native.lib().sb_resources_set_acquire_timeout(self.handle, int(acquire_timeout_ms))
 
     def stats(self):
         return json_call(_native.lib().sb_resources_stats, self.handle)

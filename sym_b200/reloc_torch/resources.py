@@ -23,7 +23,8 @@ class TransferResources:
         self._pid = os.getpid()
         self._typed = pyreloc.DispatchResources(max_retained_bytes=max_typed_retained_bytes,
                                                 max_live_bytes=max_typed_live_bytes,
-                                                max_contexts=max_typed_contexts)
+                                                max_contexts=max_typed_contexts,
+                                                acquire_timeout_ms=typed_acquire_timeout_ms)
 
     @property
     def native_typed(self):

@@ -99,3 +99,58 @@ def test_context_limit_retires_the_least_recently_used_context():
     st = res.stats()
     assert st["contexts"] == 1 and st["evictions"] == 2
     res.close()
+
+
+def test_acquire_timeout_bounds_the_wait_for_a_busy_context():
+    """A call that finds its context leased by another call fails with
+    acquire_timeout after ``acquire_timeout_ms`` (0: at once), and a call
+    that may wait long enough runs once the lease ends (reference
+    DispatchResources acquireTimeoutMs)."""
+    import threading
+    import time
+
+    import torch
+    from sym_b200 import pyreloc
+
+    blob, sym, params, q = _case(64, 256)
+    want = expected(blob, sym, params, q)
+    busy = pyreloc.DispatchResources(acquire_timeout_ms=0)
+    # a long blocking call holds the context: 1.5 GiB from pageable memory
+    big_blob, big_sym, big_params, big = _case(49152, 32768, seed=5)
+    started, done = threading.Event(), threading.Event()
+
+    def hold():
+        from sym_b200 import pyreloc as p
+
+        bound = p.bind_typed(p.load_typed_plan(big_blob), big_sym, big_params)
+        tmpl = p.prepare_dispatch_template(bound, "h2d", "cuda")
+        info = bound.describe()
+        out = torch.empty(bound.destination_bytes, dtype=torch.uint8, device="cuda:0")
+        sv = p.BufferView(big.ctypes.data, big.nbytes, 0, info["source_extents"], dense(info["source_extents"]),
+                          1, "host", -1)
+        dv = p.BufferView(out.data_ptr(), out.numel(), 0, info["result_extents"], dense(info["result_extents"]),
+                          2, "cuda", 0)
+        req = p.prepare_dispatch_from_template(tmpl, sv, dv)
+        started.set()
+        p.execute_dispatch(req, resources=busy, route="dma_ring")
+        done.set()
+
+    t = threading.Thread(target=hold)
+    t.start()
+    started.wait()
+    time.sleep(0.005)
+    raised = None
+    if not done.is_set():
+        with pytest.raises(pyreloc.TransferError) as info:
+            _run(busy, blob, sym, params, q)
+        raised = info.value.code
+    t.join()
+    assert raised in ("acquire_timeout", None)
+    assert raised == "acquire_timeout" or done.is_set()
+    patient = pyreloc.DispatchResources(acquire_timeout_ms=60_000)
+    out, _ = _run(patient, blob, sym, params, q)
+    assert np.array_equal(out, want)
+    out, _ = _run(busy, blob, sym, params, q)  # idle now: the zero timeout admits at once
+    assert np.array_equal(out, want)
+    busy.close()
+    patient.close()
