@@ -115,7 +115,9 @@ def _function_kinds():
     try:
         qd = torch.ops.quantized_decomposed
         for op, kind in ((qd.dequantize_per_tensor, "dequantize_tensor"),
-                         (qd.dequantize_per_channel, "dequantize_channel")):
+                         (qd.dequantize_per_channel, "dequantize_channel"),
+                         (qd.quantize_per_tensor, "quantize_decomposed"),
+                         (qd.quantize_per_channel, "quantize_decomposed")):
             kinds[op] = kind
             for name in op.overloads():
                 kinds[getattr(op, name)] = kind
@@ -581,6 +583,11 @@ def _step(walk, node):
         walk.pad(tuple(widths), 0 if value is None else value)
     elif k in ("dequantize_tensor", "dequantize_channel"):
         walk.dequantize(node, per_channel=k == "dequantize_channel")
+    elif k == "quantize_decomposed":
+        # the decomposition divides by the scale (a reciprocal rounded in
+        # double) and converts NaN as the platform does: not the plan
+        # format's quantize, bit for bit (the reference importer excludes it too)
+        raise _Reject("quantize_semantics_unproved")
     elif k == "pad":
         widths = node.args[1] if len(node.args) > 1 else node.kwargs.get("pad")
         mode = node.args[2] if len(node.args) > 2 else node.kwargs.get("mode", "constant")

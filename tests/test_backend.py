@@ -324,3 +324,15 @@ def test_bind_shape_caches_without_sharing_state():
         bindings["s0"] = -1
         declared["scale"][1].append(7)
     assert compiled.bind_shape((64, 96)) == ({"s0": 64, "s1": 96}, {"scale": ("float32", [64])})
+
+
+def test_decomposed_quantize_is_excluded_with_the_reference_reason():
+    import torch
+    import torch.ao.quantization.fx._decomposed  # noqa: F401
+    from sym_b200.reloc_torch.fx_import import import_graph
+
+    qd = torch.ops.quantized_decomposed
+    ((gm, ex),) = _dynamo_graphs(lambda x: qd.quantize_per_tensor(x, 0.05, 0, -128, 127, torch.int8).cuda(),
+                                 torch.zeros(8, 4))
+    r = import_graph(gm, ex)
+    assert not r.candidates and "quantize_semantics_unproved" in [e.reason for e in r.exclusions]
