@@ -1,5 +1,5 @@
 #!/usr/bin/env python3
-"""Benchmark: Llama-70B-shaped int8 weight fetch.
+"""Benchmark: Llama-70B-shaped int8 weight fetch (the sharded weight-fetch configuration).
 
 One step = one model pass: 16 layers x {q, k, v, o, gate, up, down} int8
 [out, in] matrices with per-row f32 scales (lognormal(-5, 0.5)), each
@@ -14,7 +14,7 @@ rows and an in-place NCCL all-gather assembles the layer.
 
 Metric: layers/s of the whole job (every layer assembled on every GPU), with
 relocated GB/s per GPU and its fraction of the measured pinned-memcpy H2D
-ceiling alongside (BASELINE.json metric).
+ceiling alongside.
 
   value : inputs already resident in HBM (each rank's int8 shards, or the
           whole int8 matrices with --multi allgather); the timed work is the

@@ -1,7 +1,7 @@
 // Lowering of typed programs to the fused sm_100a kernels and the H2D data
 // paths. See device_plan.hpp.
 //
-// Data paths (routes a/b):
+// Data paths (routes a and b of the design):
 //  * DmaRing: the raw source is cut into chunks of whole source rows (the
 //    coalesced axis with the largest source stride), each chunk DMA'd by the
 //    copy engine into a slot of an HBM ring on the copy stream, and the fused

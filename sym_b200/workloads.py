@@ -8,11 +8,11 @@ bounded asynchronous window), per-device retained resources, ``reference``
 and ``close``, plus the offline helper ``quantize_per_channel``.
 Its default recipe is the reference's own (int8 ``[in, out]``, per-output-
 channel f32 scale on axis 1 -> dequantize -> transpose -> f32 ``[out, in]``);
-``layout="out_in_f16"`` selects the BASELINE weight-streaming recipe (int8
+``layout="out_in_f16"`` selects the weight-streaming benchmark recipe (int8
 ``[out, in]``, per-row scale -> dequantize -> f16 RNE -> transpose -> f16
 ``[in, out]``).
 
-``ShardedLayerFetch`` is the multi-GPU path of BASELINE config 5: rank ``k`` of
+``ShardedLayerFetch`` is the all-gather multi-GPU path of the sharded weight fetch: rank ``k`` of
 ``N`` produces result rows ``[k*in/N, (k+1)*in/N)`` of every matrix (the
 matrix's source columns, pulled over this GPU's own PCIe link by 2-D DMA),
 then an in-place NCCL all-gather over NVLink assembles the full matrix on

@@ -16,7 +16,7 @@ Two sources, both written as small JSON fixtures beside this script:
   encoded by this repository's plan encoder, executed by the reference runtime
   (decode + bindTyped + executeHost) on seeded inputs; sha256 of the output.
 
-Usage: python tests/golden/make_golden.py [--reference /root/reference]
+Usage: python tests/golden/make_golden.py [--reference PATH-TO-THE-REFERENCE-CHECKOUT]
 """
 from __future__ import annotations
 

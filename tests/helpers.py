@@ -35,7 +35,7 @@ def dtypes_of(stages_or_desc):
     return [st[0]["input_dtype"]] + [s["output_dtype"] for s in st]
 
 
-# ---- config-shaped recipes (parameterized sizes) ---------
+# ---- config-shaped recipes (the benchmark configurations, parameterized sizes) ----
 
 def recipe_c1():
     """C1: f32 [N] -> reshape [N floordiv 64, 64] -> transpose -> [64, N floordiv 64] (wire v0)."""

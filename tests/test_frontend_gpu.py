@@ -38,7 +38,7 @@ def test_weight_fetcher_reference_recipe(shape):
 
 @pytest.mark.parametrize("shape", [(4096, 4096), (1000, 2304)])
 def test_weight_fetcher_f16_recipe(shape):
-    """int8 [out, in] + per-row scale -> f16 [in, out] (BASELINE configs 4/5)."""
+    """int8 [out, in] + per-row scale -> f16 [in, out] (the weight-streaming configs)."""
     import torch
     from sym_b200.workloads import WeightFetcher
 

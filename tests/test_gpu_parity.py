@@ -3,7 +3,7 @@ bit-identical to the reference typed CPU executor on the same inputs.
 
 The checker is the reference runtime itself (oracle/_ref) when it is built,
 else the C restatement (oracle/typed_oracle.c) pinned by test_oracle.py.
-Inputs are seeded; the configurations follow BASELINE.json at sizes the
+Inputs are seeded; the configurations follow the benchmark configs at sizes the
 checker finishes in seconds (full-size runs are covered by the bench's
 size-independent checks)."""
 import numpy as np
