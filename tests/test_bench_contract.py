@@ -1,0 +1,39 @@
+"""The benchmark's JSON-line contract for the reference arm, which runs on the
+host cores alone: one line with the metric, value, unit, the CPU baseline's
+description and an e2e block; configs without a CPU counterpart print an
+``unavailable`` line and exit 0."""
+import json
+import subprocess
+import sys
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def _run(*args):
+    out = subprocess.run([sys.executable, str(ROOT / "bench.py"), *args], capture_output=True, text=True,
+                         timeout=600, cwd=ROOT)
+    assert out.returncode == 0, out.stderr[-2000:]
+    lines = [ln for ln in out.stdout.splitlines() if ln.startswith("{")]
+    assert len(lines) == 1, out.stdout[-2000:]
+    return json.loads(lines[0])
+
+
+def test_reference_arm_prints_one_contract_line():
+    line = _run("--impl", "reference", "--config", "c2", "--steps", "3", "--warmup", "3")
+    assert line["impl"] == "reference"
+    if "unavailable" in line:  # the reference runtime is not built here
+        return
+    for key in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better",
+                "scaling", "dtype", "data", "config", "cpu_baseline", "e2e"):
+        assert key in line, key
+    assert line["value"] > 0 and line["unit"] == "images/s" and line["higher_is_better"] is True
+    cpu = line["cpu_baseline"]
+    assert cpu["kind"] == "reference" and cpu["cores"] >= 1 and cpu["value"] == line["value"] and cpu["sample"]
+    e2e = line["e2e"]
+    assert e2e["value"] == line["value"] and e2e["h2d_bytes_per_step"] == 0 and e2e["d2h_bytes_per_step"] == 0
+
+
+def test_latency_config_has_no_cpu_arm():
+    line = _run("--impl", "reference", "--config", "latency")
+    assert line["impl"] == "reference" and line["unavailable"]
