@@ -1,0 +1,133 @@
+"""The importer's recipes mean what the Torch ops mean: each accepted region's
+recipe, encoded and executed by the reference runtime on the host (the
+checker, not the product), gives bit for bit the result of the same ops run
+eagerly by PyTorch on the CPU. This pins the importer's translation (axes,
+scales, zero points, pads, casts, symbols) without a GPU; the GPU tests then
+pin the kernels against the same reference runtime."""
+import numpy as np
+import pytest
+
+from test_backend import _dynamo_graphs
+
+pytestmark = pytest.mark.skipif("not __import__('oracle.ref', fromlist=['ref']).available()",
+                                reason="reference runtime not built")
+
+
+def _param_entry(tensor, declared_dtype):
+    import torch
+
+    if declared_dtype == "int32":
+        tensor = tensor.to(torch.int32)
+    arr = tensor.detach().contiguous().numpy()
+    return (declared_dtype, list(arr.shape), arr.tobytes())
+
+
+def _reference_result(gm, ex, src, params):
+    """The single candidate's recipe executed by the reference runtime."""
+    from oracle import ref
+    from sym_b200.reloc_torch.compiler import CompilerClient
+    from sym_b200.reloc_torch.fx_import import import_graph
+
+    (c,) = import_graph(gm, ex).candidates
+    compiled = CompilerClient.from_environment().compile(c.recipe)
+    bindings = compiled.source_symbols(tuple(src.shape))
+    declared = {p.name: p.dtype for p in compiled.recipe.parameter_bindings}
+    named = dict(zip(c.parameters, params))
+    raw = np.ascontiguousarray(src.numpy()).view(np.uint8).reshape(-1)
+    if compiled.typed:
+        prog = ref.TypedProgram(compiled.plan_bytes, bindings,
+                                {n: _param_entry(named[n], d) for n, d in declared.items()})
+        return prog.execute(raw), c
+    return ref.LayoutPlan(compiled.plan_bytes, bindings).execute(raw), c
+
+
+def _bits(t):
+    import torch
+
+    t = t.contiguous()
+    if t.dtype in (torch.float16, torch.bfloat16):
+        t = t.view(torch.int16)  # numpy has no bfloat16
+    return np.ascontiguousarray(t.numpy()).view(np.uint8).reshape(-1)
+
+
+def test_decomposed_dequantize_per_channel_zero_points_f16_transpose():
+    import torch
+    import torch.ao.quantization.fx._decomposed  # noqa: F401
+
+    qd = torch.ops.quantized_decomposed
+    g = torch.Generator().manual_seed(3)
+    q = torch.randint(-128, 128, (48, 40), dtype=torch.int8, generator=g)
+    s = torch.exp(torch.randn(48, generator=g) - 4)
+    z = torch.randint(-9, 9, (48,), dtype=torch.int64, generator=g)
+
+    def body(q, s, z):
+        return qd.dequantize_per_channel(q, s, z, 0, -128, 127, torch.int8).half().t().contiguous()
+
+    ((gm, ex),) = _dynamo_graphs(lambda q, s, z: body(q, s, z).cuda(), q, s, z)
+    got, _ = _reference_result(gm, ex, q, (s, z))
+    assert np.array_equal(got, _bits(body(q, s, z)))
+
+
+def test_decomposed_dequantize_per_tensor_inline_and_out_dtype():
+    import torch
+    import torch.ao.quantization.fx._decomposed  # noqa: F401
+
+    qd = torch.ops.quantized_decomposed
+    q = torch.randint(-128, 128, (33, 17), dtype=torch.int8, generator=torch.Generator().manual_seed(4))
+
+    def body(q):
+        return qd.dequantize_per_tensor(q, 0.0123, -7, -128, 127, torch.int8)
+
+    ((gm, ex),) = _dynamo_graphs(lambda q: body(q).cuda(), q)
+    got, _ = _reference_result(gm, ex, q, ())
+    assert np.array_equal(got, _bits(body(q)))
+
+    s = torch.exp(torch.randn(17, generator=torch.Generator().manual_seed(5)) - 3)
+
+    def body2(q, s):
+        return qd.dequantize_per_channel(q, s, None, 1, -128, 127, torch.int8, out_dtype=torch.bfloat16)
+
+    ((gm, ex),) = _dynamo_graphs(lambda q, s: body2(q, s).cuda(), q, s)
+    got, _ = _reference_result(gm, ex, q, (s,))
+    assert np.array_equal(got, _bits(body2(q, s)))
+
+
+def test_int8_scale_multiply_and_channels_last_pad_cast():
+    import torch
+    import torch.nn.functional as F
+
+    g = torch.Generator().manual_seed(6)
+    q = torch.randint(-128, 128, (24, 40), dtype=torch.int8, generator=g)
+    s = torch.exp(torch.randn(24, generator=g) - 4)
+
+    def body(q, s):
+        return (q.float() * s[:, None]).half().t().contiguous()
+
+    ((gm, ex),) = _dynamo_graphs(lambda q, s: body(q, s).cuda(), q, s)
+    got, _ = _reference_result(gm, ex, q, (s,))
+    assert np.array_equal(got, _bits(body(q, s)))
+
+    x = torch.randn(2, 3, 7, 5, generator=g)
+    x.view(-1)[:3] = torch.tensor([float("inf"), -0.0, 65520.0])
+
+    def body2(x):
+        return F.pad(x.permute(0, 2, 3, 1), (0, 1)).half()
+
+    ((gm, ex),) = _dynamo_graphs(lambda x: body2(x).cuda(), x)
+    got, _ = _reference_result(gm, ex, x, ())
+    assert np.array_equal(got, _bits(body2(x)))
+
+
+@pytest.mark.parametrize("shape", [(2, 8, 1024), (3, 5, 1024)])
+def test_dynamic_head_split_binds_for_other_sizes(shape):
+    """A dynamic capture (traced at one size) run by the reference at another."""
+    import torch
+
+    def body(x):
+        return x.view(x.shape[0], x.shape[1], 16, 64).transpose(1, 2).contiguous().half()
+
+    ((gm, ex),) = _dynamo_graphs(lambda x: body(x).cuda(), torch.zeros(4, 6, 1024))
+    x = torch.randn(shape, generator=torch.Generator().manual_seed(7))
+    got, c = _reference_result(gm, ex, x, ())
+    assert any(type(e).__name__ == "Symbol" for e in c.recipe.source.shape)
+    assert np.array_equal(got, _bits(body(x)))
