@@ -104,6 +104,8 @@ def _function_kinds():
 
     aten = torch.ops.aten
     kinds = {torch.permute: "permute", torch.transpose: "transpose", torch.t: "t", torch.reshape: "view",
+             torch.movedim: "movedim", torch.moveaxis: "movedim", torch.swapaxes: "transpose",
+             torch.swapdims: "transpose", torch.unflatten: "unflatten",
              torch.flatten: "flatten", torch.squeeze: "squeeze", torch.unsqueeze: "unsqueeze", torch.clone: "clone",
              F.pad: "pad", torch._C._nn.pad: "pad", operator.mul: "mul", torch.mul: "mul",
              aten.permute.default: "permute", aten.transpose.int: "transpose", aten.t.default: "t",
@@ -132,8 +134,12 @@ def _kind(node):
     if node.op == "call_method":
         t = node.target
         if t in ("permute", "transpose", "t", "reshape", "view", "flatten", "squeeze", "unsqueeze", "contiguous",
-                 "clone"):
+                 "clone", "movedim", "unflatten"):
             return "view" if t == "reshape" else t
+        if t in ("swapaxes", "swapdims"):
+            return "transpose"
+        if t == "moveaxis":
+            return "movedim"
         if t in ("to", "cuda"):
             return "to"
         if t in _METHOD_CASTS:
@@ -142,6 +148,8 @@ def _kind(node):
             return "mul"
         return None
     if node.op == "call_function":
+        if node.target is getattr and len(node.args) == 2 and node.args[1] in ("T", "mT"):
+            return "attr_" + node.args[1]  # x.T (all dims reversed), x.mT (last two swapped)
         kinds = _function_kinds()
         kind = kinds.get(node.target)
         if kind is None and "quantized_decomposed" in str(node.target):
@@ -541,6 +549,50 @@ def _step(walk, node):
     elif k == "t":
         _require(len(walk.shape) <= 2, "unsupported_permutation")
         walk.permute((1, 0) if len(walk.shape) == 2 else (0,))
+    elif k == "attr_T":
+        walk.permute(tuple(reversed(range(len(walk.shape)))))
+    elif k == "attr_mT":
+        rank = len(walk.shape)
+        _require(rank >= 2, "unsupported_permutation")
+        walk.permute(tuple(range(rank - 2)) + (rank - 1, rank - 2))
+    elif k == "movedim":
+        src = node.args[1] if len(node.args) > 1 else node.kwargs.get("source")
+        dst = node.args[2] if len(node.args) > 2 else node.kwargs.get("destination")
+        src = (src,) if type(src) is int else tuple(src) if isinstance(src, (tuple, list)) else None
+        dst = (dst,) if type(dst) is int else tuple(dst) if isinstance(dst, (tuple, list)) else None
+        _require(src is not None and dst is not None and len(src) == len(dst), "unsupported_permutation")
+        rank = len(walk.shape)
+        _ints(src + dst, "unsupported_permutation")
+        _require(all(-rank <= d < rank for d in src + dst), "unsupported_permutation")
+        src, dst = [d % rank for d in src], [d % rank for d in dst]
+        _require(len(set(src)) == len(src) and len(set(dst)) == len(dst), "unsupported_permutation")
+        # result dim dst[i] is source dim src[i]; the other dims keep their order
+        perm = [None] * rank
+        for a, b in zip(src, dst):
+            perm[b] = a
+        rest = iter(d for d in range(rank) if d not in src)
+        perm = tuple(p if p is not None else next(rest) for p in perm)
+        walk.permute(perm)
+    elif k == "unflatten":
+        dim = node.args[1] if len(node.args) > 1 else node.kwargs.get("dim")
+        sizes = node.args[2] if len(node.args) > 2 else node.kwargs.get("sizes")
+        _require(type(dim) is int and isinstance(sizes, (tuple, list)), "unsupported_view_dimension")
+        rank = len(walk.shape)
+        _require(-rank <= dim < rank, "unsupported_view_dimension")
+        dim %= rank
+        sizes = _ints(sizes, "unsupported_reshape")
+        _require(sizes.count(-1) <= 1 and all(e >= 0 or e == -1 for e in sizes), "unsupported_reshape")
+        known = [Const(e) for e in sizes if e != -1]
+        if -1 in sizes:
+            q = _quotient([walk.sym[dim]], known)
+            _require(q is not None, "symbolic_reshape")
+            part = [q if e == -1 else Const(e) for e in sizes]
+        else:
+            part = [Const(e) for e in sizes]
+        concrete = list(walk.shape[:dim]) + list(sizes) + list(walk.shape[dim + 1:])
+        sym = walk.sym[:dim] + tuple(part) + walk.sym[dim + 1:]
+        _require(product_key(sym) == product_key(walk.sym), "symbolic_reshape")
+        walk.reshape(concrete, sym_target=sym)
     elif k == "view":
         _view(walk, node)
     elif k == "flatten":

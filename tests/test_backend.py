@@ -336,3 +336,18 @@ def test_decomposed_quantize_is_excluded_with_the_reference_reason():
                                  torch.zeros(8, 4))
     r = import_graph(gm, ex)
     assert not r.candidates and "quantize_semantics_unproved" in [e.reason for e in r.exclusions]
+
+
+def test_inexact_dynamic_unflatten_keeps_the_example_shape():
+    """``unflatten(d, (4, -1))`` of a dynamic dim (a quotient the plan cannot
+    prove exact) captures the example's sizes; the region takes only that
+    shape."""
+    import torch
+    from sym_b200.reloc_torch.backend import RelocBackend
+    from sym_b200.reloc_torch.symbolic import Const
+
+    fn = lambda x: x.unflatten(2, (4, -1)).transpose(1, 2).contiguous().half().cuda()  # noqa: E731
+    ((gm, ex),) = _dynamo_graphs(fn, torch.zeros(4, 6, 8))
+    (region,) = RelocBackend()(gm, ex).regions
+    assert all(isinstance(e, Const) for e in region.candidate.recipe.source.shape)
+    assert region._eligible(torch.zeros(4, 6, 8), ()) and not region._eligible(torch.zeros(3, 6, 8), ())

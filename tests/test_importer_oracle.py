@@ -131,3 +131,31 @@ def test_dynamic_head_split_binds_for_other_sizes(shape):
     got, c = _reference_result(gm, ex, x, ())
     assert any(type(e).__name__ == "Symbol" for e in c.recipe.source.shape)
     assert np.array_equal(got, _bits(body(x)))
+
+
+@pytest.mark.parametrize("name", ["T", "mT", "movedim", "movedim_tuple", "swapaxes", "unflatten", "unflatten_dyn"])
+def test_more_view_ops_match_eager(name):
+    """``x.T``, ``x.mT``, ``movedim``, ``swapaxes`` and ``unflatten`` (with a
+    -1, also in a dynamic capture) become the same permutation or reshape
+    the eager ops compute, with a cast so the plan is a typed one."""
+    import torch
+
+    bodies = {
+        "T": lambda x: x.T.contiguous().half(),
+        "mT": lambda x: x.mT.contiguous().half(),
+        "movedim": lambda x: x.movedim(0, 2).contiguous().half(),
+        "movedim_tuple": lambda x: torch.movedim(x, (0, 1), (2, 0)).contiguous().half(),
+        "swapaxes": lambda x: x.swapaxes(0, 2).contiguous().half(),
+        "unflatten": lambda x: x.unflatten(2, (2, -1)).transpose(1, 2).contiguous().half(),
+        "unflatten_dyn": lambda x: x.unflatten(1, (-1, 1)).transpose(0, 2).contiguous().half(),
+    }
+    body = bodies[name]
+    x = torch.randn(3, 5, 8, generator=torch.Generator().manual_seed(8))
+    if name == "unflatten_dyn":  # traced at one size, run at another: the -1 is an exact quotient
+        ((gm, ex),) = _dynamo_graphs(lambda x: body(x).cuda(), torch.zeros(4, 6, 8))
+    else:
+        ((gm, ex),) = _dynamo_graphs(lambda x: body(x).cuda(), x)
+    got, c = _reference_result(gm, ex, x, ())
+    if name == "unflatten_dyn":
+        assert any(type(e).__name__ == "Symbol" for e in c.recipe.source.shape)
+    assert np.array_equal(got, _bits(body(x)))
