@@ -33,7 +33,7 @@ def _reference_result(gm, ex, src, params):
     bindings = compiled.source_symbols(tuple(src.shape))
     declared = {p.name: p.dtype for p in compiled.recipe.parameter_bindings}
     named = dict(zip(c.parameters, params))
-    raw = np.ascontiguousarray(src.numpy()).view(np.uint8).reshape(-1)
+    raw = _bits(src)
     if compiled.typed:
         prog = ref.TypedProgram(compiled.plan_bytes, bindings,
                                 {n: _param_entry(named[n], d) for n, d in declared.items()})
@@ -158,4 +158,27 @@ def test_more_view_ops_match_eager(name):
     got, c = _reference_result(gm, ex, x, ())
     if name == "unflatten_dyn":
         assert any(type(e).__name__ == "Symbol" for e in c.recipe.source.shape)
+    assert np.array_equal(got, _bits(body(x)))
+
+
+@pytest.mark.parametrize("name", ["int8_half", "int8_bf16_t", "f16_float_t", "bf16_float", "f32_bf16_pad"])
+def test_casts_match_eager(name):
+    """int8 -> f16/bf16 (exact: every int8 is representable), f16/bf16 -> f32
+    widening and f32 -> bf16 narrowing with a pad, as eager PyTorch computes
+    them on finite inputs."""
+    import torch
+    import torch.nn.functional as F
+
+    g = torch.Generator().manual_seed(9)
+    cases = {
+        "int8_half": (lambda x: x.half(), torch.randint(-128, 128, (7, 33), dtype=torch.int8, generator=g)),
+        "int8_bf16_t": (lambda x: x.to(torch.bfloat16).t().contiguous(),
+                        torch.randint(-128, 128, (7, 33), dtype=torch.int8, generator=g)),
+        "f16_float_t": (lambda x: x.float().t().contiguous(), (torch.randn(9, 20, generator=g) * 1000).half()),
+        "bf16_float": (lambda x: x.float(), (torch.randn(9, 20, generator=g) * 1e30).bfloat16()),
+        "f32_bf16_pad": (lambda x: F.pad(x.to(torch.bfloat16), (1, 2)), torch.randn(6, 10, generator=g) * 3e38),
+    }
+    body, x = cases[name]
+    ((gm, ex),) = _dynamo_graphs(lambda x: body(x).cuda(), x)
+    got, _ = _reference_result(gm, ex, x, ())
     assert np.array_equal(got, _bits(body(x)))
