@@ -93,3 +93,47 @@ def test_random_recipes_bind_and_execute_like_the_reference(ref_lib, seed):
     dts = [bound["stages"][0]["input_dtype"]] + [s["output_dtype"] for s in bound["stages"]]
     mine = oracle.Program.from_description(bound, dts).execute(raw)
     assert np.array_equal(mine, theirs.execute(raw))
+
+
+def _random_layout(seed):
+    from sym_b200.reloc_torch import recipe as R
+    from sym_b200.reloc_torch import symbolic as S
+
+    rng = np.random.default_rng(seed)
+    rank = int(rng.integers(2, 5))
+    shape = [int(rng.integers(1, 7)) for _ in range(rank)]
+    dtype = ["float32", "float16", "int8"][int(rng.integers(0, 3))]
+    ops, cur = [R.Transpose(tuple(int(p) for p in rng.permutation(rank)))], None
+    cur = [shape[p] for p in ops[0].perm]
+    if rng.random() < 0.5:
+        axis = int(rng.integers(0, rank))
+        lo, hi = int(rng.integers(0, 3)), int(rng.integers(1, 3))
+        ops.append(R.Pad(axis, S.Const(lo), S.Const(hi), R.Fill(dtype, 0)))
+        cur[axis] += lo + hi
+    src = tuple(S.Const(e) for e in shape)
+    dst = tuple(S.Const(e) for e in cur)
+    return (R.Recipe(R.TensorSpec(src, S.dense_strides(src), S.Const(0), dtype), tuple(ops),
+                     R.TensorSpec(dst, S.dense_strides(dst), S.Const(0), dtype), "h2d"), shape, dtype)
+
+
+@pytest.mark.parametrize("seed", range(64))
+def test_random_layout_plans_bind_and_execute_like_the_reference(ref_lib, seed):
+    """Layout-only (wire v0) random permutations with pads: the product binder
+    and the C restatement against the reference."""
+    from oracle import oracle
+    from sym_b200 import pyreloc
+    from test_plan_parity import LAYOUT_KEYS
+
+    recipe, shape, dtype = _random_layout(seed)
+    blob = encode(recipe)
+    assert pyreloc.wire_version(blob) == 0
+    theirs = ref_lib.LayoutPlan(blob, {})
+    mine = pyreloc.bind(pyreloc.load_plan(blob), {}).describe()
+    for k in LAYOUT_KEYS:
+        assert mine[k] == theirs.info[k], k
+    width = {"float32": 4, "float16": 2, "int8": 1}[dtype]
+    raw = np.random.default_rng(2000 + seed).integers(0, 256, int(np.prod(shape)) * width, dtype=np.uint8)
+    desc = {"layout": mine, "result_extents": [mine["total_bytes"] // mine["element_size"]], "stages": [],
+            "destination_bytes": mine["total_bytes"]}
+    got = oracle.Program.from_description(desc, [dtype]).execute(raw)
+    assert np.array_equal(got, theirs.execute(raw))
