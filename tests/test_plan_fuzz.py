@@ -137,3 +137,67 @@ def test_random_layout_plans_bind_and_execute_like_the_reference(ref_lib, seed):
             "destination_bytes": mine["total_bytes"]}
     got = oracle.Program.from_description(desc, [dtype]).execute(raw)
     assert np.array_equal(got, theirs.execute(raw))
+
+
+def _random_symbolic(seed):
+    """A typed recipe whose source has one or two symbolic extents, permuted,
+    optionally with a pad and a per-channel scale on a symbolic axis."""
+    from sym_b200.reloc_torch import recipe as R
+    from sym_b200.reloc_torch import symbolic as S
+
+    rng = np.random.default_rng(seed)
+    rank = int(rng.integers(2, 5))
+    names = ["a", "b"][:int(rng.integers(1, 3))]
+    sym_axes = sorted(int(x) for x in rng.choice(rank, size=len(names), replace=False))
+    src = [S.Const(int(rng.integers(1, 6))) for _ in range(rank)]
+    for name, ax in zip(names, sym_axes):
+        src[ax] = S.Symbol(name)
+    perm = tuple(int(p) for p in rng.permutation(rank))
+    cur = [src[p] for p in perm]
+    ops = [R.Transpose(perm)]
+    per_channel = rng.random() < 0.5
+    if per_channel:
+        axis = int(rng.integers(0, rank))
+        ops.append(R.Dequantize("float32", R.BindingParam("scale", "float32", (cur[axis],)), None, axis, "affine"))
+        src_dtype, dst_dtype = "int8", "float32"
+    else:
+        ops.append(R.Cast("float16", "ieee_rne"))
+        src_dtype, dst_dtype = "float32", "float16"
+    if rng.random() < 0.5:
+        axis = int(rng.integers(0, rank))
+        if not (per_channel and axis == ops[1].axis):
+            lo, hi = int(rng.integers(0, 3)), int(rng.integers(1, 3))
+            ops.append(R.Pad(axis, S.Const(lo), S.Const(hi), R.Fill(dst_dtype, 0)))
+            cur[axis] = S.add(S.add(cur[axis], lo), hi)
+    recipe = R.Recipe(R.TensorSpec(tuple(src), S.dense_strides(tuple(src)), S.Const(0), src_dtype), tuple(ops),
+                      R.TensorSpec(tuple(cur), S.dense_strides(tuple(cur)), S.Const(0), dst_dtype), "h2d")
+    sizes = {name: int(rng.integers(1, 9)) for name in names}
+    return recipe, src, sizes, per_channel, ops
+
+
+@pytest.mark.parametrize("seed", range(64))
+def test_random_symbolic_recipes_bind_like_the_reference(ref_lib, seed):
+    """Symbols bound at random sizes: the product binder and the reference
+    binder produce the same bound layout, footprints and stage arithmetic,
+    and the C restatement executes like the reference runtime."""
+    from oracle import oracle
+    from sym_b200 import pyreloc
+
+    recipe, src, sizes, per_channel, ops = _random_symbolic(seed)
+    blob = encode(recipe)
+    shape = [sizes[e.name] if hasattr(e, "name") else e.value for e in src]
+    params = {}
+    if per_channel:
+        n = ops[1].scale.extents[0]
+        n = sizes[n.name] if hasattr(n, "name") else n.value
+        params["scale"] = ("float32", [n], np.exp(np.random.default_rng(seed).normal(-3, 0.5, n))
+                           .astype(np.float32).tobytes())
+    _compare_typed(ref_lib, blob, sizes, params)
+    count = int(np.prod(shape))
+    rng = np.random.default_rng(3000 + seed)
+    raw = (rng.integers(-128, 128, count, dtype=np.int8) if per_channel
+           else (rng.standard_normal(count) * 4).astype(np.float32)).view(np.uint8).reshape(-1)
+    bound = pyreloc.bind_typed(pyreloc.load_typed_plan(blob), sizes, params).describe()
+    dts = [bound["stages"][0]["input_dtype"]] + [s["output_dtype"] for s in bound["stages"]]
+    got = oracle.Program.from_description(bound, dts).execute(raw)
+    assert np.array_equal(got, ref_lib.TypedProgram(blob, sizes, params).execute(raw))
