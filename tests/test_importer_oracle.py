@@ -182,3 +182,80 @@ def test_casts_match_eager(name):
     ((gm, ex),) = _dynamo_graphs(lambda x: body(x).cuda(), x)
     got, _ = _reference_result(gm, ex, x, ())
     assert np.array_equal(got, _bits(body(x)))
+
+
+def _random_chain(seed):
+    """A random chain of layout ops, at most one narrowing cast and an
+    optional constant pad on the last axis, as eager callables."""
+    import torch
+    import torch.nn.functional as F
+
+    rng = np.random.default_rng(seed)
+    rank = int(rng.integers(2, 5))
+    shape = tuple(int(rng.integers(2, 6)) for _ in range(rank))
+    steps, cur = [], list(shape)
+    for _ in range(int(rng.integers(1, 5))):
+        kind = ["permute", "transpose", "flatten", "unsqueeze", "mT", "movedim"][int(rng.integers(0, 6))]
+        r = len(cur)
+        if kind == "permute":
+            p = tuple(int(i) for i in rng.permutation(r))
+            steps.append(lambda x, p=p: x.permute(*p))
+            cur = [cur[i] for i in p]
+        elif kind == "transpose" and r >= 2:
+            a, b = (int(i) for i in rng.choice(r, 2, replace=False))
+            steps.append(lambda x, a=a, b=b: x.transpose(a, b))
+            cur[a], cur[b] = cur[b], cur[a]
+        elif kind == "flatten" and r >= 3:
+            a = int(rng.integers(0, r - 1))
+            steps.append(lambda x, a=a: x.contiguous().flatten(a, a + 1))
+            cur = cur[:a] + [cur[a] * cur[a + 1]] + cur[a + 2:]
+        elif kind == "unsqueeze" and r < 5:
+            a = int(rng.integers(0, r + 1))
+            steps.append(lambda x, a=a: x.unsqueeze(a))
+            cur = cur[:a] + [1] + cur[a:]
+        elif kind == "mT" and r >= 2:
+            steps.append(lambda x: x.mT)
+            cur[-1], cur[-2] = cur[-2], cur[-1]
+        elif kind == "movedim" and r >= 2:
+            a, b = (int(i) for i in rng.choice(r, 2, replace=False))
+            steps.append(lambda x, a=a, b=b: x.movedim(a, b))
+            d = cur.pop(a)
+            cur.insert(b, d)
+    cast = [None, torch.float16, torch.bfloat16][int(rng.integers(0, 3))]
+    pad = rng.random() < 0.4
+
+    def body(x):
+        for f in steps:
+            x = f(x)
+        x = x.contiguous()
+        if cast is not None:
+            x = x.to(cast)
+        if pad:
+            x = F.pad(x, (0, 1))
+        return x
+
+    return body, shape
+
+
+@pytest.mark.parametrize("seed", range(40))
+def test_random_chains_import_to_their_eager_meaning(seed):
+    """Random chains of supported layout ops, casts and pads: the imported
+    recipe, executed by the reference runtime, equals the eager result."""
+    import torch
+
+    from sym_b200.reloc_torch.backend import RelocBackend
+    from sym_b200.reloc_torch.compiler import UnsupportedRecipe
+
+    body, shape = _random_chain(seed)
+    x = torch.randn(shape, generator=torch.Generator().manual_seed(seed))
+    ((gm, ex),) = _dynamo_graphs(lambda x: body(x).cuda(), x)
+    try:
+        got, _ = _reference_result(gm, ex, x, ())
+    except UnsupportedRecipe as error:
+        # a layout the plan format cannot state (e.g. merging axes a transpose
+        # made non-adjacent): the backend keeps the region's original ops
+        backend = RelocBackend()
+        assert not backend(gm, ex).regions
+        assert (error.reason if hasattr(error, "reason") else str(error)) in str(backend.stats()["exclusions"])
+        return
+    assert np.array_equal(got, _bits(body(x)))
