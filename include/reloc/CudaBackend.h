@@ -7,6 +7,8 @@
 #ifndef SYM_B200_RELOC_CUDABACKEND_H
 #define SYM_B200_RELOC_CUDABACKEND_H
 
+#include "reloc/Backend.h"
+
 #include <cstddef>
 #include <climits>
 #include <cstdint>
@@ -18,21 +20,54 @@
 
 namespace reloc {
 
-enum class QueueCompletion { Complete, Unknown };
+/// A context's fault word: one word of mapped pinned host memory that the
+/// kernels with bounded waits set to 2 when a wait runs out (sbc_relocate::
+/// fault). The host reads it with a plain load, no CUDA call, once the work
+/// that may have set it completed. Shared with pending completions, which
+/// read it after their event.
+struct FaultWord {
+  int32_t *host = nullptr;
+  int32_t *device = nullptr; // the same word's device address
+  FaultWord() = default;
+  FaultWord(const FaultWord &) = delete;
+  FaultWord &operator=(const FaultWord &) = delete;
+  ~FaultWord();
+  /// The word's value, then cleared (0: no wait ran out).
+  int32_t take();
+};
 
-class CudaBackend {
+/// One device's streams, HBM ring and parameter buffers behind the
+/// reference's CopyBackend interface (reference Backend.h:34-89). Queue 0 is
+/// the copy-engine stream, queue 1 the compute stream.
+class CudaBackend : public CopyBackend {
 public:
   /// Create a context on `device` (made current for the calling thread).
   static std::unique_ptr<CudaBackend> create(int device, std::string &error);
-  ~CudaBackend();
+  ~CudaBackend() override;
   CudaBackend(const CudaBackend &) = delete;
   CudaBackend &operator=(const CudaBackend &) = delete;
 
-  int device() const { return device_; }
-  bool failed() const { return failed_; }
-  const std::string &error() const { return error_; }
+  // ---- CopyBackend
+  void *allocStaging(size_t bytes) override;
+  void freeStaging(void *p) override;
+  int numQueues() const override { return 2; }
+  void copyAsync(int queue, void *dst, const void *src, size_t bytes, CopyDir dir) override;
+  EventHandle recordEvent(int queue) override;
+  void waitEvent(EventHandle ev) override;
+  bool queryEvent(EventHandle ev) override;
+  int device() const override { return device_; }
+  bool failed() const override { return failed_; }
+  const std::string &error() const override { return error_; }
   /// Record a failure (first one wins). Returns false for call chaining.
   bool fail(const std::string &what, int status);
+  /// Record a failure with a message of its own (first one wins).
+  bool failWith(const std::string &message);
+  /// Reads (and clears) the fault word: a wait that ran out in work that has
+  /// completed makes the context failed. Returns !failed().
+  bool healthy();
+  /// Device address of the fault word, for the descriptors of this context.
+  int32_t *faultWord() const { return fault_->device; }
+  const std::shared_ptr<FaultWord> &faultShared() const { return fault_; }
   /// Make this backend's device current on the calling thread.
   bool activate();
 
@@ -40,13 +75,14 @@ public:
   void *computeStream() const { return compute_; }
 
   /// Order both private streams after the work already on `external`.
-  bool waitStream(const void *external);
+  bool waitStream(const void *external) override;
   /// Record completion of everything enqueued so far on the private streams;
   /// with `hasExternal`, order `external` (a null handle = the legacy default
   /// stream) after it.
   bool signalStream(const void *external, bool hasExternal, bool copyUsed = true);
-  /// Block until all enqueued work completed.
-  QueueCompletion quiesce();
+  /// Block until all enqueued work completed (every queue is attempted
+  /// despite earlier failures); Unknown when a queue cannot be drained.
+  QueueCompletion quiesce() override;
 
   /// HBM ring of `slots` buffers of `slotBytes` (grown, never shrunk).
   bool ensureRing(int slots, size_t slotBytes);
@@ -92,8 +128,6 @@ public:
   uint64_t eventWaits = 0;
   uint64_t callerWaits = 0;
   uint64_t kernelLaunches = 0;
-  /// sbc_wait_launch_count() when this context last read the fault word.
-  uint64_t waitLaunchesChecked = 0;
   /// Set while a group runs: its members share one status word, cleared once
   /// before the first member instead of once per execution.
   bool keepStatus = false;
@@ -141,6 +175,11 @@ private:
   size_t paramBytes_ = 0;
   int32_t *status_ = nullptr;
   int32_t *statusHost_ = nullptr;
+  std::shared_ptr<FaultWord> fault_;
+  // CopyBackend events handed out by recordEvent (handle = index + 1) and
+  // staging blocks handed out by allocStaging.
+  std::vector<void *> events_;
+  std::vector<void *> stagingBlocks_;
 };
 
 } // namespace reloc

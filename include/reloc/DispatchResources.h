@@ -57,6 +57,7 @@ struct ResourceStats {
   size_t peakLiveBytes = 0; // sum over contexts of each one's peak scratch
   uint64_t releases = 0;    // scratch releases at lease end (over the retained quota)
   uint64_t evictions = 0;   // contexts retired to admit one for another device
+  uint64_t retirements = 0; // contexts retired after a failed execution (completion proven)
 };
 
 class Resources {
@@ -95,6 +96,10 @@ public:
   std::optional<TransferError> clear();
   std::optional<TransferError> close();
 
+  /// Keep `anything` (a context, buffer owners) alive until the process
+  /// exits: work that may still touch it has no proven completion.
+  static void quarantine(std::shared_ptr<void> anything);
+
 private:
   struct Slot {
     std::unique_ptr<CudaBackend> backend;
@@ -111,8 +116,7 @@ private:
   size_t maxRetained_, maxLive_;
   unsigned maxContexts_;
   bool closed_ = false, quarantined_ = false;
-  uint64_t requests_ = 0, hits_ = 0, created_ = 0;
-  std::vector<std::shared_ptr<void>> quarantinedOwners_;
+  uint64_t requests_ = 0, hits_ = 0, created_ = 0, retired_ = 0;
 };
 
 } // namespace dispatch

@@ -98,6 +98,11 @@ typedef struct {
    * outside its parameter table; such elements are skipped, never read past
    * the table. The runtime reports it as channel_out_of_range. */
   int32_t *status;
+  /* Word (or NULL) that a kernel with bounded waits sets to 2 when a wait
+   * runs out (a TMA copy it waited for never landed; the kernel left early
+   * and its output is incomplete). Device memory or mapped pinned host
+   * memory; the caller clears it and reads it after the launch completed. */
+  int32_t *fault;
   int64_t src_offset;
   int64_t dst_offset;
   int32_t result_rank;
@@ -132,12 +137,35 @@ int sbc_fill(void *dst, int64_t count, int32_t width, uint64_t bits, void *strea
 /* Kernels launched by this library since load (instrumentation). */
 uint64_t sbc_launch_count(void);
 /* Launches since load of kernels with bounded waits, the only kernels that
- * set the fault word: while it has not moved, the fault word is clear. */
+ * write a descriptor's `fault` word: while it has not moved, no fault word
+ * can have been set. */
 uint64_t sbc_wait_launch_count(void);
-/* The current device's kernel fault word, then cleared: 0 none, 2 a TMA copy
- * a kernel waited for did not land within the wait limit (the kernel left
- * early; its output is incomplete). Synchronizes with the device. */
-int sbc_device_fault(int *code);
+/* Time limit of every bounded wait inside the kernels launched from now on
+ * (nanoseconds of the GPU's global timer; 0 restores the default, one
+ * second). */
+void sbc_set_wait_limit_ns(uint64_t ns);
+
+/* ---- test hooks (never armed by the library itself) ---------------------
+ * Failure injection for the tests of the error paths; neither hook faults,
+ * traps or hangs a GPU.
+ *
+ * sbc_test_fault_mode: make this layer's CUDA calls report cudaErrorUnknown
+ * on the host without issuing them (the work already queued still runs):
+ *   0 off;
+ *   1 every event record fails;
+ *   2 event records and stream synchronizations fail (completion unknown);
+ *   3 the third host-to-device copy after arming fails;
+ *   4 as 3, and stream synchronizations fail (completion unknown);
+ *   5 event synchronizations fail;
+ *   6 event and stream synchronizations fail (completion unknown).
+ *
+ * sbc_test_withhold_tile: the next TMA tile launch (any device) issues no
+ * copy and no arrival for its job `job`, so the warps that wait for that
+ * tile run out of their bounded wait after `wait_limit_ns` (0: the current
+ * limit), set the descriptor's fault word and leave; the launch after it is
+ * normal again. job = UINT32_MAX disarms. */
+int sbc_test_fault_mode(int mode);
+void sbc_test_withhold_tile(uint32_t job, uint64_t wait_limit_ns);
 
 /* ---- devices, memory and copies */
 int sbc_device_count(int *count);

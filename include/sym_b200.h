@@ -169,11 +169,17 @@ int sb_ipc_close(void *device_ptr, sb_error *err);
  * the legacy default stream) with no copy/compute overlap. Plans whose
  * parameters exceed 1 MiB, or whose single source row (or whole source, when
  * rows cannot be split) exceeds the staging slot, are rejected with
- * invalid_options. The first call on a device resolves the array's device
+ * invalid_options. The scratch is the current device's: `destination` must
+ * be memory of the current device (device_mismatch otherwise), and `stream`
+ * a stream of it. The first call on a device resolves the array's device
  * address (cudaGetSymbolAddress) with that device current: make that first
  * call outside any stream capture. All calls share the array, so calls that
- * overlap on the GPU (other streams, other threads) race; plans whose channel
- * map is checked on the device synchronize `stream` before returning. */
+ * overlap on the GPU (other streams, other threads) race. Calls whose plan
+ * checks its channel map on the device, or that ran a kernel with bounded
+ * waits (the TMA tile transposes), synchronize `stream` before returning and
+ * report a wait that ran out as backend_failure; otherwise the call returns
+ * with the copies still queued on `stream`, and `source` must stay valid and
+ * unchanged until `stream` has passed them. */
 int sb_execute_h2d_static(const sb_template *tmpl, const void *source, void *destination, void *stream,
                           sb_error *err);
 

@@ -118,6 +118,30 @@ def lib():
     return L
 
 
+_cuda = None
+
+
+def cuda_layer():
+    """The thin CUDA layer (libsb_cuda.so, include/sb_cuda.h), loaded by the
+    runtime library; for its wait-limit setting and the test hooks that
+    inject failures (``sbc_test_fault_mode``, ``sbc_test_withhold_tile``)."""
+    global _cuda
+    if _cuda is not None:
+        return _cuda
+    lib()
+    L = ctypes.CDLL(str(CUDA_LIB))
+    L.sbc_test_fault_mode.restype = ctypes.c_int
+    L.sbc_test_fault_mode.argtypes = [ctypes.c_int]
+    L.sbc_test_withhold_tile.restype = None
+    L.sbc_test_withhold_tile.argtypes = [ctypes.c_uint32, ctypes.c_uint64]
+    L.sbc_set_wait_limit_ns.restype = None
+    L.sbc_set_wait_limit_ns.argtypes = [ctypes.c_uint64]
+    L.sbc_wait_launch_count.restype = ctypes.c_uint64
+    L.sbc_wait_launch_count.argtypes = []
+    _cuda = L
+    return L
+
+
 def error_of(err: SbError):
     return err.code.decode(), err.message.decode(), err.offset
 

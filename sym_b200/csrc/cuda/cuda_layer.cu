@@ -8,11 +8,33 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <cstring>
 
 namespace {
 cudaStream_t S(void *s) { return static_cast<cudaStream_t>(s); }
 cudaEvent_t E(void *e) { return static_cast<cudaEvent_t>(e); }
+
+// Test-only failure injection (sbc_test_fault_mode): the wrapped call reports
+// cudaErrorUnknown without being issued. Off unless a test arms it.
+std::atomic<int> g_fault_mode{0};
+std::atomic<int> g_fault_copies{0};
+bool inject_event_record() {
+  const int m = g_fault_mode.load(std::memory_order_relaxed);
+  return m == 1 || m == 2;
+}
+bool inject_stream_sync() {
+  const int m = g_fault_mode.load(std::memory_order_relaxed);
+  return m == 2 || m == 4 || m == 6;
+}
+bool inject_event_sync() {
+  const int m = g_fault_mode.load(std::memory_order_relaxed);
+  return m == 5 || m == 6;
+}
+bool inject_h2d_copy() {
+  const int m = g_fault_mode.load(std::memory_order_relaxed);
+  return (m == 3 || m == 4) && g_fault_copies.fetch_add(1) + 1 == 3;
+}
 } // namespace
 
 extern "C" {
@@ -120,6 +142,8 @@ int sbc_pointer_info(const void *ptr, int *kind, int *device) {
 }
 
 int sbc_memcpy_h2d_async(void *dst, const void *src, size_t bytes, void *stream) {
+  if (inject_h2d_copy())
+    return cudaErrorUnknown;
   return cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, S(stream));
 }
 int sbc_memcpy_d2h_async(void *dst, const void *src, size_t bytes, void *stream) {
@@ -140,7 +164,11 @@ int sbc_stream_create(void **stream) {
   return e;
 }
 int sbc_stream_destroy(void *stream) { return cudaStreamDestroy(S(stream)); }
-int sbc_stream_synchronize(void *stream) { return cudaStreamSynchronize(S(stream)); }
+int sbc_stream_synchronize(void *stream) {
+  if (inject_stream_sync())
+    return cudaErrorUnknown;
+  return cudaStreamSynchronize(S(stream));
+}
 
 int sbc_event_create(void **event, int timing) {
   cudaEvent_t ev = nullptr;
@@ -149,7 +177,11 @@ int sbc_event_create(void **event, int timing) {
   return e;
 }
 int sbc_event_destroy(void *event) { return cudaEventDestroy(E(event)); }
-int sbc_event_record(void *event, void *stream) { return cudaEventRecord(E(event), S(stream)); }
+int sbc_event_record(void *event, void *stream) {
+  if (inject_event_record())
+    return cudaErrorUnknown;
+  return cudaEventRecord(E(event), S(stream));
+}
 int sbc_event_query(void *event) {
   cudaError_t e = cudaEventQuery(E(event));
   if (e == cudaErrorNotReady) {
@@ -157,9 +189,21 @@ int sbc_event_query(void *event) {
   }
   return e;
 }
-int sbc_event_synchronize(void *event) { return cudaEventSynchronize(E(event)); }
+int sbc_event_synchronize(void *event) {
+  if (inject_event_sync())
+    return cudaErrorUnknown;
+  return cudaEventSynchronize(E(event));
+}
 int sbc_stream_wait_event(void *stream, void *event) { return cudaStreamWaitEvent(S(stream), E(event), 0); }
 int sbc_event_elapsed_ms(void *start, void *stop, float *ms) { return cudaEventElapsedTime(ms, E(start), E(stop)); }
+
+int sbc_test_fault_mode(int mode) {
+  if (mode < 0 || mode > 6)
+    return SBC_EINVAL;
+  g_fault_copies.store(0);
+  g_fault_mode.store(mode);
+  return 0;
+}
 
 const char *sbc_error_string(int status) {
   if (status == SBC_EINVAL)

@@ -28,9 +28,15 @@
 namespace {
 
 std::atomic<uint64_t> g_launches{0};
-// Launches of kernels with bounded waits (the only writers of the device
-// fault word): callers read the fault word only after one of these ran.
+// Launches of kernels with bounded waits (the only writers of a descriptor's
+// fault word): callers read their fault word only after one of these ran.
 std::atomic<uint64_t> g_wait_launches{0};
+// Time limit of each bounded wait (sbc_set_wait_limit_ns) and the test
+// hook's withheld job with its own limit (sbc_test_withhold_tile).
+constexpr uint64_t kDefaultWaitLimitNs = 1000000000ull; // one second
+std::atomic<uint64_t> g_wait_ns{kDefaultWaitLimitNs};
+std::atomic<uint32_t> g_withhold_job{UINT32_MAX};
+std::atomic<uint64_t> g_withhold_ns{0};
 
 // ---------------------------------------------------------------------------
 // Scalar stage arithmetic
@@ -1198,22 +1204,26 @@ __global__ void __launch_bounds__(256, 4) k_tile_s8(const __grid_constant__ sbc_
 // `full` mbarrier (32 producer arrivals + the tile's byte count) and an
 // `empty` mbarrier (one arrival per consumer warp). Per tile it waits for the
 // stage to be empty, lane 0 arms `full` with the byte count and issues
-// cp.async.bulk.tensor (no multicast, local memory only), then the lanes stage
+// cp.async.bulk.tensor (plain tiled loads, no multicast; the source is this
+// GPU's memory or, in the multi-GPU fetch, a peer's shard), then the lanes stage
 // the tile's 64 per-column scales and biases next to it and arrive. Consumer
 // warps wait on `full`, read the tile and its parameters into registers,
 // release the stage and convert; there is no CTA-wide barrier in the loop, so
 // warps drift up to KStages tiles apart instead of meeting every tile.
 // Conversion and the 16-byte streaming stores are those of k_tile_s8.
 //
-// Every wait is bounded (kWaitLimit polls). A thread whose wait runs out sets
-// the status word and the device fault word to 2 and leaves; thread 0 (or the
-// producer) first waits, again bounded, for the copies that may still be in
-// flight into this CTA's shared memory.
+// Every wait is bounded in time (TmaCtl::wait_ns of the global timer). A
+// thread whose wait runs out sets the descriptor's fault word to 2 and leaves;
+// thread 0 (or the producer) first waits, again bounded, for the copies that
+// may still be in flight into this CTA's shared memory.
 // ---------------------------------------------------------------------------
 
-/// Set by a kernel whose bounded wait ran out (2 = TMA copy never landed);
-/// read and cleared by sbc_device_fault.
-__device__ int g_device_fault = 0;
+/// Per-launch controls of k_tma_tile: the time limit of each bounded wait and
+/// the test hook's withheld job (UINT32_MAX: none; see sbc_test_withhold_tile).
+struct TmaCtl {
+  uint64_t wait_ns;
+  uint32_t withhold_job;
+};
 
 // Ring depth and resident CTAs per SM of k_tma_tile (compile-time tuning
 // points). Measured on the gate matrix (TB/s): 6 x 3 CTAs 5.00-5.03,
@@ -1229,7 +1239,6 @@ constexpr int KStages = SBC_TMA_STAGES;
 constexpr int KTmaTileBytes = 64 * 128;
 constexpr int KTmaConsumers = 256;              // warps 0-7
 constexpr int KTmaThreads = KTmaConsumers + 32; // + the producer warp
-constexpr uint32_t kWaitLimit = 1u << 24;
 
 __device__ __forceinline__ uint32_t smem_addr(const void *p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -1269,20 +1278,35 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
 
-/// Bounded wait for `parity`; true when the phase completed.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ bool mbar_try(uint32_t a, uint32_t parity) {
+  uint32_t done;
+  asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+               " selp.u32 %0, 1, 0, p;\n}"
+               : "=r"(done)
+               : "r"(a), "r"(parity)
+               : "memory");
+  return done != 0;
+}
+
+/// Wait for `parity` for at most `limit_ns` of the global timer (read only
+/// once the first poll failed); true when the phase completed.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint64_t limit_ns) {
   const uint32_t a = smem_addr(bar);
-  for (uint32_t i = 0; i < kWaitLimit; ++i) {
-    uint32_t done;
-    asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
-                 " selp.u32 %0, 1, 0, p;\n}"
-                 : "=r"(done)
-                 : "r"(a), "r"(parity)
-                 : "memory");
-    if (done)
+  if (mbar_try(a, parity))
+    return true;
+  const uint64_t t0 = global_ns();
+  for (;;) {
+    if (mbar_try(a, parity))
       return true;
+    if (global_ns() - t0 > limit_ns)
+      return false;
   }
-  return false;
 }
 
 __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, int32_t x, int32_t y, int32_t z,
@@ -1311,7 +1335,7 @@ struct TmaSources {
 template <int WS, int CHAIN, int CH_ON>
 __global__ void __launch_bounds__(KTmaThreads, SBC_TMA_CTAS_PER_SM) k_tma_tile(const __grid_constant__ TmaSources srcs,
                                                              const __grid_constant__ sbc_relocate d, TileOrder ord,
-                                                             uint32_t tiles) {
+                                                             uint32_t tiles, TmaCtl ctl) {
   constexpr int TB = 64, VD = 8;
   constexpr int TA = 128 / WS;                     // A cells per tile
   constexpr int WD = CHAIN == CH_COPY ? WS : 2;    // result bytes per cell
@@ -1343,17 +1367,18 @@ __global__ void __launch_bounds__(KTmaThreads, SBC_TMA_CTAS_PER_SM) k_tma_tile(c
     timed_out = 0;
   }
   __syncthreads(); // the only CTA-wide barrier
+  // The fault word may be mapped host memory: a plain store made visible
+  // system-wide (only the value 2 is ever written, so no atomic is needed).
   auto fail = [&]() {
-    if (atomicExch(&timed_out, 1) == 0) {
-      if (d.status)
-        atomicExch(d.status, 2);
-      atomicExch(&g_device_fault, 2);
+    if (atomicExch(&timed_out, 1) == 0 && d.fault) {
+      *reinterpret_cast<volatile int32_t *>(d.fault) = 2;
+      __threadfence_system();
     }
   };
   // Bounded wait for the copies of local tiles [lo, hi) (issued, maybe in flight).
   auto drain = [&](uint32_t lo, uint32_t hi) {
     for (uint32_t q = lo; q < hi && blockIdx.x + q * G < tiles; ++q)
-      mbar_wait(&full[q % KStages], (q / KStages) & 1);
+      mbar_wait(&full[q % KStages], (q / KStages) & 1, ctl.wait_ns);
   };
 
   if (t >= KTmaConsumers) { // ---- producer warp
@@ -1390,7 +1415,7 @@ __global__ void __launch_bounds__(KTmaThreads, SBC_TMA_CTAS_PER_SM) k_tma_tile(c
       if (job >= tiles)
         break;
       const int st = k % KStages;
-      if (k >= KStages && !mbar_wait(&empty[st], (k / KStages - 1) & 1)) {
+      if (k >= KStages && !mbar_wait(&empty[st], (k / KStages - 1) & 1, ctl.wait_ns)) {
         fail();
         if (lane == 0)
           drain(k - KStages, k);
@@ -1408,7 +1433,10 @@ __global__ void __launch_bounds__(KTmaThreads, SBC_TMA_CTAS_PER_SM) k_tma_tile(c
         if (lane == 0)
           s_bad[st] = bad;
       }
-      if (lane == 0) {
+      if (job == ctl.withhold_job) {
+        // test hook: neither the copy nor any arrival, so this tile's
+        // consumers run out of their bounded wait
+      } else if (lane == 0) {
         uint32_t ta, tb;
         tile_of(job, ord, ta, tb);
         int j = 0; // the source holding b-tile tb
@@ -1442,7 +1470,7 @@ __global__ void __launch_bounds__(KTmaThreads, SBC_TMA_CTAS_PER_SM) k_tma_tile(c
     if (job >= tiles)
       break;
     const int st = k % KStages;
-    if (!mbar_wait(&full[st], (k / KStages) & 1)) {
+    if (!mbar_wait(&full[st], (k / KStages) & 1, ctl.wait_ns)) {
       fail();
       if (t == 0) // the producer cannot pass tile k + KStages - 1 before this warp releases tile k
         drain(k, k + KStages);
@@ -2004,10 +2032,18 @@ int launch_tma(const sbc_relocate &d, int chain, int ch_on, const void *const *b
   ord.group = make_fastdiv(static_cast<uint32_t>(tiles_b << ord.lg));
   const size_t smem = KStages * KTmaTileBytes + 1024;
   const uint32_t nt = static_cast<uint32_t>(tiles);
+  TmaCtl ctl;
+  ctl.wait_ns = g_wait_ns.load(std::memory_order_relaxed);
+  ctl.withhold_job = g_withhold_job.exchange(UINT32_MAX); // a test hook arms one launch
+  if (ctl.withhold_job != UINT32_MAX) {
+    const uint64_t ns = g_withhold_ns.load();
+    if (ns)
+      ctl.wait_ns = ns;
+  }
 #define SBC_TMA(WS_, CH_, ON_)                                                                                 \
   (cudaFuncSetAttribute(k_tma_tile<WS_, CH_, ON_>, cudaFuncAttributeMaxDynamicSharedMemorySize,                    \
                         static_cast<int>(smem)),                                                                 \
-   k_tma_tile<WS_, CH_, ON_><<<blocks, KTmaThreads, smem, st>>>(srcs, d, ord, nt))
+   k_tma_tile<WS_, CH_, ON_><<<blocks, KTmaThreads, smem, st>>>(srcs, d, ord, nt, ctl))
   if (tma_32)
     chain == CH_COPY ? SBC_TMA(4, CH_COPY, 0) : chain == CH_F16 ? SBC_TMA(4, CH_F16, 0) : SBC_TMA(4, CH_BF16, 0);
   else if (chain == CH_DQ_F16)
@@ -2283,12 +2319,11 @@ uint64_t sbc_launch_count(void) { return g_launches.load(); }
 
 uint64_t sbc_wait_launch_count(void) { return g_wait_launches.load(); }
 
-int sbc_device_fault(int *code) {
-  int zero = 0;
-  cudaError_t e = cudaMemcpyFromSymbol(code, g_device_fault, sizeof(int));
-  if (e == cudaSuccess && *code)
-    e = cudaMemcpyToSymbol(g_device_fault, &zero, sizeof(int));
-  return e;
+void sbc_set_wait_limit_ns(uint64_t ns) { g_wait_ns.store(ns ? ns : kDefaultWaitLimitNs); }
+
+void sbc_test_withhold_tile(uint32_t job, uint64_t wait_limit_ns) {
+  g_withhold_ns.store(wait_limit_ns);
+  g_withhold_job.store(job);
 }
 
 } // extern "C"

@@ -637,6 +637,12 @@ int sb_execute_h2d_static(const sb_template *t, const void *source, void *destin
     return setErr(err, "implementation_unavailable", "template has no lowered program");
   if (!source || !destination)
     return setErr(err, "invalid_view", "source and destination must be non-null");
+  // The scratch used is the current device's: the destination must live there.
+  int current = -1, kind = 0, owner = -1;
+  if (sbc_get_device(&current) == 0 && sbc_pointer_info(destination, &kind, &owner) == 0 && kind == 2 &&
+      owner != current)
+    return setErr(err, "device_mismatch", "the destination lives on cuda:" + std::to_string(owner) +
+                                              ", the current device is cuda:" + std::to_string(current));
   void *scratch = nullptr;
   size_t bytes = 0;
   const int rc = sbc_static_scratch(&scratch, &bytes);
@@ -667,7 +673,8 @@ int sb_resources_stats(const sb_resources *r, char *json, size_t cap) {
      << ",\"closed\":" << (s.closed ? "true" : "false") << ",\"quarantined\":" << (s.quarantined ? "true" : "false")
      << ",\"retained_limit\":" << s.retainedLimit << ",\"live_limit\":" << s.liveLimit
      << ",\"context_limit\":" << s.contextLimit << ",\"peak_live_bytes\":" << s.peakLiveBytes
-     << ",\"releases\":" << s.releases << ",\"evictions\":" << s.evictions << "}";
+     << ",\"releases\":" << s.releases << ",\"evictions\":" << s.evictions
+     << ",\"retirements\":" << s.retirements << "}";
   return putJson(os.str(), json, cap);
 }
 

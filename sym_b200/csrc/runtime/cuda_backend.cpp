@@ -154,6 +154,111 @@ bool CudaBackend::fail(const std::string &what, int status) {
   return false;
 }
 
+bool CudaBackend::failWith(const std::string &message) {
+  if (!failed_) {
+    failed_ = true;
+    error_ = message;
+  }
+  return false;
+}
+
+FaultWord::~FaultWord() {
+  if (host)
+    sbc_free_host(host);
+}
+
+int32_t FaultWord::take() {
+  auto *w = reinterpret_cast<volatile int32_t *>(host);
+  const int32_t v = *w;
+  if (v)
+    *w = 0;
+  return v;
+}
+
+bool CudaBackend::healthy() {
+  if (fault_ && fault_->take())
+    failWith("a kernel's bounded wait for a TMA copy ran out; the output is incomplete");
+  return !failed_;
+}
+
+// ---- CopyBackend ------------------------------------------------------------
+
+void *CudaBackend::allocStaging(size_t bytes) {
+  void *p = nullptr;
+  const int rc = sbc_malloc_host(&p, bytes ? bytes : 1, 0);
+  if (rc) {
+    fail("cudaHostAlloc(staging)", rc);
+    return nullptr;
+  }
+  stagingBlocks_.push_back(p);
+  return p;
+}
+
+void CudaBackend::freeStaging(void *p) {
+  auto it = std::find(stagingBlocks_.begin(), stagingBlocks_.end(), p);
+  if (it == stagingBlocks_.end())
+    return;
+  stagingBlocks_.erase(it);
+  const int rc = sbc_free_host(p);
+  if (rc)
+    fail("cudaFreeHost(staging)", rc);
+}
+
+void CudaBackend::copyAsync(int queue, void *dst, const void *src, size_t bytes, CopyDir dir) {
+  if (failed_)
+    return;
+  void *s = queue == 1 ? compute_ : copy_;
+  const int rc = dir == CopyDir::HostToDevice ? sbc_memcpy_h2d_async(dst, src, bytes, s)
+                                              : sbc_memcpy_d2h_async(dst, src, bytes, s);
+  if (rc)
+    fail("cudaMemcpyAsync", rc);
+  else
+    ++copyCalls;
+}
+
+EventHandle CudaBackend::recordEvent(int queue) {
+  if (failed_)
+    return 0;
+  void *e = nullptr;
+  int rc = sbc_event_create(&e, 0);
+  if (rc) {
+    fail("cudaEventCreate", rc);
+    return 0;
+  }
+  if ((rc = sbc_event_record(e, queue == 1 ? compute_ : copy_))) {
+    sbc_event_destroy(e);
+    fail("cudaEventRecord", rc);
+    return 0;
+  }
+  ++eventRecords;
+  events_.push_back(e);
+  return static_cast<EventHandle>(events_.size());
+}
+
+void CudaBackend::waitEvent(EventHandle ev) {
+  if (ev == 0 || ev > events_.size() || !events_[ev - 1])
+    return;
+  void *&e = events_[ev - 1];
+  const int rc = sbc_event_synchronize(e);
+  if (rc) {
+    fail("cudaEventSynchronize", rc);
+    return;
+  }
+  sbc_event_destroy(e);
+  e = nullptr;
+}
+
+bool CudaBackend::queryEvent(EventHandle ev) {
+  if (ev == 0 || ev > events_.size() || !events_[ev - 1])
+    return true;
+  const int rc = sbc_event_query(events_[ev - 1]);
+  if (rc == 1)
+    return false;
+  if (rc)
+    fail("cudaEventQuery", rc);
+  return true;
+}
+
 bool CudaBackend::activate() {
   const int rc = sbc_set_device(device_);
   return rc == 0 || fail("cudaSetDevice", rc);
@@ -177,6 +282,22 @@ std::unique_ptr<CudaBackend> CudaBackend::create(int device, std::string &error)
     return nullptr;
   }
   b->statusHost_ = static_cast<int32_t *>(host);
+  // The fault word: mapped pinned memory the kernels write and the host reads
+  // without a CUDA call.
+  auto fw = std::make_shared<FaultWord>();
+  void *word = nullptr, *dev = nullptr;
+  if ((rc = sbc_malloc_host(&word, 64, 1))) {
+    error = std::string("context creation (fault word): ") + sbc_error_string(rc);
+    return nullptr;
+  }
+  fw->host = static_cast<int32_t *>(word);
+  *fw->host = 0;
+  if ((rc = sbc_host_device_pointer(word, &dev))) {
+    error = std::string("context creation (fault word mapping): ") + sbc_error_string(rc);
+    return nullptr;
+  }
+  fw->device = static_cast<int32_t *>(dev);
+  b->fault_ = std::move(fw);
   return b;
 }
 
@@ -210,6 +331,11 @@ CudaBackend::~CudaBackend() {
   for (void *e : {done_, fence_, start_, stop_, stagingReady_, stagingFree_})
     if (e)
       sbc_event_destroy(e);
+  for (void *e : events_)
+    if (e)
+      sbc_event_destroy(e);
+  for (void *p : stagingBlocks_)
+    sbc_free_host(p);
   if (copy_)
     sbc_stream_destroy(copy_);
   if (compute_)

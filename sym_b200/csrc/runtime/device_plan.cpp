@@ -335,9 +335,12 @@ std::optional<TransferError> uploadParams(const Lowered &l, CudaBackend &b, sbc_
 
 namespace {
 
-/// Launch the family kernel for `d` on the compute stream.
+/// Launch the family kernel for `d` on the compute stream, with this
+/// context's fault word.
 std::optional<TransferError> launch(const Lowered &l, CudaBackend &b, const sbc_relocate &d, RunStats &st) {
-  const int rc = launchFamily(l.family, d, b.computeStream());
+  sbc_relocate e = d;
+  e.fault = b.faultWord();
+  const int rc = launchFamily(l.family, e, b.computeStream());
   if (rc) {
     b.fail("relocation kernel", rc);
     return terr("backend_failure", b.error());
@@ -576,6 +579,7 @@ std::optional<TransferError> runSourceShards(const Lowered &l, CudaBackend &b, c
     if (auto e = zeroStatus(l, b, d))
       return e;
     d.dst = ddst;
+    d.fault = b.faultWord();
     const int rc = sbc_relocate_transpose_shards(&d, srcs.data(), rb.data(), static_cast<int32_t>(srcs.size()),
                                                  b.computeStream());
     if (rc == 0) {
@@ -821,8 +825,8 @@ std::optional<TransferError> runH2D(const Lowered &l, CudaBackend &b, const void
 
 std::optional<TransferError> runH2DStatic(const Lowered &l, const void *hsrc, void *ddst, void *stream,
                                           uint8_t *scratch, size_t scratchBytes) {
-  // Scratch layout: [0, 256) status word | [256, 256 + kParams) parameters |
-  // the rest one staging slot for source rows.
+  // Scratch layout: [0, 4) status word, [4, 8) fault word (in [0, 256)) |
+  // [256, 256 + kParams) parameters | the rest one staging slot for source rows.
   constexpr size_t kStatus = 256, kParams = size_t(1) << 20;
   if (l.paramBlob.size() > kParams)
     return terr("invalid_options", "parameters exceed the static scratch's 1 MiB parameter area (" +
@@ -842,12 +846,14 @@ std::optional<TransferError> runH2DStatic(const Lowered &l, const void *hsrc, vo
         base.stages[k].zero_point = reinterpret_cast<const int32_t *>(pdev + l.zpOffset[static_cast<size_t>(k)]);
     }
   }
-  // The scratch keeps the previous call's contents: the status word must start at 0.
-  if (l.needsStatus) {
+  // The scratch keeps the previous call's contents: the status and fault words
+  // must start at 0 (one 8-byte fill covers both).
+  if (l.needsStatus)
     base.status = reinterpret_cast<int32_t *>(scratch);
-    if ((rc = sbc_fill(scratch, 1, 4, 0, stream)))
-      return terr("backend_failure", std::string("status reset: ") + sbc_error_string(rc));
-  }
+  base.fault = reinterpret_cast<int32_t *>(scratch + 4);
+  if ((rc = sbc_fill(scratch, 2, 4, 0, stream)))
+    return terr("backend_failure", std::string("status reset: ") + sbc_error_string(rc));
+  const uint64_t waits0 = sbc_wait_launch_count();
   if (l.desc.has_fill && !l.denseCover &&
       (rc = sbc_fill(ddst, l.dstElements, l.desc.dst_width, l.desc.fill_bits, stream)))
     return terr("backend_failure", std::string("fill kernel: ") + sbc_error_string(rc));
@@ -894,11 +900,17 @@ std::optional<TransferError> runH2DStatic(const Lowered &l, const void *hsrc, vo
         return terr("backend_failure", std::string("relocation kernel: ") + sbc_error_string(rc));
     }
   }
-  if (l.needsStatus) {
-    int32_t status = 0;
-    if ((rc = sbc_memcpy_d2h_async(&status, scratch, 4, stream)) || (rc = sbc_stream_synchronize(stream)))
+  // A kernel with bounded waits ran (this call's, or another thread's at the
+  // same time: then the read is only unneeded): wait for the stream and read
+  // the fault word with the status word.
+  const bool waited = sbc_wait_launch_count() != waits0;
+  if (l.needsStatus || waited) {
+    int32_t words[2] = {0, 0};
+    if ((rc = sbc_memcpy_d2h_async(words, scratch, sizeof(words), stream)) || (rc = sbc_stream_synchronize(stream)))
       return terr("backend_failure", std::string("status readback: ") + sbc_error_string(rc));
-    if (status)
+    if (words[1])
+      return terr("backend_failure", "a kernel's bounded wait for a TMA copy ran out; the output is incomplete");
+    if (words[0])
       return terr("channel_out_of_range", "a channel index fell outside its parameter table");
   }
   return std::nullopt;

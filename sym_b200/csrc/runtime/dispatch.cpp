@@ -200,8 +200,11 @@ Route routeOf(const Implementation &row, const TransferOptions &o) {
 
 /// Shared tail of an execution: signal the caller stream, record
 /// `completionEvent`, then (blocking, or when a status word or a route timing
-/// must be read) wait, check the device fault word and the status word, and
-/// learn the route timing.
+/// must be read) wait, check the context's fault word and the status word,
+/// and learn the route timing. An asynchronous execution returns once
+/// enqueued; the fault word then still reports any earlier execution of this
+/// context whose kernels have finished (the word is host memory: reading it
+/// costs no CUDA call), and a later call or the completion reports this one.
 std::optional<TransferError> finish(bool needsStatus, const std::string &classKey, CudaBackend &b,
                                     const TransferOptions &o, bool timed, Route route, int64_t bytes,
                                     void *completionEvent = nullptr, bool copyUsed = true) {
@@ -215,25 +218,17 @@ std::optional<TransferError> finish(bool needsStatus, const std::string &classKe
     }
     ++b.eventRecords;
   }
-  if (o.asyncCompletion && !needsStatus && !timed)
+  if (o.asyncCompletion && !needsStatus && !timed) {
+    if (!completionEvent && !b.healthy())
+      return terr("backend_failure", b.error());
     return std::nullopt;
+  }
   if ((rc = sbc_event_synchronize(b.doneEvent()))) {
     b.fail("completion", rc);
     return terr("backend_failure", b.error());
   }
-  // The fault word is written only by kernels with bounded waits; reading it
-  // synchronizes with the device, so skip it while none has launched.
-  const uint64_t waits = sbc_wait_launch_count();
-  if (waits != b.waitLaunchesChecked) {
-    int fault = 0;
-    if ((rc = sbc_device_fault(&fault))) {
-      b.fail("fault word", rc);
-      return terr("backend_failure", b.error());
-    }
-    b.waitLaunchesChecked = waits;
-    if (fault)
-      return terr("backend_failure", "a kernel's bounded wait for a TMA copy ran out; the output is incomplete");
-  }
+  if (!completionEvent && !b.healthy())
+    return terr("backend_failure", b.error());
   if (timed) {
     float ms = 0;
     if (sbc_event_elapsed_ms(b.startEvent(), b.stopEvent(), &ms) == 0 && bytes > 0) {
@@ -310,7 +305,7 @@ std::optional<TransferError> executeDispatch(DispatchRequest &req, CudaBackend &
   if (executionDevice(req) != b.device())
     return terr("device_mismatch", "the device end lives on cuda:" + std::to_string(executionDevice(req)) +
                                        ", the context on cuda:" + std::to_string(b.device()));
-  if (b.failed())
+  if (!b.healthy())
     return terr("backend_failure", b.error());
   if (!b.activate())
     return terr("backend_failure", b.error());
@@ -347,7 +342,7 @@ std::optional<TransferError> executeSourceRows(const DispatchTemplate &t, CudaBa
                                                Report &rep) {
   if (!t.lowered)
     return terr("implementation_unavailable", "template has no lowered program");
-  if (b.failed())
+  if (!b.healthy())
     return terr("backend_failure", b.error());
   if (!b.activate())
     return terr("backend_failure", b.error());
@@ -371,7 +366,7 @@ std::optional<TransferError> executeSourceShards(const DispatchTemplate &t, Cuda
                                                  const TransferOptions &o, Report &rep) {
   if (!t.lowered)
     return terr("implementation_unavailable", "template has no lowered program");
-  if (b.failed())
+  if (!b.healthy())
     return terr("backend_failure", b.error());
   if (!b.activate())
     return terr("backend_failure", b.error());
@@ -447,7 +442,7 @@ std::optional<TransferError> executeGroup(GroupRequest &g, CudaBackend &b, const
   for (const DispatchRequest &r : g.items)
     if (r.consumed || !r.lowered)
       return terr("already_executed", "a group member was already executed");
-  if (b.failed())
+  if (!b.healthy())
     return terr("backend_failure", b.error());
   if (!b.activate())
     return terr("backend_failure", b.error());
@@ -500,7 +495,7 @@ std::optional<TransferError> executeWindow(const DispatchTemplate &t, CudaBacken
                                            Report &rep) {
   if (!t.lowered)
     return terr("implementation_unavailable", "template has no lowered program");
-  if (b.failed())
+  if (!b.healthy())
     return terr("backend_failure", b.error());
   if (!b.activate())
     return terr("backend_failure", b.error());

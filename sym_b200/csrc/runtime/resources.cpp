@@ -96,24 +96,44 @@ TransferOutcome Resources::withContext(int device,
   if (releaseAfter && !slot->backend->failed())
     slot->backend->trim(slot->backend->retainedLimit);
   if (out.error && slot->backend->failed()) {
-    // A failed CUDA call leaves completion unknown: retire the context.
-    if (slot->backend->quiesce() != QueueCompletion::Complete) {
+    // A failed backend call: completion must be proven before anything the
+    // work touched may be reused. Proven: the context is retired (freed once
+    // this lease ends) and the next call gets a fresh one. Not proven: the
+    // context and the owners stay alive for the life of the process and the
+    // owner refuses all further work.
+    const bool known = slot->backend->quiesce() == QueueCompletion::Complete;
+    std::lock_guard<std::mutex> g(mutex_);
+    auto it = slots_.find(device);
+    if (it != slots_.end() && it->second == slot)
+      slots_.erase(it);
+    if (known) {
+      ++retired_;
+    } else {
       out.completion = TransferCompletion::Unknown;
-      std::lock_guard<std::mutex> g(mutex_);
+      out.error = terr("completion_unknown", "typed dispatch and its owners were quarantined (" +
+                                                 out.error->message + ")");
       quarantined_ = true;
+      quarantine(slot);
     }
   }
   return out;
+}
+
+void Resources::quarantine(std::shared_ptr<void> keep) {
+  // Never freed: work that may still touch these allocations has no proven
+  // end (reference: process-lifetime quarantine of the context and owners).
+  static auto *kept = new std::vector<std::shared_ptr<void>>();
+  static std::mutex m;
+  std::lock_guard<std::mutex> g(m);
+  kept->push_back(std::move(keep));
 }
 
 TransferOutcome Resources::execute(DispatchRequest &request, int device, int /*streams*/,
                                    const TransferOptions &options, std::shared_ptr<void> owners) {
   TransferOutcome out = withContext(
       device, [&](CudaBackend &b) { return executeDispatch(request, b, options); }, !options.asyncCompletion);
-  if (out.completion == TransferCompletion::Unknown) {
-    std::lock_guard<std::mutex> g(mutex_);
-    quarantinedOwners_.push_back(std::move(owners)); // keep buffers alive for good
-  }
+  if (out.completion == TransferCompletion::Unknown)
+    quarantine(std::move(owners)); // keep the buffers alive for good
   if (!out.error && options.asyncCompletion)
     out.completion = TransferCompletion::Pending;
   return out;
@@ -126,7 +146,7 @@ struct Completion::State {
   void *event = nullptr;
   int device = -1;
   bool finished = false;
-  uint64_t waitsBefore = 0; // sbc_wait_launch_count() before the work was enqueued
+  std::shared_ptr<FaultWord> fault; // the context's fault word
   TransferOutcome outcome;
   std::shared_ptr<void> owners; // buffers kept alive until completion
   ~State() {
@@ -136,32 +156,22 @@ struct Completion::State {
       sbc_event_destroy(event);
     }
   }
-  /// Finalize after the event completed: the device's fault word.
+  /// Finalize after the event completed: the context's fault word (plain
+  /// host memory, written by any kernel of the group whose wait ran out).
   void finalizeLocked() {
     finished = true;
-    if (sbc_wait_launch_count() == waitsBefore) { // no kernel that writes the fault word ran
-      outcome.completion = TransferCompletion::Complete;
-      owners.reset();
-      return;
-    }
-    int fault = 0;
-    int dev = -1;
-    sbc_get_device(&dev);
-    if (dev != device)
-      sbc_set_device(device);
-    const int rc = sbc_device_fault(&fault);
-    if (dev != device && dev >= 0)
-      sbc_set_device(dev);
-    if (rc) {
-      outcome.error = terr("backend_failure", std::string("fault word: ") + sbc_error_string(rc));
-      outcome.completion = TransferCompletion::Unknown;
-    } else if (fault) {
+    outcome.completion = TransferCompletion::Complete;
+    if (fault && fault->take())
       outcome.error = terr("backend_failure", "a kernel's bounded wait for a TMA copy ran out; the output is incomplete");
-      outcome.completion = TransferCompletion::Complete;
-    } else {
-      outcome.completion = TransferCompletion::Complete;
-    }
     owners.reset();
+  }
+  /// The event could not be waited for: completion is unknown, and the
+  /// owners are kept for the life of the process.
+  void unknownLocked(int rc) {
+    finished = true;
+    outcome.error = terr("completion_unknown", std::string("completion: ") + sbc_error_string(rc));
+    outcome.completion = TransferCompletion::Unknown;
+    Resources::quarantine(std::move(owners));
   }
 };
 
@@ -170,8 +180,13 @@ Completion::Completion(std::shared_ptr<State> state) : state_(std::move(state)) 
 Completion::~Completion() {
   if (state_) {
     std::lock_guard<std::mutex> g(state_->m);
-    if (!state_->finished && state_->event && sbc_event_synchronize(state_->event) == 0)
-      state_->finalizeLocked();
+    if (!state_->finished && state_->event) {
+      const int rc = sbc_event_synchronize(state_->event);
+      if (rc)
+        state_->unknownLocked(rc);
+      else
+        state_->finalizeLocked();
+    }
   }
 }
 
@@ -179,13 +194,10 @@ TransferOutcome Completion::wait() {
   std::lock_guard<std::mutex> g(state_->m);
   if (!state_->finished) {
     const int rc = sbc_event_synchronize(state_->event);
-    if (rc) {
-      state_->finished = true;
-      state_->outcome.error = terr("backend_failure", std::string("completion: ") + sbc_error_string(rc));
-      state_->outcome.completion = TransferCompletion::Unknown; // owners stay referenced for good
-      return state_->outcome;
-    }
-    state_->finalizeLocked();
+    if (rc)
+      state_->unknownLocked(rc);
+    else
+      state_->finalizeLocked();
   }
   return state_->outcome;
 }
@@ -200,13 +212,10 @@ std::variant<bool, TransferError> Completion::query() {
   const int rc = sbc_event_query(state_->event);
   if (rc == 1)
     return false;
-  if (rc) {
-    state_->finished = true;
-    state_->outcome.error = terr("backend_failure", std::string("completion: ") + sbc_error_string(rc));
-    state_->outcome.completion = TransferCompletion::Unknown;
-    return *state_->outcome.error;
-  }
-  state_->finalizeLocked();
+  if (rc)
+    state_->unknownLocked(rc);
+  else
+    state_->finalizeLocked();
   if (state_->outcome.error)
     return *state_->outcome.error;
   return true;
@@ -231,10 +240,8 @@ TransferOutcome Resources::execute(GroupRequest &group, const TransferOptions &o
   TransferOutcome out = withContext(
       group.device, [&](CudaBackend &b) { return executeGroup(group, b, options, nullptr); },
       !options.asyncCompletion);
-  if (out.completion == TransferCompletion::Unknown) {
-    std::lock_guard<std::mutex> g(mutex_);
-    quarantinedOwners_.push_back(std::move(owners));
-  }
+  if (out.completion == TransferCompletion::Unknown)
+    quarantine(std::move(owners));
   if (!out.error && options.asyncCompletion)
     out.completion = TransferCompletion::Pending;
   return out;
@@ -256,14 +263,12 @@ Resources::submit(GroupRequest &group, const TransferOptions &options, std::shar
       state->event = nullptr;
       return terr("backend_failure", std::string("cudaEventCreate: ") + sbc_error_string(rc));
     }
-    state->waitsBefore = sbc_wait_launch_count();
+    state->fault = b.faultShared();
     return executeGroup(group, b, o, state->event);
   }, false);
   if (out.error) {
-    if (out.completion == TransferCompletion::Unknown) {
-      std::lock_guard<std::mutex> g(mutex_);
-      quarantinedOwners_.push_back(std::move(owners));
-    }
+    if (out.completion == TransferCompletion::Unknown)
+      quarantine(std::move(owners));
     return *out.error;
   }
   state->owners = std::move(owners);
@@ -294,6 +299,7 @@ ResourceStats Resources::stats() const {
     s.kernelLaunches += b.kernelLaunches;
   }
   s.evictions = evictions_;
+  s.retirements = retired_;
   s.retainedBytes = s.deviceBytes;
   return s;
 }

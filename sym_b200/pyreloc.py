@@ -42,8 +42,16 @@ class TransferError(RuntimeError):
         self.detail = message
 
 
-def _raise_transfer(err: SbError):
+# Owners of executions whose completion could not be proven
+# (completion_unknown): kept alive for the life of the process, because work
+# that may still touch their memory has no proven end.
+_QUARANTINED = []
+
+
+def _raise_transfer(err: SbError, owners=None):
     code, message, _ = error_of(err)
+    if code == "completion_unknown" and owners is not None:
+        _QUARANTINED.append(owners)
     raise TransferError(code, message)
 
 
@@ -409,7 +417,7 @@ def execute_dispatch(request: DispatchRequest, *, caller_stream=None, n_buffers=
     report = json.loads(buf.value.decode())
     request.report = MappingProxyType(report)
     if rc:
-        _raise_transfer(err)
+        _raise_transfer(err, owners)
     return MappingProxyType(report)
 
 
@@ -709,7 +717,7 @@ def execute_dispatch_group(group, *, caller_stream=None, gather_threads=8, gathe
         del _keep
     if rc:
         group.failed = True
-        _raise_transfer(err)
+        _raise_transfer(err, owners)
     import json
 
     return MappingProxyType(json.loads(buf.value.decode()))
@@ -734,17 +742,18 @@ class DispatchCompletion(_Handle):
     def wait(self):
         err = SbError()
         if _native.lib().sb_completion_wait(self._ptr, ctypes.byref(err)):
-            code = err.code.decode()
-            if code != "backend_failure" or "completion" not in err.message.decode():
-                self._done()
-            _raise_transfer(err)
+            owners = self._owners
+            self._done()
+            _raise_transfer(err, owners)
         self._done()
 
     def query(self):
         done = ctypes.c_int32()
         err = SbError()
         if _native.lib().sb_completion_query(self._ptr, ctypes.byref(done), ctypes.byref(err)):
-            _raise_transfer(err)
+            owners = self._owners
+            self._done()
+            _raise_transfer(err, owners)
         if done.value:
             self._done()
         return bool(done.value)
@@ -776,5 +785,5 @@ def submit_dispatch_group(group, *, caller_stream=None, gather_threads=8, gather
         group.consumed = True
     if rc:
         group.failed = True
-        _raise_transfer(err)
+        _raise_transfer(err, owners)
     return DispatchCompletion(out, group, owners)

@@ -37,6 +37,15 @@ def _static_twice(blob, symbols, params, src):
     return outs
 
 
+def _reference(blob, symbols, params, src):
+    """The reference CPU executor's bytes, when its build is present."""
+    from oracle import ref
+
+    if not ref.available():
+        return None
+    return ref.TypedProgram(blob, symbols, params).execute(np.ascontiguousarray(src).view(np.uint8).reshape(-1))
+
+
 def test_static_entry_point_matches_execute_dispatch_weights():
     """int8 [out, in] -> dequantize (per-row scale) -> f16 -> transpose, with
     more source rows than one staging slot holds (several chunks per call)."""
@@ -51,6 +60,8 @@ def test_static_entry_point_matches_execute_dispatch_weights():
     first, second = _static_twice(blob, sym, params, q)
     assert np.array_equal(first, want)
     assert np.array_equal(second, want)
+    reference = _reference(blob, sym, params, q)
+    assert reference is None or np.array_equal(first, reference)
 
 
 def test_static_entry_point_matches_execute_dispatch_quantize():
@@ -63,6 +74,8 @@ def test_static_entry_point_matches_execute_dispatch_quantize():
     first, second = _static_twice(blob, {"B": 8, "S": 7}, {}, x)
     assert np.array_equal(first, want)
     assert np.array_equal(second, want)
+    reference = _reference(blob, {"B": 8, "S": 7}, {}, x)
+    assert reference is None or np.array_equal(first, reference)
 
 
 def test_static_entry_point_rejects_rows_beyond_the_scratch():
