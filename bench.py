@@ -2,32 +2,45 @@
 """Benchmark: Llama-70B-shaped int8 weight fetch (the sharded weight-fetch configuration).
 
 One step = one model pass: 16 layers x {q, k, v, o, gate, up, down} int8
-[out, in] matrices with per-row f32 scales (lognormal(-5, 0.5)), each
-dequantized, narrowed to f16 (RNE) and transposed to [in, out] on the GPU by
-the fused sm_100a kernel. With N GPUs (default `--multi peer`) rank k copies
-the contiguous int8 source rows of its shard of every matrix (sized by each
-GPU's measured concurrent PCIe bandwidth, `--balance 1`) into its own HBM,
-and every rank's kernels read all shards -- its peers' over NVLink through
-CUDA IPC mappings -- writing the full f16 layer locally: NVLink carries int8,
-not f16. `--multi allgather`: every rank produces its 1/N window of result
-rows and an in-place NCCL all-gather assembles the layer.
+[out, in] matrices with per-row f32 scales (lognormal(-5, 0.5)), held in
+pinned host memory, each moved to the GPU, dequantized, narrowed to f16 (RNE)
+and transposed to [in, out] by the fused sm_100a kernel. With N GPUs (default
+`--multi peer`) rank k copies the contiguous int8 source rows of its shard of
+every matrix (sized by each GPU's measured concurrent host-to-device
+bandwidth, `--balance 1`) into its own HBM, and every rank's kernels read all
+shards -- its peers' over NVLink through CUDA IPC mappings -- writing the full
+f16 layer locally: NVLink carries int8, not f16. `--multi allgather`: every
+rank produces its 1/N window of result rows and an in-place NCCL all-gather
+assembles the layer.
 
 Metric: layers/s of the whole job (every layer assembled on every GPU), with
-relocated GB/s per GPU and its fraction of the measured pinned-memcpy H2D
-ceiling alongside.
+relocated GB/s and its fraction of the measured pinned-memcpy H2D ceiling
+alongside.
 
-  value : inputs already resident in HBM (each rank's int8 shards, or the
-          whole int8 matrices with --multi allgather); the timed work is the
-          transform kernels (peer reads over NVLink / the all-gather).
-  e2e   : the same through the drop-in C-ABI with HOST pinned sources: each
-          rank's window bytes cross PCIe by DMA into the HBM ring inside the
-          timed region; one small device->host read of the result per step.
+  value           : host-to-device + transform (the metric's own work): int8
+                    in pinned host memory when the timed region starts, every
+                    layer crosses PCIe inside it; CUDA events on the caller
+                    stream, max over ranks.
+  e2e             : the same job through the public API a user calls (N = 1:
+                    pyreloc.execute_dispatch, the drop-in C-ABI call, once per
+                    matrix; N > 1: workloads.PeerShardedFetch), plus a
+                    device-to-host read of the step's result; host wall clock
+                    between synchronization points, max over ranks.
+  device_resident : the transform kernels alone with the int8 already in HBM
+                    (peer reads over NVLink for N > 1), for the kernel
+                    roofline; not the metric.
+
+After the timed regions the last assembled layer is hashed (SHA-256 per
+matrix): every rank's digests must agree, rank 0 compares them with the
+single-GPU path on the same synthetic layer (N > 1), and at N = 1 the
+CPU-baseline leg compares them with the reference executor's output. A
+mismatch exits 1.
 
 Synthetic data (no checkpoints): int8 uniform[-127, 127]; scales
 exp(N(-5, 0.5)); seed = layer index. Host memory holds `--distinct-layers`
-(default 2) layers per rank and the 16 layers of a step cycle over them --
-every layer still crosses PCIe in full; layers are 855 MB >> L2 (126 MB) and
->> the host LLC, so no cache can serve a repeat.
+(default 2) layers and the 16 layers of a step cycle over them -- every layer
+still crosses PCIe in full; layers are 855 MB >> L2 (126 MB) and >> the host
+LLC, so no cache can serve a repeat.
 
 `--impl reference`: the reference's own CPU executor (oracle/_ref, typed::
 executeHost with a GatherPool of every host core) on a bounded sample of
@@ -36,6 +49,7 @@ the same workload (one layer per step), rank 0 only.
 from __future__ import annotations
 
 import argparse
+import hashlib
 import json
 import os
 import statistics
@@ -143,20 +157,41 @@ def run_reference(args):
 # our arm
 # ---------------------------------------------------------------------------
 
-class Clocks:
-    """nvidia-smi sampling during the timed region."""
+def gpu_selector(torch, device_index):
+    """nvidia-smi's -i argument for this process's GPU: its UUID (robust to
+    CUDA_VISIBLE_DEVICES), else the physical index."""
+    try:
+        uuid = str(torch.cuda.get_device_properties(device_index).uuid)
+        if uuid:
+            return uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
+    except Exception:
+        pass
+    visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if visible:
+        return visible.split(",")[device_index].strip()
+    return str(device_index)
 
-    def __init__(self):
+
+class Clocks:
+    """nvidia-smi samples of ONE GPU (read-only queries) during a timed
+    region; the reported clock is the median of the samples taken under load
+    (utilization above zero)."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,utilization.gpu,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+    REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+
+    def __init__(self, selector):
+        self.selector = selector
         self.path = Path(tempfile.mkstemp(prefix="clocks", suffix=".csv")[1])
         self.proc = None
 
     def start(self):
-        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits",
-                                          "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", self.selector, f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
 
@@ -165,29 +200,27 @@ class Clocks:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.proc.terminate()
         self.proc.wait()
-        sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        rows = []
         for line in self.path.read_text().splitlines():
             f = [x.strip() for x in line.split(",")]
-            if len(f) < 9:
+            if len(f) < 8:
                 continue
             try:
-                sm.append(float(f[1]))
-                mx.append(float(f[2]))
+                rows.append((float(f[0]), float(f[1]), float(f[3]), f[4:8]))
             except ValueError:
                 continue
-            for n, v in zip(names, f[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
         self.path.unlink(missing_ok=True)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        loaded = [r for r in rows if r[2] > 0] or rows
+        reasons = sorted({n for r in loaded for n, v in zip(self.REASONS, r[3]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[0] for r in loaded) if loaded else None,
+                "sm_max_mhz": max(r[1] for r in rows) if rows else None, "reasons": reasons,
+                "samples": len(rows), "samples_under_load": len([r for r in rows if r[2] > 0]),
+                "gpu": self.selector}
 
 
-def pinned_h2d_gbs(torch, device, nbytes=256 << 20, reps=10, sync=None, d2h=False):
-    """Best-of-``reps`` pinned cudaMemcpyAsync H2D (or D2H) GB/s; with
-    ``sync`` (a barrier), every rank starts each copy together (concurrent
-    bandwidth)."""
+def pinned_h2d_gbs(torch, device, nbytes=256 << 20, reps=10, d2h=False):
+    """Best-of-``reps`` pinned cudaMemcpyAsync H2D (or D2H) GB/s of this GPU
+    alone."""
     host = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
     gpu = torch.empty(nbytes, dtype=torch.uint8, device=device)
     src, dst = (gpu, host) if d2h else (host, gpu)
@@ -197,9 +230,6 @@ def pinned_h2d_gbs(torch, device, nbytes=256 << 20, reps=10, sync=None, d2h=Fals
         for _ in range(3):
             dst.copy_(src, non_blocking=True)
         for _ in range(reps):
-            if sync is not None:
-                s.synchronize()
-                sync()
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record(s)
             dst.copy_(src, non_blocking=True)
@@ -208,6 +238,46 @@ def pinned_h2d_gbs(torch, device, nbytes=256 << 20, reps=10, sync=None, d2h=Fals
             best = max(best, nbytes / (a.elapsed_time(b) * 1e-3) / 1e9)
     del src, dst
     return best
+
+
+def sustained_h2d_gbs(torch, device, barrier, nbytes=512 << 20, reps=4):
+    """Sustained pinned H2D GB/s of this GPU while every rank copies at once:
+    ``reps`` back-to-back copies of ``nbytes`` (2 GiB by default), started
+    together after a barrier. The job's host-to-device bound is the sum over
+    ranks."""
+    host = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    gpu = torch.empty(nbytes, dtype=torch.uint8, device=device)
+    s = torch.cuda.Stream(device)
+    with torch.cuda.stream(s):
+        gpu.copy_(host, non_blocking=True)
+    s.synchronize()
+    barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(s):
+        a.record(s)
+        for _ in range(reps):
+            gpu.copy_(host, non_blocking=True)
+        b.record(s)
+    b.synchronize()
+    rate = nbytes * reps / (a.elapsed_time(b) * 1e-3) / 1e9
+    del host, gpu
+    return rate
+
+
+def device_map(mode, local, world, visible):
+    """GPU index of local rank `local`: identity, or `halves` -- ranks
+    alternate between the two halves of the visible GPUs (0, V/2, 1, V/2+1,
+    ...), which sit behind different host bridges on the pool's 8-GPU boxes,
+    so N < V ranks do not share one bridge's host-to-device bandwidth."""
+    if mode == "identity" or world >= visible or visible < 2:
+        return local
+    half = visible // 2
+    return (local % 2) * half + local // 2
+
+
+def layer_digests(torch, outs):
+    """SHA-256 of each matrix's result bytes (the output check)."""
+    return [hashlib.sha256(o.contiguous().view(torch.uint8).cpu().numpy().tobytes()).hexdigest() for o in outs]
 
 
 def run_ours(args):
@@ -220,8 +290,9 @@ def run_ours(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
+    gpu_index = device_map(args.gpu_map, local, world, torch.cuda.device_count())
+    torch.cuda.set_device(gpu_index)
+    dev = torch.device("cuda", gpu_index)
     if world > 1:
         import datetime
 
@@ -229,7 +300,7 @@ def run_ours(args):
 
     def barrier():
         if world > 1:
-            dist.barrier(device_ids=[local])
+            dist.barrier(device_ids=[gpu_index])
 
     def max_over_ranks(x):
         if world == 1:
@@ -238,8 +309,15 @@ def run_ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    def gather(obj):
+        if world == 1:
+            return [obj]
+        out = [None] * world
+        dist.all_gather_object(out, obj)
+        return out
+
     res = pyreloc.DispatchResources()
-    copy_s, compute_s = res.streams(local)
+    _, compute_s = res.streams(gpu_index)
     compute_stream = torch.cuda.ExternalStream(compute_s, device=dev)
 
     # host data and templates
@@ -255,35 +333,32 @@ def run_ours(args):
                                        {"scale": ("float32", [out_f], scale.tobytes())})
             tmpl = pyreloc.prepare_dispatch_template(bound, "h2d", "cuda", implementation="b200_fused_h2d@dma_ring")
             host = torch.from_numpy(q).pin_memory()
-            devsrc = host.to(dev)
-            mats.append({"name": name, "out": out_f, "in": in_f, "tmpl": tmpl, "host": host, "dev": devsrc})
+            mats.append({"name": name, "out": out_f, "in": in_f, "tmpl": tmpl, "host": host, "dev": host.to(dev),
+                         "scale": scale,
+                         "sv": pyreloc.BufferView(host.data_ptr(), host.numel(), 0, [out_f, in_f], [in_f, 1], 1,
+                                                  "host", -1)})
         distinct.append(mats)
     outs = [[torch.empty((m["in"], m["out"]), dtype=torch.float16, device=dev) for m in distinct[0]]
             for _ in range(2)]
-    from sym_b200.workloads import PeerShardedFetch, ShardedLayerFetch, shard_bounds
+    from sym_b200.workloads import PeerShardedFetch, ShardedLayerFetch
 
-    rows = [shard_bounds(m["in"], world, rank) for m in distinct[0]]
     sample = torch.empty(32, dtype=torch.float16).pin_memory()
-    # Host->device bandwidth of this rank alone and with every rank copying at
-    # once (the GPUs of one box share the host's memory and PCIe links).
+    # Host-to-device bandwidth: this GPU alone (best of 10 256 MiB copies) and
+    # sustained while every rank copies 2 GiB at once (the job's bound).
     alone = pinned_h2d_gbs(torch, dev)
-    concurrent = pinned_h2d_gbs(torch, dev, sync=barrier) if world > 1 else alone
+    concurrent = sustained_h2d_gbs(torch, dev, barrier)
+    rates = gather(concurrent)
     peer = world > 1 and args.multi == "peer"
-    weights = None
+    weights = rates if (peer and args.balance) else None
     if peer:
-        if args.balance:
-            w = torch.tensor([concurrent], dtype=torch.float64, device=dev)
-            ws = [torch.zeros_like(w) for _ in range(world)]
-            dist.all_gather(ws, w)
-            weights = [float(x.item()) for x in ws]
-        fetcher = PeerShardedFetch(res, local, world, rank, [(m["out"], m["in"]) for m in distinct[0]],
+        fetcher = PeerShardedFetch(res, gpu_index, world, rank, [(m["out"], m["in"]) for m in distinct[0]],
                                    weights=weights, buffers=len(distinct))
         for d, mats in enumerate(distinct):
             fetcher.preload(d, [m["host"] for m in mats])
         torch.cuda.synchronize(dev)
         barrier()
     else:
-        fetcher = ShardedLayerFetch(res, local, world, rank, chunk_bytes=args.chunk_bytes,
+        fetcher = ShardedLayerFetch(res, gpu_index, world, rank, chunk_bytes=args.chunk_bytes,
                                     ring_slots=args.ring_slots, route=args.route)
 
     def layer(l, host_source):
@@ -303,8 +378,23 @@ def run_ours(args):
                 handles = handles[-7:]
         for h in handles:
             h.wait()
-        if host_source:
-            sample.copy_(outs[(n_layers - 1) % 2][-1].view(-1)[:32], non_blocking=True)
+
+    cur = torch.cuda.current_stream(dev)
+
+    def public_step():
+        """One step through the public API, with the result read back."""
+        if world == 1:
+            for l in range(n_layers):
+                for m, out in zip(distinct[l % len(distinct)], outs[l % 2]):
+                    dv = pyreloc.BufferView(out.data_ptr(), out.numel() * 2, 0, [m["in"], m["out"]],
+                                            [m["out"], 1], 2, "cuda", gpu_index)
+                    req = pyreloc.prepare_dispatch_from_template(m["tmpl"], m["sv"], dv)
+                    pyreloc.execute_dispatch(req, resources=res, caller_stream=cur.cuda_stream,
+                                             chunk_size=args.chunk_bytes, n_buffers=args.ring_slots)
+        else:
+            step(True)
+        sample.copy_(outs[(n_layers - 1) % 2][-1].view(-1)[:32], non_blocking=True)
+        torch.cuda.synchronize(dev)
 
     def timed(host_source, steps):
         torch.cuda.synchronize(dev)
@@ -320,38 +410,66 @@ def run_ours(args):
         torch.cuda.synchronize(dev)
         return max_over_ranks(a.elapsed_time(b) * 1e-3)
 
-    launches0 = pyreloc.kernel_launches()
+    def timed_public(steps):
+        torch.cuda.synchronize(dev)
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            public_step()
+        dt = time.perf_counter() - t0
+        barrier()
+        return max_over_ranks(dt)
+
     for _ in range(args.warmup):
-        step(False)
         step(True)
+        step(False)
+        public_step()
     torch.cuda.synchronize(dev)
 
-    clocks = Clocks() if rank == 0 else None
-    if clocks:
-        clocks.start()
+    clocks = Clocks(gpu_selector(torch, gpu_index))
+    clocks.start()
     l0 = pyreloc.kernel_launches()
-    t_value = timed(False, args.steps)
+    t_value = timed(True, args.steps)
     l1 = pyreloc.kernel_launches()
-    t_e2e = timed(True, args.steps)
-    ck = clocks.stop() if clocks else None
+    t_e2e = timed_public(args.steps)
+    t_dev = timed(False, args.steps)
+    ck = clocks.stop()
     launches_value = l1 - l0
+    clock_records = gather(ck)
+
+    # Output check: the last layer the e2e region assembled, on every rank.
+    last = (n_layers - 1) % len(distinct)
+    digests = layer_digests(torch, outs[(n_layers - 1) % 2])
+    all_digests = gather(digests)
+    check = {"sha256_last_layer": digests, "layer_seed": last,
+             "ranks_agree": all(d == digests for d in all_digests)}
+    if world > 1 and rank == 0:
+        # the single-GPU path on the same synthetic layer, into fresh buffers
+        single = []
+        for m in distinct[last]:
+            o = torch.empty((m["in"], m["out"]), dtype=torch.float16, device=dev)
+            pyreloc.execute_rows(m["tmpl"], m["host"].data_ptr(), o.data_ptr(), 0, m["in"], device=gpu_index,
+                                 host_source=True, resources=res)
+            single.append(o)
+        check["vs_single_gpu"] = "match" if layer_digests(torch, single) == digests else "mismatch"
+        del single
 
     # dominant kernel (k_tma_tile<1, ...>, every launch of the step): one launch on the
-    # largest matrix (gate, this rank's result rows), device-resident source,
-    # timed on the compute stream it runs on. Algorithmic bytes per launch:
-    # 1 B int8 read + 2 B f16 written per element + 4 B per source-row scale.
+    # largest matrix (gate), device-resident source, timed on the compute stream it
+    # runs on. Algorithmic bytes per launch: 1 B int8 read + 2 B f16 written per
+    # element + 4 B per source-row scale.
     torch.cuda.synchronize(dev)
     gi = [m["name"] for m in distinct[0]].index("gate")
-    gm, gout, (gb, ge) = distinct[0][gi], outs[0][gi], rows[gi]
+    gm, gout = distinct[0][gi], outs[0][gi]
 
     def gate_launch():
-        pyreloc.execute_rows(gm["tmpl"], gm["dev"].data_ptr(), gout[gb:ge].data_ptr(), gb, ge, device=local,
+        pyreloc.execute_rows(gm["tmpl"], gm["dev"].data_ptr(), gout.data_ptr(), 0, gm["in"], device=gpu_index,
                              host_source=False, resources=res, async_completion=True)
 
     for _ in range(3):
         gate_launch()
-    # 705 MB per launch at N=1: larger than L2, so launches do not hit each
-    # other's lines. Each launch between its own pair of events; median and p95.
+    # 705 MB per launch: larger than L2, so launches do not hit each other's
+    # lines. Each launch between its own pair of events; median and p95.
     reps = 20
     marks = [torch.cuda.Event(enable_timing=True) for _ in range(reps + 1)]
     marks[0].record(compute_stream)
@@ -362,72 +480,103 @@ def run_ours(args):
     launch_s = sorted(marks[i].elapsed_time(marks[i + 1]) * 1e-3 for i in range(reps))
     kernel_s = statistics.median(launch_s)
     kernel_p95_s = launch_s[int(0.95 * (reps - 1) + 0.5)]
-    gate_elems = gm["out"] * (ge - gb)
+    gate_elems = gm["out"] * gm["in"]
     kernel_bytes = gate_elems * 3 + gm["out"] * 4
     achieved_gbs = kernel_bytes / kernel_s / 1e9
     # the ncu capture is of the 70B gate launch; other shapes carry no traffic figure
     traffic = GATE_DRAM_BYTES_PER_ELEM * gate_elems if args.config == "c5" else None
 
-    # the ceiling of the slowest rank when all copy at once (the job waits for it)
-    ceiling = -max_over_ranks(-concurrent) if world > 1 else alone
+    layer_src_bytes = sum(o * i for _, o, i in shapes)
+    layers_value = args.steps * n_layers / t_value
+    layers_e2e = args.steps * n_layers / t_e2e
+    layers_dev = args.steps * n_layers / t_dev
+    aggregate_ceiling = sum(rates)  # GB/s of the whole box while every rank copies
+    bound_layers = aggregate_ceiling * 1e9 / layer_src_bytes
+    gpus = gather(gpu_index)
 
-    # checksum: size-independent property -- every layer assembled == the
-    # same bytes the single-GPU path produces (compared in tests); here the
-    # finite-ness of a sample of the last output.
-    assert torch.isfinite(sample.float()).all()
-
+    if peer:
+        fetcher.close()
     if rank != 0:
         if world > 1:
             dist.destroy_process_group()
         return 0
-    layers_value = args.steps * n_layers / t_value
-    layers_e2e = args.steps * n_layers / t_e2e
-    layer_src_bytes = sum(o * i for _, o, i in shapes)
-    per_gpu_wire = layer_src_bytes / world
-    gbs_per_gpu = per_gpu_wire * layers_e2e / 1e9
     peaks = _peaks()
     hbm = peaks.get("hbm_gbs")
     peak_note = "measured" if hbm else "fallback"
     hbm = hbm or 6650.0
+    cpu = None
     from oracle import ref
 
-    cpu = None
-    if ref.available() and world >= 1:
-        cpu = cpu_baseline(shapes)
+    if world == 1 and ref.available():
+        cpu = cpu_baseline(distinct[last], digests)
+        check["vs_reference"] = cpu.pop("output_check")
+    ok = check["ranks_agree"] and check.get("vs_single_gpu", "match") == "match" and \
+        check.get("vs_reference", "match") == "match"
+    check["status"] = "match" if ok else "mismatch"
+    extras = run_extras() if (world == 1 and args.extras) else None
+    gbs_job = layer_src_bytes * layers_value / 1e9
+    if peer:
+        shard = ("int8 source rows per rank (weighted by sustained concurrent H2D bandwidth)" if args.balance
+                 else "int8 source rows per rank, equal") + "; every rank's kernels read all shards (peers' over " \
+                                                           "NVLink, CUDA IPC)"
+    elif world > 1:
+        shard = "result rows [k*in/N,(k+1)*in/N) + in-place NCCL all-gather"
+    else:
+        shard = "none"
     line = {
         "metric": METRIC, "value": layers_value, "unit": "layers/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": 1e3 * t_value / args.steps, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "int8->f16", "data": "synthetic",
         "config": {"workload": workload, "layers_per_step": n_layers,
                    "matrices": {n: [o, i] for n, o, i in shapes}, "distinct_host_layers": args.distinct_layers,
-                   "shard": ("int8 source rows per rank (weighted by concurrent PCIe bandwidth)" if args.balance
-                             else "int8 source rows per rank, equal") + "; every rank's kernels read all shards "
-                            "(peers' over NVLink, CUDA IPC)" if peer else
-                            "result rows [k*in/N,(k+1)*in/N) + in-place NCCL all-gather" if world > 1 else "none",
-                   "shard_weights": weights,
+                   "shard": shard, "shard_weights": weights, "gpu_map": args.gpu_map, "gpus": gpus,
                    "route": args.route, "ring_slots": args.ring_slots, "chunk_bytes": args.chunk_bytes,
-                   "l2": "inputs larger than L2 (855 MB int8 per layer)"},
-        "gbs_per_gpu": gbs_per_gpu, "pinned_h2d_ceiling_gbs": ceiling, "pinned_h2d_alone_gbs": alone,
-        "pct_of_pinned_memcpy": 100.0 * gbs_per_gpu / ceiling if ceiling else None,
+                   "l2": "inputs larger than L2 (855 MB int8 per layer)",
+                   "value_timing": "CUDA events on the caller stream around the steps, max over ranks"},
+        "gbs_per_gpu": gbs_job / world, "gbs_job": gbs_job,
+        "pinned_h2d_sustained_gbs_per_rank": rates, "pinned_h2d_aggregate_gbs": aggregate_ceiling,
+        "pinned_h2d_alone_gbs": alone,
+        "pct_of_pinned_memcpy": 100.0 * gbs_job / aggregate_ceiling,
+        "h2d_bound_layers_per_s": bound_layers,
         "e2e": {"value": layers_e2e, "unit": "layers/s", "ms_per_step": 1e3 * t_e2e / args.steps,
-                "h2d_bytes_per_step": int(per_gpu_wire * n_layers), "d2h_bytes_per_step": int(sample.numel() * 2)},
+                "h2d_bytes_per_step": int(layer_src_bytes / world * n_layers),
+                "d2h_bytes_per_step": int(sample.numel() * 2),
+                "api": "pyreloc.execute_dispatch per matrix (sb_execute_dispatch)" if world == 1 else
+                       "workloads.PeerShardedFetch.fetch" if peer else "workloads.ShardedLayerFetch.fetch",
+                "timing": "host wall clock between synchronizations, max over ranks",
+                "pct_of_pinned_memcpy": 100.0 * layer_src_bytes * layers_e2e / 1e9 / aggregate_ceiling},
+        "device_resident": {"value": layers_dev, "unit": "layers/s", "ms_per_step": 1e3 * t_dev / args.steps,
+                            "note": "int8 already in HBM; transform kernels only"
+                                    + (" (peer shards read over NVLink)" if peer else "")},
         "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": hbm, "unit": "GB/s",
                      "frac": achieved_gbs / hbm, "traffic": traffic, "peak_source": peak_note,
-                     "kernel": f"k_tma_tile<int8, CH_DQ_F16, per-column scale> on gate [{gm['out']}, {gm['in']}], "
-                               "this rank's rows",
+                     "kernel": f"k_tma_tile<int8, CH_DQ_F16, per-column scale> on gate [{gm['out']}, {gm['in']}]",
                      "bytes_per_launch": kernel_bytes, "launch_ms": kernel_s * 1e3,
                      "launch_ms_p95": kernel_p95_s * 1e3, "launches_timed": reps,
                      "bytes_per_launch_note": "int8 read + f16 write per element + 4 B per source-row scale",
                      "traffic_note": "ncu dram__bytes_read.sum + dram__bytes_write.sum of the full gate launch "
-                                     "(--kernel-case), scaled by this rank's share of its elements"},
-        "gpu_launches": int(launches_value), "clocks": ck,
+                                     "(--kernel-case)"},
+        "output_check": check,
+        "gpu_launches": int(launches_value), "clocks": _merge_clocks(clock_records),
     }
     if cpu:
         line["cpu_baseline"] = cpu
+    if extras:
+        line["configs"] = extras
     print(json.dumps(line))
     if world > 1:
         dist.destroy_process_group()
-    return 0
+    return 0 if ok else 1
+
+
+def _merge_clocks(records):
+    """One clock record for the job: the lowest per-GPU median under load,
+    the union of the reasons seen, every GPU's own record beside them."""
+    meds = [r.get("sm_mhz") for r in records if r.get("sm_mhz") is not None]
+    maxes = [r.get("sm_max_mhz") for r in records if r.get("sm_max_mhz") is not None]
+    reasons = sorted({x for r in records for x in r.get("reasons", [])})
+    return {"sm_mhz": min(meds) if meds else None, "sm_max_mhz": max(maxes) if maxes else None,
+            "reasons": reasons, "per_gpu": records}
 
 
 def host_info():
@@ -450,40 +599,46 @@ def host_info():
             "numa_nodes": len(nodes) or None}
 
 
-def cpu_baseline(shapes):
-    """The reference CPU executor on one Llama-70B matrix pair (~10-20 s of
-    CPU work) with every usable host thread, and again with 8 threads (the
-    reference's own qualified setting)."""
+def cpu_baseline(mats, digests, seconds=10.0):
+    """The reference CPU executor (typed::executeHost, GatherPool of every
+    usable host thread) on the bench's last synthetic layer, whole: repeated
+    for about ``seconds`` (at least once), then once with 8 threads (the
+    reference's own qualified setting). Its result's digests are compared with
+    the GPU's (the output check)."""
     from helpers import encode, recipe_c4
     from oracle import ref
 
     threads = len(os.sched_getaffinity(0))
     blob = encode(recipe_c4())
-    rng = np.random.default_rng(0)
-    out_f, in_f = 8192, 8192
-    q = rng.integers(-127, 128, size=(out_f, in_f), dtype=np.int8)
-    scale = np.exp(rng.normal(-5.0, 0.5, out_f)).astype(np.float32)
-    p = ref.TypedProgram(blob, {"out_features": out_f, "in_features": in_f},
-                         {"scale": ("float32", [out_f], scale.tobytes())})
-    dst = np.empty(out_f * in_f * 2, np.uint8)
-    src = q.reshape(-1).view(np.uint8)
-    layer_elems = sum(o * i for _, o, i in shapes)
+    progs = []
+    for m in mats:
+        p = ref.TypedProgram(blob, {"out_features": m["out"], "in_features": m["in"]},
+                             {"scale": ("float32", [m["out"]], m["scale"].tobytes())})
+        progs.append((p, m["host"].numpy().reshape(-1).view(np.uint8), np.empty(m["out"] * m["in"] * 2, np.uint8)))
 
-    def rate(pool, seconds):
-        p.execute_into(src, dst, pool=pool)
-        t0, n = time.perf_counter(), 0
-        while time.perf_counter() - t0 < seconds and n < 20:
+    def layer(pool):
+        for p, src, dst in progs:
             p.execute_into(src, dst, pool=pool)
-            n += 1
-        return (out_f * in_f / ((time.perf_counter() - t0) / n)) / layer_elems, n
 
     pool = ref.GatherPool(threads)
-    value, n = rate(pool, 8.0)
-    value8, n8 = rate(ref.GatherPool(8), 4.0)
-    return {"value": value, "unit": "layers/s", "cores": pool.threads, "kind": "reference",
-            "sample": f"q-projection [8192, 8192] int8 -> f16 [8192, 8192] x{n} via typed::executeHost, "
-                      "scaled to layers by element count",
-            "value_8_threads": value8, "runs_8_threads": n8, "host": host_info()}
+    t0 = time.perf_counter()
+    layer(pool)
+    busy = time.perf_counter() - t0
+    ref_digests = [hashlib.sha256(dst.tobytes()).hexdigest() for _, _, dst in progs]
+    runs = 1
+    while busy < seconds and runs < 8:
+        t = time.perf_counter()
+        layer(pool)
+        busy += time.perf_counter() - t
+        runs += 1
+    t = time.perf_counter()
+    layer(ref.GatherPool(8))
+    t8 = time.perf_counter() - t
+    return {"value": runs / busy, "unit": "layers/s", "cores": pool.threads, "kind": "reference",
+            "sample": f"the bench's last layer (7 matrices, {sum(m['out'] * m['in'] for m in mats):,} int8 "
+                      f"elements) x{runs} via typed::executeHost",
+            "value_8_threads": 1.0 / t8, "host": host_info(),
+            "output_check": "match" if ref_digests == digests else "mismatch"}
 
 
 def run_kernel_case(args):
@@ -596,9 +751,9 @@ def _config_case(name):
     raise ValueError(name)
 
 
-def _cpu_config(case, threads):
+def _cpu_config(case, threads, seconds=5.0):
     """The reference CPU executor on the config's whole input, host->host
-    (each finishes in well under a second); returns (rate, seconds, runs)."""
+    (each run finishes in well under a second); returns (rate, seconds, runs)."""
     from oracle import ref
 
     src = np.ascontiguousarray(case["src"]).reshape(-1).view(np.uint8)
@@ -612,48 +767,31 @@ def _cpu_config(case, threads):
         run = lambda: p.execute_into(src, dst, pool=pool)  # noqa: E731
     run()
     t0, n = time.perf_counter(), 0
-    while n < 3 or (time.perf_counter() - t0 < 5.0 and n < 20):
+    while n < 3 or (time.perf_counter() - t0 < seconds and n < 20):
         run()
         n += 1
     dt = (time.perf_counter() - t0) / n
     return case["unit_per_step"] / dt, dt, n
 
 
-def run_config(args):
-    """One JSON line for config C1, C2, C3q or C3d on one GPU: `value` with the
-    source resident in HBM (the kernels alone, L2 flushed before each timed
-    launch), `e2e` through the public dispatch API from pinned host memory
-    (the source crosses PCIe inside the timed region, plus a 4 KiB
+def measure_config(name, steps, warmup, cpu_seconds=5.0, cpu_8_threads=True, device=0):
+    """One config (C1, C2, C3q, C3d, tc, c3q_d2h) on one GPU: `value` with
+    the source resident in HBM (the kernels alone, L2 flushed before each
+    timed launch), `e2e` through the public dispatch API from pinned host
+    memory (the source crosses PCIe inside the timed region, plus a 4 KiB
     device->host read of the result per step), the kernel roofline, and the
-    reference CPU executor on the same input."""
-    from oracle import ref
-
-    threads = len(os.sched_getaffinity(0))
-    case = _config_case(args.config)
-    if args.impl == "reference":
-        if not ref.available():
-            print(json.dumps({"impl": "reference", "unavailable": "reference runtime (oracle/_ref) not built"}))
-            return 0
-        rate, dt, n = _cpu_config(case, threads)
-        print(json.dumps({"impl": "reference", "metric": f"{case['workload']} {case['unit']}", "value": rate,
-                          "unit": case["unit"], "n_gpus": args.gpus, "steps": n, "warmup": 1,
-                          "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "weak",
-                          "vs_baseline": None, "dtype": case["dtype"], "data": "synthetic",
-                          "config": {"workload": case["workload"], "shape": case["shape"]},
-                          "cpu_baseline": {"value": rate, "unit": case["unit"], "cores": threads,
-                                           "kind": "reference", "sample": "the whole config input per step"},
-                          "e2e": {"value": rate, "unit": case["unit"], "h2d_bytes_per_step": 0,
-                                  "d2h_bytes_per_step": 0}}))
-        return 0
-
+    reference CPU executor on the same input. Returns the JSON-line dict."""
     import torch
 
+    from oracle import ref
     from sym_b200 import pyreloc
 
-    dev = torch.device("cuda", 0)
+    threads = len(os.sched_getaffinity(0))
+    case = _config_case(name)
+    dev = torch.device("cuda", device)
     torch.cuda.set_device(dev)
     res = pyreloc.DispatchResources()
-    _, compute_s = res.streams(0)
+    _, compute_s = res.streams(device)
     compute = torch.cuda.ExternalStream(compute_s, device=dev)
     if case["layout"]:
         bound = pyreloc.bind(pyreloc.load_plan(case["blob"]), case["symbols"])
@@ -673,17 +811,17 @@ def run_config(args):
     flush = torch.ones(64 << 20, dtype=torch.float32, device=dev)
 
     def kernel():
-        pyreloc.execute_rows(tmpl, dsrc.data_ptr(), out.data_ptr(), 0, rows, device=0, host_source=False,
+        pyreloc.execute_rows(tmpl, dsrc.data_ptr(), out.data_ptr(), 0, rows, device=device, host_source=False,
                              resources=res, async_completion=True)
 
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         kernel()
     torch.cuda.synchronize(dev)
-    clocks = Clocks()
+    clocks = Clocks(gpu_selector(torch, device))
     clocks.start()
     l0 = pyreloc.kernel_launches()
     times = []
-    for _ in range(args.steps):
+    for _ in range(steps):
         flush.sum()
         compute.wait_stream(torch.cuda.default_stream(dev))  # the flush ends before the launch
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -707,14 +845,14 @@ def run_config(args):
 
         def request():
             sv = pyreloc.BufferView(dsrc.data_ptr(), dsrc.numel(), 0, info["source_extents"],
-                                    _dense(info["source_extents"]), sw, "cuda", 0)
+                                    _dense(info["source_extents"]), sw, "cuda", device)
             dv = pyreloc.BufferView(host_out.data_ptr(), host_out.numel(), 0, info["result_extents"],
                                     _dense(info["result_extents"]), dw, "host", -1)
             return pyreloc.prepare_dispatch_from_template(tmpl_d2h, sv, dv)
     elif case["layout"]:
         def request():
             sv = pyreloc.BufferView(host.data_ptr(), host.numel(), 0, [host.numel() // 4], [1], 4, "host", -1)
-            dv = pyreloc.BufferView(out.data_ptr(), out.numel(), 0, [out.numel() // 4], [1], 4, "cuda", 0)
+            dv = pyreloc.BufferView(out.data_ptr(), out.numel(), 0, [out.numel() // 4], [1], 4, "cuda", device)
             return pyreloc.make_transfer(bound, sv, dv)
     else:
         info = bound.describe()
@@ -724,7 +862,7 @@ def run_config(args):
             sv = pyreloc.BufferView(host.data_ptr(), host.numel(), 0, info["source_extents"],
                                     _dense(info["source_extents"]), sw, "host", -1)
             dv = pyreloc.BufferView(out.data_ptr(), out.numel(), 0, info["result_extents"],
-                                    _dense(info["result_extents"]), dw, "cuda", 0)
+                                    _dense(info["result_extents"]), dw, "cuda", device)
             return pyreloc.prepare_dispatch_from_template(tmpl, sv, dv)
 
     def e2e_step():
@@ -738,22 +876,22 @@ def run_config(args):
     torch.cuda.synchronize(dev)
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record(cur)
-    for _ in range(args.steps):
+    for _ in range(steps):
         e2e_step()
     b.record(cur)
     torch.cuda.synchronize(dev)
-    t_e2e = a.elapsed_time(b) * 1e-3 / args.steps
+    t_e2e = a.elapsed_time(b) * 1e-3 / steps
     ck = clocks.stop()
     ceiling = pinned_h2d_gbs(torch, dev, d2h=d2h)
     peaks = _peaks()
     hbm = peaks.get("hbm_gbs") or 6650.0
     achieved = case["kernel_bytes"] / t_kernel / 1e9
-    cpu_rate, _, cpu_n = _cpu_config(case, threads)
+    cpu_rate, _, cpu_n = _cpu_config(case, threads, cpu_seconds) if ref.available() else (None, None, 0)
     h2d = 0 if d2h else host.numel()
     wire = case["dst_bytes"] if d2h else h2d  # bytes that cross PCIe per step
-    print(json.dumps({
+    line = {
         "metric": f"{case['workload']} {case['unit']}", "value": case["unit_per_step"] / t_kernel,
-        "unit": case["unit"], "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "unit": case["unit"], "n_gpus": 1, "steps": steps, "warmup": warmup,
         "ms_per_step": t_kernel * 1e3, "ms_per_step_p95": t_p95 * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": case["dtype"], "data": "synthetic",
         "config": {"workload": case["workload"], "shape": case["shape"],
@@ -767,14 +905,155 @@ def run_config(args):
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                      "traffic": None, "peak_source": "measured" if peaks.get("hbm_gbs") else "fallback",
                      "kernel": desc.get("device_kernel"), "bytes_per_launch": case["kernel_bytes"],
-                     "launches_per_execution": launches / max(1, args.steps),
+                     "launches_per_execution": launches / max(1, steps),
                      "bytes_per_launch_note": case["bytes_note"]},
         "gpu_launches": int(launches), "clocks": ck,
-        "cpu_baseline": {"value": cpu_rate, "unit": case["unit"], "cores": threads, "kind": "reference",
-                         "sample": f"the whole input x{cpu_n}, reference executor host->host",
-                         "value_8_threads": _cpu_config(case, 8)[0], "host": host_info()},
-    }))
+    }
+    if cpu_rate is not None:
+        line["cpu_baseline"] = {"value": cpu_rate, "unit": case["unit"], "cores": threads, "kind": "reference",
+                                "sample": f"the whole input x{cpu_n}, reference executor host->host",
+                                "host": host_info()}
+        if cpu_8_threads:
+            line["cpu_baseline"]["value_8_threads"] = _cpu_config(case, 8, cpu_seconds)[0]
+    res.close()
+    return line
+
+
+def run_config(args):
+    """One JSON line for config C1, C2, C3q, C3d, c3q_d2h or tc on one GPU
+    (see measure_config); `--impl reference` times the reference CPU executor
+    on the same input."""
+    from oracle import ref
+
+    if args.impl == "reference":
+        threads = len(os.sched_getaffinity(0))
+        case = _config_case(args.config)
+        if not ref.available():
+            print(json.dumps({"impl": "reference", "unavailable": "reference runtime (oracle/_ref) not built"}))
+            return 0
+        rate, dt, n = _cpu_config(case, threads)
+        print(json.dumps({"impl": "reference", "metric": f"{case['workload']} {case['unit']}", "value": rate,
+                          "unit": case["unit"], "n_gpus": args.gpus, "steps": n, "warmup": 1,
+                          "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "weak",
+                          "vs_baseline": None, "dtype": case["dtype"], "data": "synthetic",
+                          "config": {"workload": case["workload"], "shape": case["shape"]},
+                          "cpu_baseline": {"value": rate, "unit": case["unit"], "cores": threads,
+                                           "kind": "reference", "sample": "the whole config input per step"},
+                          "e2e": {"value": rate, "unit": case["unit"], "h2d_bytes_per_step": 0,
+                                  "d2h_bytes_per_step": 0}}))
+        return 0
+    print(json.dumps(measure_config(args.config, args.steps, args.warmup)))
     return 0
+
+
+def measure_c4(steps=2, warmup=3, cpu_seconds=3.0):
+    """Config 4 (Llama-7B int8 weight streaming, 32 layers, one GPU) in
+    brief: host-pinned H2D+transform layers/s (CUDA events), the gate
+    kernel's roofline with its source in HBM (L2 flushed before each launch),
+    and the reference CPU executor on one layer."""
+    import torch
+
+    from helpers import encode, recipe_c4
+    from oracle import ref
+    from sym_b200 import pyreloc
+    from sym_b200.workloads import ShardedLayerFetch
+
+    dev = torch.device("cuda", 0)
+    res = pyreloc.DispatchResources()
+    _, compute_s = res.streams(0)
+    compute = torch.cuda.ExternalStream(compute_s, device=dev)
+    blob = encode(recipe_c4())
+    plan = pyreloc.load_typed_plan(blob)
+    layers = []
+    for d in range(2):
+        mats = []
+        for name, q, scale in make_layer(d, LLAMA7B):
+            out_f, in_f = q.shape
+            bound = pyreloc.bind_typed(plan, {"out_features": out_f, "in_features": in_f},
+                                       {"scale": ("float32", [out_f], scale.tobytes())})
+            host = torch.from_numpy(q).pin_memory()
+            mats.append({"name": name, "out": out_f, "in": in_f, "host": host, "dev": host.to(dev), "q": q,
+                         "scale": scale, "tmpl": pyreloc.prepare_dispatch_template(
+                             bound, "h2d", "cuda", implementation="b200_fused_h2d@dma_ring")})
+        layers.append(mats)
+    outs = [[torch.empty((m["in"], m["out"]), dtype=torch.float16, device=dev) for m in layers[0]] for _ in range(2)]
+    fetch = ShardedLayerFetch(res, 0, 1, 0, chunk_bytes=16 << 20)
+
+    def step():
+        for l in range(32):
+            fetch.fetch(layers[l % 2], outs[l % 2], True)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        step()
+    b.record()
+    torch.cuda.synchronize(dev)
+    t = a.elapsed_time(b) * 1e-3
+    gm, gout = layers[0][4], outs[0][4]
+    flush = torch.ones(64 << 20, dtype=torch.float32, device=dev)
+    times = []
+    for _ in range(10):
+        flush.sum()
+        compute.wait_stream(torch.cuda.default_stream(dev))
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(compute)
+        pyreloc.execute_rows(gm["tmpl"], gm["dev"].data_ptr(), gout.data_ptr(), 0, gm["in"], device=0,
+                             host_source=False, resources=res, async_completion=True)
+        e1.record(compute)
+        torch.cuda.synchronize(dev)
+        times.append(e0.elapsed_time(e1) * 1e-3)
+    tk = statistics.median(times)
+    kbytes = gm["out"] * gm["in"] * 3 + gm["out"] * 4
+    hbm = _peaks().get("hbm_gbs") or 6650.0
+    layer_bytes = sum(o * i for _, o, i in LLAMA7B)
+    line = {"workload": "llama7b_int8_fetch", "value": 32 * steps / t, "unit": "layers/s",
+            "gbs": layer_bytes * 32 * steps / t / 1e9,
+            "roofline": {"kernel": "k_tma_tile on gate [11008, 4096]", "achieved": kbytes / tk / 1e9, "peak": hbm,
+                         "frac": kbytes / tk / 1e9 / hbm, "launch_ms": tk * 1e3, "unit": "GB/s"}}
+    if ref.available():
+        threads = len(os.sched_getaffinity(0))
+        pool = ref.GatherPool(threads)
+        progs = []
+        for m in layers[0]:
+            p = ref.TypedProgram(blob, {"out_features": m["out"], "in_features": m["in"]},
+                                 {"scale": ("float32", [m["out"]], m["scale"].tobytes())})
+            progs.append((p, m["q"].reshape(-1).view(np.uint8), np.empty(m["out"] * m["in"] * 2, np.uint8)))
+        t0, n = time.perf_counter(), 0
+        while n < 1 or (time.perf_counter() - t0 < cpu_seconds and n < 10):
+            for p, src, dst in progs:
+                p.execute_into(src, dst, pool=pool)
+            n += 1
+        line["cpu_baseline"] = {"value": n / (time.perf_counter() - t0), "unit": "layers/s", "cores": pool.threads,
+                                "kind": "reference", "sample": f"one Llama-7B layer x{n}"}
+    res.close()
+    return line
+
+
+def run_extras():
+    """Configs 1-4 in brief beside the headline line (one GPU, about a
+    minute): each one's kernel roofline fraction, e2e rate and fraction of
+    the pinned-memcpy ceiling, and the reference CPU rate."""
+    out = {}
+    for name in ("c1", "c2", "c3q", "c3d"):
+        try:
+            line = measure_config(name, steps=10, warmup=3, cpu_seconds=2.0, cpu_8_threads=False)
+            out[name] = {"workload": line["config"]["workload"], "value": line["value"], "unit": line["unit"],
+                         "kernel_frac": line["roofline"]["frac"], "kernel": line["roofline"]["kernel"],
+                         "e2e": line["e2e"]["value"],
+                         "e2e_pct_of_pinned_memcpy": line["e2e"]["pct_of_pinned_memcpy"],
+                         "cpu_baseline": (line.get("cpu_baseline") or {}).get("value"),
+                         "clocks_sm_mhz": line["clocks"].get("sm_mhz")}
+        except Exception as e:  # reported, not hidden: the headline line still stands
+            out[name] = {"error": f"{type(e).__name__}: {e}"}
+    try:
+        out["c4"] = measure_c4()
+    except Exception as e:
+        out["c4"] = {"error": f"{type(e).__name__}: {e}"}
+    return out
 
 
 LATENCY_CASES = (  # the cases of the reference's typed H2D latency table (bench/results/typed-h2d-221)
@@ -913,7 +1192,12 @@ def main():
                         help="N>1: peer (int8 shards read over NVLink by every rank's kernel) or allgather "
                              "(f16 result rows all-gathered by NCCL)")
     parser.add_argument("--balance", type=int, default=1,
-                        help="N>1 peer: size shards by each rank's concurrent PCIe bandwidth (1) or equally (0)")
+                        help="N>1 peer: size shards by each rank's sustained concurrent H2D bandwidth (1) or "
+                             "equally (0)")
+    parser.add_argument("--gpu-map", default="identity", choices=["identity", "halves"],
+                        help="rank -> GPU: identity, or alternate between the two halves of the visible GPUs")
+    parser.add_argument("--extras", type=int, default=1,
+                        help="N=1 headline run: also measure configs 1-4 in brief (about a minute)")
     args = parser.parse_args()
     if args.warmup < 3:
         args.warmup = 3
