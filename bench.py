@@ -316,7 +316,10 @@ def run_ours(args):
         dist.all_gather_object(out, obj)
         return out
 
-    res = pyreloc.DispatchResources()
+    # A retained quota that holds the ring (4 x 16 MiB) and the parameters, so
+    # blocking calls keep their scratch between matrices (the reference's
+    # 64 MiB default would release and re-allocate it after every call).
+    res = pyreloc.DispatchResources(max_retained_bytes=256 << 20)
     _, compute_s = res.streams(gpu_index)
     compute_stream = torch.cuda.ExternalStream(compute_s, device=dev)
 
