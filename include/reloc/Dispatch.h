@@ -152,6 +152,18 @@ int executionDevice(const DispatchRequest &request);
 /// options.asyncCompletion. Marks the request consumed before launching.
 std::optional<TransferError> executeDispatch(DispatchRequest &request, CudaBackend &backend,
                                              const TransferOptions &options);
+/// The reference's signature (Dispatch.h:269): every B200 row needs a
+/// CudaBackend; any other CopyBackend gets backend_mismatch before any work
+/// (the request stays unconsumed).
+std::optional<TransferError> executeDispatch(DispatchRequest &request, CopyBackend &backend,
+                                             const TransferOptions &options);
+
+/// A layout-only (wire v0) bound plan as a stage-free dispatch template: the
+/// source is the dense 1-D span the plan reads (its element 0 is the view's
+/// element 0), the result the dense padded destination. Used by
+/// executeTransfer and by the C-ABI's layout transfers.
+std::variant<DispatchTemplate, TransferError> prepareTransferTemplate(const BoundPlan &bound,
+                                                                      TransferDirection direction);
 
 /// Execute the physical row window [rowBegin, rowEnd) of axis 0 of the
 /// padded result (a shard of the result, e.g. one GPU's rows of a sharded

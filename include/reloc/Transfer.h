@@ -5,10 +5,14 @@
 #ifndef SYM_B200_RELOC_TRANSFER_H
 #define SYM_B200_RELOC_TRANSFER_H
 
+#include "reloc/Backend.h"
+#include "reloc/Bind.h"
+
 #include <cstddef>
 #include <cstdint>
 #include <optional>
 #include <string>
+#include <variant>
 #include <vector>
 
 namespace reloc {
@@ -73,6 +77,51 @@ struct TransferOptions {
   /// establish through that stream. Default: block until complete.
   bool asyncCompletion = false;
 };
+
+// ---- layout-only (wire v0) transfers ------------------------------------------
+// The reference's validated forward-transfer API (libreloc/include/reloc/
+// Transfer.h:100-200), kept with its names, signatures and error codes so C++
+// callers compile unchanged. Execution is the B200 executor's: the bound
+// layout plan runs as a stage-free fused kernel on a CudaBackend (host-to-
+// device through the HBM DMA ring, device-to-host through the result-row
+// ring); any other backend gets `backend_mismatch`.
+
+/// A validated request; owns copies of the plan and both views. Single-use.
+struct TransferRequest {
+  BoundPlan bound;
+  BufferView source;
+  BufferView destination;
+  TransferDirection direction = TransferDirection::HostToDevice;
+  size_t sourceSpanBytes = 0;  // bytes the plan may read from the source's element 0
+  size_t destinationBytes = 0; // == bound.totalBytes
+  bool consumed = false;
+};
+
+/// Bytes a view addresses, elementSize * (1 + sum((extent - 1) * stride)),
+/// after rejecting null, empty, negative-stride, broadcast (stride 0) and
+/// overlapping views and checking the capacity; every step overflow-checked.
+std::variant<size_t, TransferError> viewSpanBytes(const BufferView &view, const char *role);
+
+/// The source half of validateTransfer: the view is admissible for the
+/// direction and every source read of the plan lies inside it. Returns the
+/// source span in bytes.
+std::variant<size_t, TransferError> validateTransferSource(const BoundPlan &bound, const BufferView &source,
+                                                           TransferDirection direction);
+
+/// Full validation: the source as above, a dense row-major destination of
+/// exactly bound.totalBytes that holds every plan write, both capacities.
+std::variant<TransferRequest, TransferError> validateTransfer(const BoundPlan &bound, const BufferView &source,
+                                                              const BufferView &destination,
+                                                              TransferDirection direction);
+
+/// Execute a validated request and block until its work completed (no
+/// device-wide synchronization). The request is re-validated (its public
+/// fields may have changed) and marked consumed before any work; a consumed
+/// request fails with already_executed. `backend` must be a CudaBackend
+/// (backend_mismatch otherwise) of the device end's ordinal
+/// (device_mismatch otherwise). Errors are returned, never thrown.
+std::optional<TransferError> executeTransfer(TransferRequest &request, CopyBackend &backend,
+                                             const TransferOptions &options);
 
 
 } // namespace reloc

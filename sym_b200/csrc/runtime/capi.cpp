@@ -460,31 +460,7 @@ int sb_prepare_dispatch_template(const sb_bound *b, int32_t direction, int32_t p
 int sb_prepare_transfer_template(const sb_bound *b, sb_template **out, sb_error *err) {
   if (b->typed)
     return setErr(err, "typed_unsupported", "layout transfers take a layout-only (v0) bound plan");
-  const BoundPlan &l = b->layout;
-  if (l.padRegions.size() > 1)
-    for (const PadRegion &p : l.padRegions)
-      if (p.fillBits != l.padRegions.front().fillBits)
-        return setErr(err, "mixed_fills_unsupported", "v0 plans carry a single fill value");
-  // The plan as a stage-free typed program: a dense 1-D source of the plan's
-  // source span, a dense 1-D result of its padded element count.
-  TypedBoundPlan t;
-  t.layout = l;
-  const ElementType et{ElementTypeKind::Integer, l.elementSize * 8};
-  int64_t span = 1;
-  for (size_t k = 0; k < l.extents.size(); ++k)
-    span += (l.extents[k] - 1) * l.srcStrides[k];
-  t.sourceExtents = {span};
-  t.resultExtents = {l.totalBytes / static_cast<int64_t>(l.elementSize)};
-  t.sourceType = t.resultType = et;
-  for (const PadRegion &p : l.padRegions)
-    t.fills.push_back(TypedFill{static_cast<uint32_t>(p.axis), 0, et, p.fillBits});
-  t.cuts.push_back(StageFootprint{0, et, t.resultExtents[0], l.totalBytes});
-  t.sourceBytes = span * l.elementSize;
-  t.destinationBytes = l.totalBytes;
-  t.requirements = {"layout_transfer"};
-  dispatch::Options o;
-  o.cuda = true;
-  auto r = dispatch::prepareDispatchTemplate(t, TransferDirection::HostToDevice, o);
+  auto r = dispatch::prepareTransferTemplate(b->layout, TransferDirection::HostToDevice);
   if (auto *e = std::get_if<TransferError>(&r))
     return setErr(err, e->code, e->message);
   *out = new sb_template{std::get<dispatch::DispatchTemplate>(std::move(r))};

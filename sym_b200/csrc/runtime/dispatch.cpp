@@ -337,6 +337,45 @@ std::optional<TransferError> executeDispatch(DispatchRequest &req, CudaBackend &
                 nullptr, timed || b.copyCalls != copies0);
 }
 
+std::optional<TransferError> executeDispatch(DispatchRequest &req, CopyBackend &backend, const TransferOptions &o) {
+  auto *cuda = dynamic_cast<CudaBackend *>(&backend);
+  if (!cuda)
+    return terr("backend_mismatch", "row " + req.selected.label() + " needs a CudaBackend");
+  return executeDispatch(req, *cuda, o);
+}
+
+std::variant<DispatchTemplate, TransferError> prepareTransferTemplate(const BoundPlan &l,
+                                                                      TransferDirection direction) {
+  if (l.typed)
+    return terr("typed_unsupported", "layout transfers take a layout-only (v0) bound plan");
+  if (l.extents.empty() || l.extents.size() != l.srcStrides.size() || l.extents.size() != l.dstStrides.size())
+    return terr("plan_mismatch", "bound plan has inconsistent axes");
+  if (l.padRegions.size() > 1)
+    for (const PadRegion &p : l.padRegions)
+      if (p.fillBits != l.padRegions.front().fillBits)
+        return terr("mixed_fills_unsupported", "v0 plans carry a single fill value");
+  // The plan as a stage-free typed program: a dense 1-D source of the plan's
+  // source span, a dense 1-D result of its padded element count.
+  TypedBoundPlan t;
+  t.layout = l;
+  const ElementType et{ElementTypeKind::Integer, l.elementSize * 8};
+  int64_t span = 1;
+  for (size_t k = 0; k < l.extents.size(); ++k)
+    span += (l.extents[k] - 1) * l.srcStrides[k];
+  t.sourceExtents = {span};
+  t.resultExtents = {l.totalBytes / static_cast<int64_t>(l.elementSize)};
+  t.sourceType = t.resultType = et;
+  for (const PadRegion &p : l.padRegions)
+    t.fills.push_back(TypedFill{static_cast<uint32_t>(p.axis), 0, et, p.fillBits});
+  t.cuts.push_back(StageFootprint{0, et, t.resultExtents[0], l.totalBytes});
+  t.sourceBytes = span * l.elementSize;
+  t.destinationBytes = l.totalBytes;
+  t.requirements = {"layout_transfer"};
+  Options o;
+  o.cuda = true;
+  return prepareDispatchTemplate(t, direction, o);
+}
+
 std::optional<TransferError> executeSourceRows(const DispatchTemplate &t, CudaBackend &b, const void *rows,
                                                int64_t rowBegin, int64_t rowEnd, void *dst, const TransferOptions &o,
                                                Report &rep) {
