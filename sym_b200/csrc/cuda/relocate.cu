@@ -1278,6 +1278,25 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
 
+/// Raise the phase's expected transaction bytes without arriving.
+__device__ __forceinline__ void mbar_expect_tx_only(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+               : "memory");
+}
+
+/// 4-byte asynchronous global -> shared copy (tracked per thread).
+__device__ __forceinline__ void cp_async4(void *dst_smem, const void *src_global) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(dst_smem)),
+               "l"(__cvta_generic_to_global(src_global))
+               : "memory");
+}
+
+/// This thread's arrival on `bar`, made once all its earlier cp.async copies
+/// completed (the barrier's expected count includes it: no increment).
+__device__ __forceinline__ void cp_async_arrive(uint64_t *bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
 __device__ __forceinline__ uint64_t global_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -1348,10 +1367,10 @@ __global__ void __launch_bounds__(KTmaThreads, SBC_TMA_CTAS_PER_SM) k_tma_tile(c
   static_assert(WS == 1 || CH_ON == 0, "32-bit tiles carry no parameters");
   extern __shared__ __align__(1024) uint8_t dyn[];
   __shared__ __align__(8) uint64_t full[KStages], empty[KStages];
-  // Per-column dequantize parameters of the tile in each stage (CH_ON == 2).
+  // Per-column dequantize parameters of the tile in each stage (CH_ON == 2):
+  // scales, and zero points when they are per channel.
   __shared__ __align__(16) float s_scale[KStages][64];
-  __shared__ __align__(16) float s_bias[KStages][64];
-  __shared__ int s_bad[KStages];
+  __shared__ __align__(16) int32_t s_zp[KStages][64];
   __shared__ int timed_out;
   uint8_t *stage0 = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(dyn) + 1023) & ~uintptr_t(1023));
   const int t = threadIdx.x;
@@ -1385,71 +1404,60 @@ __global__ void __launch_bounds__(KTmaThreads, SBC_TMA_CTAS_PER_SM) k_tma_tile(c
     const int lane = t - KTmaConsumers;
     if (lane < srcs.n)
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&srcs.map[lane])) : "memory");
-    // This lane's two parameter columns of a tile, loaded one tile ahead so
-    // the global-load latency overlaps the wait for a free stage.
-    float p_scale[2], p_bias[2];
-    bool p_bad = false;
-    auto load_params = [&](uint32_t k) {
-      if constexpr (CH_ON == 2) {
-        const uint32_t job = blockIdx.x + k * G;
-        if (job >= tiles)
-          return;
-        uint32_t ta, tb;
-        tile_of(job, ord, ta, tb);
-        p_bad = false;
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          int64_t ch = d.box_lo[1] + static_cast<int64_t>(tb) * TB + lane + 32 * h;
-          if (ch >= s.channel_length) {
-            p_bad = true;
-            ch = 0;
-          }
-          p_scale[h] = s.param[ch];
-          p_bias[h] = 8388736.0f + static_cast<float>(zp_of(s, ch));
-        }
-      }
-    };
-    load_params(0);
-    for (uint32_t k = 0;; ++k) {
+    uint32_t k = 0;
+    for (;; ++k) {
       const uint32_t job = blockIdx.x + k * G;
       if (job >= tiles)
         break;
       const int st = k % KStages;
       if (k >= KStages && !mbar_wait(&empty[st], (k / KStages - 1) & 1, ctl.wait_ns)) {
         fail();
-        if (lane == 0)
-          drain(k - KStages, k);
+        drain(k - KStages, k); // every lane: its own parameter copies land before it leaves
         return;
-      }
-      // Every lane writes its parameters before its own arrival (lane 0's is
-      // the expect_tx), so the phase completes only after all of them.
-      if constexpr (CH_ON == 2) {
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          s_scale[st][param_slot(lane + 32 * h)] = p_scale[h];
-          s_bias[st][param_slot(lane + 32 * h)] = p_bias[h];
-        }
-        const bool bad = __any_sync(0xffffffffu, p_bad);
-        if (lane == 0)
-          s_bad[st] = bad;
       }
       if (job == ctl.withhold_job) {
         // test hook: neither the copy nor any arrival, so this tile's
         // consumers run out of their bounded wait
-      } else if (lane == 0) {
-        uint32_t ta, tb;
-        tile_of(job, ord, ta, tb);
+        continue;
+      }
+      uint32_t ta, tb;
+      tile_of(job, ord, ta, tb);
+      if constexpr (CH_ON == 2) {
+        // This lane's two parameter columns go straight from global to the
+        // stage's shared slots by cp.async, and its arrival on `full` is
+        // made when they have landed: the producer never waits for a global
+        // load. Columns past the table read entry 0 (the consumers flag the
+        // tile).
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          int64_t ch = d.box_lo[1] + static_cast<int64_t>(tb) * TB + lane + 32 * h;
+          if (ch >= s.channel_length)
+            ch = 0;
+          cp_async4(&s_scale[st][param_slot(lane + 32 * h)], s.param + ch);
+          if (s.zp_mode == 2)
+            cp_async4(&s_zp[st][param_slot(lane + 32 * h)], s.zero_point + ch);
+        }
+      }
+      if (lane == 0) {
         int j = 0; // the source holding b-tile tb
         while (j + 1 < srcs.n && tb >= srcs.tb_first[j + 1])
           ++j;
-        mbar_expect_tx(&full[st], KTmaTileBytes); // lane 0's arrival
+        if constexpr (CH_ON == 2)
+          mbar_expect_tx_only(&full[st], KTmaTileBytes); // lane 0 arrives below, with the other lanes
+        else
+          mbar_expect_tx(&full[st], KTmaTileBytes); // lane 0's arrival
         tma_load_3d(stage0 + st * KTmaTileBytes, &srcs.map[j], static_cast<int32_t>(ta * TA),
                     static_cast<int32_t>((tb - srcs.tb_first[j]) * (TB / GR)), 0, &full[st]);
-      } else {
-        mbar_arrive(&full[st]);
       }
-      load_params(k + 1);
+      if constexpr (CH_ON == 2)
+        cp_async_arrive(&full[st]); // once this lane's parameter copies landed
+      else if (lane != 0)
+        mbar_arrive(&full[st]);
     }
+    // A lane leaves only after its parameter copies of the last tiles landed
+    // (the stage's phase completes after every lane's copies).
+    if constexpr (CH_ON == 2)
+      drain(k > KStages ? k - KStages : 0, k);
     return;
   }
 
@@ -1458,11 +1466,16 @@ __global__ void __launch_bounds__(KTmaThreads, SBC_TMA_CTAS_PER_SM) k_tma_tile(c
   const int64_t Da = d.dst_strides[0], DaB = Da * WD;
   uint8_t *const dst0 = static_cast<uint8_t *>(d.dst) - d.dst_offset * WD;
   float ps[VD], bias[VD];
+  // 2^23 + 128 + zero point: the int8 -> f32 conversion's bias; the same for
+  // every column unless the zero points are per channel.
+  float bias_all = 0.0f;
+  if constexpr (WS == 1)
+    bias_all = 8388736.0f + static_cast<float>(s.zp_mode == 1 ? s.zero_point[0] : 0);
   if constexpr (WS == 1 && CH_ON == 0) {
 #pragma unroll
     for (int j = 0; j < VD; ++j) {
       ps[j] = s.param[0];
-      bias[j] = 8388736.0f + static_cast<float>(zp_of(s, 0));
+      bias[j] = bias_all;
     }
   }
   for (uint32_t k = 0;; ++k) {
@@ -1476,20 +1489,29 @@ __global__ void __launch_bounds__(KTmaThreads, SBC_TMA_CTAS_PER_SM) k_tma_tile(c
         drain(k, k + KStages);
       return;
     }
+    uint32_t ta, tb;
+    tile_of(job, ord, ta, tb);
     bool ok = true;
     if constexpr (CH_ON == 2) {
       const int lo = param_slot(c * VD), hi = param_slot(c * VD + 4);
       const float4 s0 = *reinterpret_cast<const float4 *>(&s_scale[st][lo]);
       const float4 s1 = *reinterpret_cast<const float4 *>(&s_scale[st][hi]);
-      const float4 b0v = *reinterpret_cast<const float4 *>(&s_bias[st][lo]);
-      const float4 b1v = *reinterpret_cast<const float4 *>(&s_bias[st][hi]);
       ps[0] = s0.x, ps[1] = s0.y, ps[2] = s0.z, ps[3] = s0.w, ps[4] = s1.x, ps[5] = s1.y, ps[6] = s1.z, ps[7] = s1.w;
-      bias[0] = b0v.x, bias[1] = b0v.y, bias[2] = b0v.z, bias[3] = b0v.w;
-      bias[4] = b1v.x, bias[5] = b1v.y, bias[6] = b1v.z, bias[7] = b1v.w;
-      ok = !s_bad[st];
+      if (s.zp_mode == 2) {
+        const int4 z0 = *reinterpret_cast<const int4 *>(&s_zp[st][lo]);
+        const int4 z1 = *reinterpret_cast<const int4 *>(&s_zp[st][hi]);
+        const int z[VD] = {z0.x, z0.y, z0.z, z0.w, z1.x, z1.y, z1.z, z1.w};
+#pragma unroll
+        for (int j = 0; j < VD; ++j)
+          bias[j] = 8388736.0f + static_cast<float>(z[j]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < VD; ++j)
+          bias[j] = bias_all;
+      }
+      // a column past the parameter table (its copy read entry 0) flags the tile
+      ok = d.box_lo[1] + static_cast<int64_t>(tb) * TB + (TB - 1) < s.channel_length;
     }
-    uint32_t ta, tb;
-    tile_of(job, ord, ta, tb);
     const int64_t a0 = d.box_lo[0] + static_cast<int64_t>(ta) * TA;
     const int64_t b0 = d.box_lo[1] + static_cast<int64_t>(tb) * TB;
     const uint8_t *sp = stage0 + st * KTmaTileBytes;
@@ -1549,19 +1571,23 @@ __global__ void __launch_bounds__(KTmaThreads, SBC_TMA_CTAS_PER_SM) k_tma_tile(c
           bias[j] = bi;
         }
       }
-      float f[VD];
-#pragma unroll
-      for (int j = 0; j < VD; ++j)
-        f[j] = __fmul_rn(__fsub_rn(__int_as_float(__byte_perm(w[j], 0x4B000000u, 0x7650 + i)), bias[j]), ps[j]);
+      // Two columns at a time on the packed f32x2 pipe: (x - bias) then
+      // * scale, each an IEEE round-to-nearest-even operation per lane (the
+      // same results as the scalar __fsub_rn / __fmul_rn, half the
+      // instructions).
       uint4 out;
       uint32_t *u = reinterpret_cast<uint32_t *>(&out);
 #pragma unroll
       for (int j = 0; j < VD; j += 2) {
+        const float2 x = make_float2(__int_as_float(__byte_perm(w[j], 0x4B000000u, 0x7650 + i)),
+                                     __int_as_float(__byte_perm(w[j + 1], 0x4B000000u, 0x7650 + i)));
+        const float2 f = __fmul2_rn(__fadd2_rn(x, make_float2(-bias[j], -bias[j + 1])),
+                                    make_float2(ps[j], ps[j + 1]));
         if constexpr (CHAIN == CH_DQ_BF16) {
-          const __nv_bfloat162 h = __floats2bfloat162_rn(f[j], f[j + 1]);
+          const __nv_bfloat162 h = __floats2bfloat162_rn(f.x, f.y);
           u[j / 2] = *reinterpret_cast<const uint32_t *>(&h);
         } else {
-          const __half2 h = __floats2half2_rn(f[j], f[j + 1]);
+          const __half2 h = __floats2half2_rn(f.x, f.y);
           u[j / 2] = *reinterpret_cast<const uint32_t *>(&h);
         }
       }
