@@ -542,6 +542,15 @@ class DispatchResources:
         err = SbError()
         if acquire_timeout_ms is not None and int(acquire_timeout_ms) < 0:
             raise ValueError("acquire_timeout_ms must be None or non-negative")
+        # Caps that a context here meets by construction (2 streams, one
+        # context per device, no background transform workers): only their
+        # range is checked.
+        for name, value, least in (("max_streams", max_streams, 2), ("max_contexts_per_device",
+                                                                     max_contexts_per_device, 1),
+                                   ("max_background_workers", max_background_workers, 1), ("max_contexts",
+                                                                                           max_contexts, 1)):
+            if int(value) < least:
+                raise ValueError(f"{name} must be at least {least} on this executor")
         _native.lib().sb_resources_create(int(max_retained_bytes), int(max_live_bytes or 0), int(max_contexts),
                                           ctypes.byref(out), ctypes.byref(err))
         self.handle = out

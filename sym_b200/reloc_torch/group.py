@@ -1,20 +1,18 @@
-"""Consumer-sized transfer groups (reference ``reloc_torch.group``,
-libreloc/python/reloc_torch/group.py:41-147).
+"""Consumer-sized transfer groups: the API of the reference's
+``reloc_torch.group`` (libreloc/python/reloc_torch/group.py:41-147 -- the
+names, fields and error messages below are that interface).
 
-A group holds 1..256 fresh typed preparations for one CUDA device. Executing
-it allocates every output, validates all members together at the native
-boundary (``pyreloc.prepare_dispatch_group``: one device, no destination
-aliasing another destination or any source) and then runs all members behind
-ONE wait on the caller's current stream with ONE completion: on the B200 the
-members' DMA chunks and kernels queue back to back on the context's copy and
-compute streams, so a layer's seven matrices cost one caller-stream round
-trip instead of seven. Any failure consumes the whole group; members are
-never retried.
+On this executor a group is one native dispatch group
+(``pyreloc.prepare_dispatch_group`` / ``execute_dispatch_group``): its
+members' DMA chunks and fused kernels queue back to back on one device
+context's copy and compute streams, after ONE wait on the caller's stream,
+and complete through ONE event. A layer's seven weight matrices therefore
+cost one caller-stream round trip instead of seven. Any failure consumes the
+whole group; members are never retried.
 """
 from __future__ import annotations
 
 import operator
-from contextlib import ExitStack
 from dataclasses import dataclass, field
 from threading import Lock
 from types import MappingProxyType
@@ -36,7 +34,7 @@ class PreparedTransferGroup:
     @property
     def destinations(self):
         """One output descriptor per member, in member order."""
-        return tuple(r.destination for r in self.requests)
+        return tuple(member.destination for member in self.requests)
 
 
 @dataclass(frozen=True)
@@ -46,92 +44,119 @@ class GroupResult:
     report: MappingProxyType
 
 
+def _member_device(member):
+    """The canonical CUDA device of one fresh typed member."""
+    import torch
+
+    if not isinstance(member, PreparedTypedTransfer):
+        raise TypeError("group members must be prepared typed transfers")
+    if member.consumed:
+        raise RuntimeError("group member was already executed")
+    if member.template is None:
+        raise ValueError("typed group members require an immutable dispatch template")
+    device = torch.device(member.device)
+    if device.type != "cuda" or device.index is None:
+        raise ValueError("group members need a canonical CUDA device")
+    return device
+
+
 def prepare_transfer_group(requests):
     """Group fresh typed preparations that target one CUDA device. Launches
     nothing; the group owns its members from here on."""
-    import torch
-
-    requests = tuple(requests)
-    if not 1 <= len(requests) <= MAX_MEMBERS:
+    members = tuple(requests)
+    if not 1 <= len(members) <= MAX_MEMBERS:
         raise ValueError(f"a group must contain between 1 and {MAX_MEMBERS} requests")
-    if len({id(r) for r in requests}) != len(requests):
+    if len(set(map(id, members))) != len(members):
         raise ValueError("a request cannot occur twice in a group")
-    device = None
-    for r in requests:
-        if not isinstance(r, PreparedTypedTransfer):
-            raise TypeError("group members must be prepared typed transfers")
-        if r.consumed:
-            raise RuntimeError("group member was already executed")
-        if r.template is None:
-            raise ValueError("typed group members require an immutable dispatch template")
-        here = torch.device(r.device)
-        if here.type != "cuda" or here.index is None:
-            raise ValueError("group members need a canonical CUDA device")
-        if device is not None and here != device:
-            raise ValueError("group members must use the same CUDA device")
-        device = here
-    return PreparedTransferGroup(requests, device)
+    devices = {_member_device(m) for m in members}
+    if len(devices) != 1:
+        raise ValueError("group members must use the same CUDA device")
+    return PreparedTransferGroup(members, devices.pop())
 
 
-def execute_transfer_group(group, *, resources=None, gather_threads=8, gather_pool=None, pinning="auto",
-                           min_pinned_bytes=None, max_scratch_bytes=64 << 20):
-    """Complete one group (blocking for the host: outputs are ready on return)."""
-    return _execute_transfer_group(group, resources=resources, gather_threads=gather_threads,
-                                   gather_pool=gather_pool, pinning=pinning, min_pinned_bytes=min_pinned_bytes,
-                                   max_scratch_bytes=max_scratch_bytes)
+class _Claim:
+    """Exclusive use of a group and of each of its members for one
+    execution: all of them are claimed, or none (a partial claim is given
+    back before the error propagates)."""
+
+    def __init__(self, group):
+        self._locks = [group._execution_lock, *(m._execution_lock for m in group.requests)]
+        self._items = [group, *group.requests]
+        self._held = []
+
+    def __enter__(self):
+        for lock, item in zip(self._locks, self._items):
+            if not lock.acquire(blocking=False):
+                self.__exit__()
+                raise RuntimeError("group or member is already executing")
+            self._held.append(lock)
+            if item.consumed:
+                self.__exit__()
+                raise RuntimeError("group or member was already executed")
+        return self
+
+    def __exit__(self, *exc):
+        while self._held:
+            self._held.pop().release()
+        return False
 
 
-def _execute_transfer_group(group, *, resources=None, gather_threads=8, gather_pool=None, pinning="auto",
-                            min_pinned_bytes=None, max_scratch_bytes=64 << 20, submit=False):
-    """Allocate the outputs, validate and run the group. ``submit``: return
-    ``(DispatchCompletion, outputs, descriptors)`` without waiting."""
-    import torch
-
+def _checked_options(group, resources, gather_threads, max_scratch_bytes):
     from .resources import TransferResources
 
     if not isinstance(group, PreparedTransferGroup):
         raise TypeError("group must be a PreparedTransferGroup")
-    max_scratch_bytes = operator.index(max_scratch_bytes)
-    if not 0 < max_scratch_bytes < 1 << 64:
+    scratch = operator.index(max_scratch_bytes)
+    if not 0 < scratch < 1 << 64:
         raise ValueError("max_scratch_bytes must be positive and fit size_t")
     if not 0 < operator.index(gather_threads) < 1 << 31:
         raise ValueError("gather_threads must be positive and fit a native int")
     if resources is not None and not isinstance(resources, TransferResources):
         raise TypeError("resources must be TransferResources or None")
-    owner = None if resources is None else resources.native_typed
-    with ExitStack() as locks:
-        for item in (group, *group.requests):
-            if not item._execution_lock.acquire(blocking=False):
-                raise RuntimeError("group or member is already executing")
-            locks.callback(item._execution_lock.release)
-            if item.consumed:
-                raise RuntimeError("group or member was already executed")
-        for r in group.requests:  # stale sources / parameters fail before any allocation
-            r.recheck()
+    return scratch, None if resources is None else resources.native_typed
+
+
+def execute_transfer_group(group, *, resources=None, gather_threads=8, gather_pool=None, pinning="auto",
+                           min_pinned_bytes=None, max_scratch_bytes=64 << 20):
+    """Complete one group (blocking for the host: outputs are ready on return).
+    The host-worker knobs of the reference are accepted and unused: no member
+    is transformed on the CPU."""
+    return _execute_transfer_group(group, resources=resources, gather_threads=gather_threads,
+                                   max_scratch_bytes=max_scratch_bytes)
+
+
+def _execute_transfer_group(group, *, resources=None, gather_threads=8, gather_pool=None, pinning="auto",
+                            min_pinned_bytes=None, max_scratch_bytes=64 << 20, submit=False):
+    """Allocate the outputs, validate the members together at the native
+    boundary and run them as one native group. ``submit``: return
+    ``(DispatchCompletion, outputs, descriptors)`` without waiting."""
+    import torch
+
+    scratch, owner = _checked_options(group, resources, gather_threads, max_scratch_bytes)
+    with _Claim(group):
+        # stale sources or parameters fail here, before anything is allocated
+        for member in group.requests:
+            member.recheck()
         descriptors = group.destinations
         outputs = tuple(torch.empty_strided(d.shape, d.strides, dtype=getattr(torch, d.dtype), device=d.device)
                         for d in descriptors)
-        entries = [(r.template, r.source_view, storage_view(out, "cuda", out.device.index), "h2d")
-                   for r, out in zip(group.requests, outputs)]
-        try:
-            native = pyreloc.prepare_dispatch_group(entries)
-        except pyreloc.TransferError as error:
-            raise RuntimeError(f"transfer group rejected: {error}") from error
+        native = pyreloc.prepare_dispatch_group(
+            [(m.template, m.source_view, storage_view(o, "cuda", o.device.index), "h2d")
+             for m, o in zip(group.requests, outputs)])
+        # From here the group is spent, whatever happens next.
         group.native = native
-        group.consumed = True
-        for r in group.requests:
-            r.consumed = True
-        stream = torch.cuda.current_stream(group.device).cuda_stream
-        owners = (tuple(r.source for r in group.requests), outputs)
-        run = pyreloc.submit_dispatch_group if submit else pyreloc.execute_dispatch_group
+        for item in (group, *group.requests):
+            item.consumed = True
+        launch = pyreloc.submit_dispatch_group if submit else pyreloc.execute_dispatch_group
         try:
-            result = run(native, caller_stream=stream, resources=owner, owners=owners,
-                         max_scratch_bytes=max_scratch_bytes)
+            outcome = launch(native, caller_stream=torch.cuda.current_stream(group.device).cuda_stream,
+                             resources=owner, max_scratch_bytes=scratch,
+                             owners=(tuple(m.source for m in group.requests), outputs))
         except pyreloc.TransferError as error:
             raise RuntimeError(f"transfer group failed: {error}") from error
     if submit:
-        return result, outputs, descriptors
-    return GroupResult(outputs, descriptors, MappingProxyType(dict(result)))
+        return outcome, outputs, descriptors
+    return GroupResult(outputs, descriptors, MappingProxyType(dict(outcome)))
 
 
 __all__ = ("GroupResult", "PreparedTransferGroup", "execute_transfer_group", "prepare_transfer_group")
