@@ -23,6 +23,7 @@ from __future__ import annotations
 import argparse
 import hashlib
 import json
+import os
 import sys
 from pathlib import Path
 
@@ -87,7 +88,10 @@ def layout_corpus(corpus: Path):
 
 def main():
     parser = argparse.ArgumentParser()
-    parser.add_argument("--reference", default="/root/reference")
+    parser.add_argument("--reference",
+                        default=os.environ.get("SYM_REFERENCE_DIR", str(HERE.parent.parent.parent / "reference")),
+                        help="the reference checkout ($SYM_REFERENCE_DIR, else a `reference` directory beside "
+                             "the repository)")
     args = parser.parse_args()
     corpus = Path(args.reference) / "libreloc" / "test" / "corpus"
     (HERE / "typed_corpus.json").write_text(json.dumps(typed_corpus(corpus), indent=1) + "\n")
