@@ -1197,8 +1197,10 @@ def main():
     parser.add_argument("--balance", type=int, default=1,
                         help="N>1 peer: size shards by each rank's sustained concurrent H2D bandwidth (1) or "
                              "equally (0)")
-    parser.add_argument("--gpu-map", default="identity", choices=["identity", "halves"],
-                        help="rank -> GPU: identity, or alternate between the two halves of the visible GPUs")
+    parser.add_argument("--gpu-map", default="halves", choices=["identity", "halves"],
+                        help="rank -> GPU: alternate between the two halves of the visible GPUs (default; on the "
+                             "pool's 8-GPU boxes GPUs 0-3 and 4-7 sit behind different host bridges: N=4 measured "
+                             "224 layers/s against 134 with identity), or identity")
     parser.add_argument("--extras", type=int, default=1,
                         help="N=1 headline run: also measure configs 1-4 in brief (about a minute)")
     args = parser.parse_args()
