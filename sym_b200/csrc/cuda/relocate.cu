@@ -1328,12 +1328,43 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint64
   }
 }
 
+// Cache-policy tuning points of k_tma_tile: SBC_TMA_LOAD_EVICT_FIRST = 1
+// marks the source boxes evict-first in L2 (they are read once);
+// SBC_TMA_STORE = 0 streaming stores (st.global.cs), 1 L2-only (.cg),
+// 2 write-back (default policy).
+#ifndef SBC_TMA_LOAD_EVICT_FIRST
+#define SBC_TMA_LOAD_EVICT_FIRST 0
+#endif
+#ifndef SBC_TMA_STORE
+#define SBC_TMA_STORE 0
+#endif
+
 __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, int32_t x, int32_t y, int32_t z,
                                             uint64_t *bar) {
+#if SBC_TMA_LOAD_EVICT_FIRST
+  uint64_t policy;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
+  asm volatile("cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+               " [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(smem_addr(dst)),
+               "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_addr(bar)), "l"(policy)
+               : "memory");
+#else
   asm volatile("cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
                " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_addr(dst)),
                "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_addr(bar))
                : "memory");
+#endif
+}
+
+/// A 16-byte result store of k_tma_tile (policy: SBC_TMA_STORE).
+__device__ __forceinline__ void tma_out_store(uint4 *p, uint4 v) {
+#if SBC_TMA_STORE == 1
+  __stcg(p, v);
+#elif SBC_TMA_STORE == 2
+  *p = v;
+#else
+  __stcs(p, v);
+#endif
 }
 
 /// Tensor maps of the sources of one k_tma_tile launch: source j (a block of
@@ -1591,7 +1622,7 @@ __global__ void __launch_bounds__(KTmaThreads, SBC_TMA_CTAS_PER_SM) k_tma_tile(c
           u[j / 2] = *reinterpret_cast<const uint32_t *>(&h);
         }
       }
-      __stcs(reinterpret_cast<uint4 *>(dp), out);
+      tma_out_store(reinterpret_cast<uint4 *>(dp), out);
     }
     if (!ok)
       flag(d);
