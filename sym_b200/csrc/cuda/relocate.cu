@@ -1929,6 +1929,11 @@ bool basic_ok(const sbc_relocate &d) {
 #ifndef SBC_NARROW_VMAX
 #define SBC_NARROW_VMAX 2
 #endif
+// SBC_NARROW_BALANCED = 1: size the span grid so every warp takes the same
+// number of spans instead of filling every resident slot.
+#ifndef SBC_NARROW_BALANCED
+#define SBC_NARROW_BALANCED 0
+#endif
 
 
 template <int WS, int WD, int CH>
@@ -1946,8 +1951,18 @@ int launch_narrow(const sbc_relocate &d, int nb, int64_t per_batch, int64_t tota
     int per_sm = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, 256, 0) != cudaSuccess || per_sm < 1)
       per_sm = 1;
-    const int64_t want = (total / (32 * v) + 7) / 8, cap = static_cast<int64_t>(sm_count()) * per_sm;
+    const int64_t spans = total / (32 * v), cap = static_cast<int64_t>(sm_count()) * per_sm;
+#if SBC_NARROW_BALANCED
+    // As many rounds of spans as the resident grid needs, then just enough
+    // warps that every warp takes that many: no last round with a third of
+    // the warps idle.
+    const int64_t rounds = (spans + cap * 8 - 1) / (cap * 8);
+    const int64_t warps = (spans + rounds - 1) / rounds;
+    return static_cast<unsigned>((warps + 7) / 8);
+#else
+    const int64_t want = (spans + 7) / 8;
     return static_cast<unsigned>(want < cap ? want : cap);
+#endif
   };
 #define SBC_NARROW(NB_, V_)                                                                                  \
   k_narrow<WS, WD, CH, NB_, V_><<<grid(k_narrow<WS, WD, CH, NB_, V_>), 256, 0, s>>>(d, pb, n)
