@@ -37,3 +37,29 @@ def test_reference_arm_prints_one_contract_line():
 def test_latency_config_has_no_cpu_arm():
     line = _run("--impl", "reference", "--config", "latency")
     assert line["impl"] == "reference" and line["unavailable"]
+
+
+def test_rank_to_gpu_map_alternates_host_bridge_halves():
+    import importlib.util
+
+    spec = importlib.util.spec_from_file_location("bench_mod", ROOT / "bench.py")
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    halves = [bench.device_map("halves", r, 4, 8) for r in range(4)]
+    assert halves == [0, 4, 1, 5]
+    assert [bench.device_map("halves", r, 2, 8) for r in range(2)] == [0, 4]
+    assert [bench.device_map("halves", r, 8, 8) for r in range(8)] == list(range(8))  # every GPU in use
+    assert [bench.device_map("identity", r, 4, 8) for r in range(4)] == [0, 1, 2, 3]
+    assert bench.device_map("halves", 0, 1, 1) == 0
+
+
+def test_job_clock_record_is_the_slowest_gpu_with_every_reason():
+    import importlib.util
+
+    spec = importlib.util.spec_from_file_location("bench_mod", ROOT / "bench.py")
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    merged = bench._merge_clocks([{"sm_mhz": 1965.0, "sm_max_mhz": 1965.0, "reasons": []},
+                                  {"sm_mhz": 1800.0, "sm_max_mhz": 1965.0, "reasons": ["sw_power_cap"]}])
+    assert merged["sm_mhz"] == 1800.0 and merged["sm_max_mhz"] == 1965.0
+    assert merged["reasons"] == ["sw_power_cap"] and len(merged["per_gpu"]) == 2
