@@ -342,10 +342,14 @@ class PeerShardedFetch:
     Ordering: per matrix, one 4-byte NCCL all-reduce (on the caller's stream)
     after this rank's copy says every shard of the matrix has landed; the
     kernels follow it on that stream. Each rank enters an all-reduce only
-    after all its earlier kernels, so the next copy into a buffer (two layers
-    later, with two buffers) waits for the all-reduce of the layer in between,
-    by which every rank had finished reading it. No kernel waits on another
-    GPU.
+    after all its earlier kernels, so once any all-reduce entered after the
+    previous reader of a shard buffer has completed, every rank has finished
+    reading that buffer. A copy into a buffer therefore waits for the first
+    all-reduce of the earliest layer fetched after the buffer's previous use
+    (with ``buffers`` buffers used in turn: the layer ``buffers - 1`` back),
+    not for the latest all-reduce of its own matrix; more buffers let a
+    rank's copy engine run further ahead of the slowest rank. No kernel waits
+    on another GPU.
     """
 
     def __init__(self, resources, device_index, world, rank, shapes, *, weights=None, group=None, buffers=2):
@@ -387,8 +391,9 @@ class PeerShardedFetch:
         self.copy_stream = torch.cuda.Stream(dev)
         self._flag = torch.zeros(1, dtype=torch.int32, device=dev)
         self._landed = [[torch.cuda.Event() for _ in shapes] for _ in range(buffers)]
-        # per matrix: the caller-stream event after its latest all-reduce
-        self._last = [None for _ in shapes]
+        self._fetches = 0                    # layers fetched so far (host or preloaded)
+        self._last_use = [-1] * buffers      # per buffer: the fetch that last read it
+        self._fenced = {}                    # host fetch -> caller event after its first all-reduce
 
     def shard(self, parity, m):
         """(row_begin, row_end, device tensor view) of this rank's shard."""
@@ -411,15 +416,27 @@ class PeerShardedFetch:
         import torch.distributed as dist
 
         caller = torch.cuda.current_stream(self.device)
+        fetch, previous = self._fetches, self._last_use[parity]
+        self._fetches += 1
+        self._last_use[parity] = fetch
+        if host_mats is not None and previous >= 0:
+            # Every rank has finished the previous readers of this buffer once
+            # an all-reduce entered after them completed.
+            later = [f for f in self._fenced if f > previous]
+            if later:
+                self.copy_stream.wait_event(self._fenced[min(later)])
+            else:  # none since (preloaded layers were read): synchronize the ranks now
+                if self.world > 1:
+                    dist.all_reduce(self._flag, group=self.group, async_op=True).wait()
+                fence = torch.cuda.Event()
+                fence.record(caller)
+                self.copy_stream.wait_event(fence)
+        oldest = min(u for u in self._last_use if u >= 0)
+        self._fenced = {f: e for f, e in self._fenced.items() if f > oldest}  # no longer needed
         for m, (tmpl, out) in enumerate(zip(templates, outputs)):
             in_f = self.shapes[m][1]
             if host_mats is not None:
                 b0, b1, view = self.shard(parity, m)
-                # The previous layer's all-reduce of this matrix was entered by
-                # every rank after all its earlier kernels, including those
-                # that read this buffer two layers ago.
-                if self._last[m] is not None:
-                    self.copy_stream.wait_event(self._last[m])
                 with torch.cuda.stream(self.copy_stream):
                     view.copy_(host_mats[m].reshape(-1)[b0 * in_f:b1 * in_f], non_blocking=True)
                     self._landed[parity][m].record(self.copy_stream)
@@ -427,9 +444,10 @@ class PeerShardedFetch:
                 if self.world > 1:
                     work = dist.all_reduce(self._flag, group=self.group, async_op=True)
                     work.wait()  # the caller stream waits: all shards of matrix m are in HBM
-                ev = torch.cuda.Event()
-                ev.record(caller)
-                self._last[m] = ev
+                if m == 0:
+                    fence = torch.cuda.Event()
+                    fence.record(caller)
+                    self._fenced[fetch] = fence
             # one call (one tile launch where the shapes allow) reads every shard
             pyreloc.execute_source_shards(tmpl, [self.bases[j] + self.offsets[j][parity][m] for j in range(self.world)],
                                           self.bounds[m], out.data_ptr(), device=self.device, resources=self.res,
