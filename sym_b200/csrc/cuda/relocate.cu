@@ -1630,8 +1630,223 @@ __global__ void __launch_bounds__(KTmaThreads, SBC_TMA_CTAS_PER_SM) k_tma_tile(c
 }
 
 // ---------------------------------------------------------------------------
+// Tall int8 tiles: 128 A cells x 128 source rows per tile (16 KB boxes), so
+// every destination row segment a tile writes is 128 f16 = 256 bytes. The
+// 32-bit tile kernel, which writes 256-byte segments, reaches ~0.96 of the
+// copy peak where the 64-row int8 tile (128-byte segments) stays at ~0.77.
+//
+// The box is the same 3-D view with y = 16 groups of 8 rows: source row
+// 8y + z lands at shared slot 16z + y (128 bytes each, 128-byte swizzle).
+// Consumer thread (ag, c), ag and c in 0..15, owns destination rows
+// a0 + 8ag + i (i < 8) and columns b0 + 8c + j (j < 8): it reads the 8 bytes
+// at column 8ag of source rows 8c + j (slots 16j + c). Lanes are laid out so
+// that each half-warp covers c mod 8 and ag mod 2 once: its sixteen 8-byte
+// reads hit 32 distinct banks; each store instruction of a warp writes two
+// destination rows x 256 contiguous bytes. Producer, barriers, bounded waits,
+// fault word and the test hook are those of k_tma_tile.
+// ---------------------------------------------------------------------------
+
+#ifndef SBC_TMA_TALL_STAGES
+#define SBC_TMA_TALL_STAGES 5
+#endif
+constexpr int KTallStages = SBC_TMA_TALL_STAGES;
+constexpr int KTallTileBytes = 128 * 128;
+
+template <int CHAIN, int CH_ON>
+__global__ void __launch_bounds__(KTmaThreads, SBC_TMA_CTAS_PER_SM) k_tma_tall(const __grid_constant__ TmaSources srcs,
+                                                             const __grid_constant__ sbc_relocate d, TileOrder ord,
+                                                             uint32_t tiles, TmaCtl ctl) {
+  constexpr int TA = 128, TB = 128, VD = 8, GR = 8;
+  extern __shared__ __align__(1024) uint8_t dyn[];
+  __shared__ __align__(8) uint64_t full[KTallStages], empty[KTallStages];
+  __shared__ __align__(16) float s_scale[KTallStages][TB];
+  __shared__ __align__(16) int32_t s_zp[KTallStages][TB];
+  __shared__ int timed_out;
+  uint8_t *stage0 = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(dyn) + 1023) & ~uintptr_t(1023));
+  const int t = threadIdx.x;
+  const sbc_stage &s = d.stages[0];
+  const uint32_t G = gridDim.x;
+
+  if (t == 0) {
+    for (int i = 0; i < KTallStages; ++i) {
+      mbar_init(&full[i], 32);
+      mbar_init(&empty[i], KTmaConsumers / 32);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    timed_out = 0;
+  }
+  __syncthreads(); // the only CTA-wide barrier
+  auto fail = [&]() {
+    if (atomicExch(&timed_out, 1) == 0 && d.fault) {
+      *reinterpret_cast<volatile int32_t *>(d.fault) = 2;
+      __threadfence_system();
+    }
+  };
+  auto drain = [&](uint32_t lo, uint32_t hi) {
+    for (uint32_t q = lo; q < hi && blockIdx.x + q * G < tiles; ++q)
+      mbar_wait(&full[q % KTallStages], (q / KTallStages) & 1, ctl.wait_ns);
+  };
+
+  if (t >= KTmaConsumers) { // ---- producer warp
+    const int lane = t - KTmaConsumers;
+    if (lane < srcs.n)
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&srcs.map[lane])) : "memory");
+    uint32_t k = 0;
+    for (;; ++k) {
+      const uint32_t job = blockIdx.x + k * G;
+      if (job >= tiles)
+        break;
+      const int st = k % KTallStages;
+      if (k >= KTallStages && !mbar_wait(&empty[st], (k / KTallStages - 1) & 1, ctl.wait_ns)) {
+        fail();
+        drain(k - KTallStages, k);
+        return;
+      }
+      if (job == ctl.withhold_job)
+        continue; // test hook: no copy and no arrival for this tile
+      uint32_t ta, tb;
+      tile_of(job, ord, ta, tb);
+      if constexpr (CH_ON == 2) {
+#pragma unroll
+        for (int h = 0; h < TB / 32; ++h) {
+          int64_t ch = d.box_lo[1] + static_cast<int64_t>(tb) * TB + lane + 32 * h;
+          if (ch >= s.channel_length)
+            ch = 0;
+          cp_async4(&s_scale[st][param_slot(lane + 32 * h)], s.param + ch);
+          if (s.zp_mode == 2)
+            cp_async4(&s_zp[st][param_slot(lane + 32 * h)], s.zero_point + ch);
+        }
+      }
+      if (lane == 0) {
+        int j = 0;
+        while (j + 1 < srcs.n && tb >= srcs.tb_first[j + 1])
+          ++j;
+        if constexpr (CH_ON == 2)
+          mbar_expect_tx_only(&full[st], KTallTileBytes);
+        else
+          mbar_expect_tx(&full[st], KTallTileBytes);
+        tma_load_3d(stage0 + st * KTallTileBytes, &srcs.map[j], static_cast<int32_t>(ta * TA),
+                    static_cast<int32_t>((tb - srcs.tb_first[j]) * (TB / GR)), 0, &full[st]);
+      }
+      if constexpr (CH_ON == 2)
+        cp_async_arrive(&full[st]);
+      else if (lane != 0)
+        mbar_arrive(&full[st]);
+    }
+    if constexpr (CH_ON == 2)
+      drain(k > KTallStages ? k - KTallStages : 0, k);
+    return;
+  }
+
+  // ---- consumer warps
+  const int lane = t & 31;
+  const int c = (lane & 7) | (((lane >> 4) & 1) << 3);  // 0..15
+  const int ag = 2 * (t >> 5) + ((lane >> 3) & 1);      // 0..15
+  const int64_t Da = d.dst_strides[0], DaB = Da * 2;
+  uint8_t *const dst0 = static_cast<uint8_t *>(d.dst) - d.dst_offset * 2;
+  const float bias_all = 8388736.0f + static_cast<float>(s.zp_mode == 1 ? s.zero_point[0] : 0);
+  float ps[VD], bias[VD];
+  if constexpr (CH_ON == 0) {
+#pragma unroll
+    for (int j = 0; j < VD; ++j) {
+      ps[j] = s.param[0];
+      bias[j] = bias_all;
+    }
+  }
+  for (uint32_t k = 0;; ++k) {
+    const uint32_t job = blockIdx.x + k * G;
+    if (job >= tiles)
+      break;
+    const int st = k % KTallStages;
+    if (!mbar_wait(&full[st], (k / KTallStages) & 1, ctl.wait_ns)) {
+      fail();
+      if (t == 0)
+        drain(k, k + KTallStages);
+      return;
+    }
+    uint32_t ta, tb;
+    tile_of(job, ord, ta, tb);
+    bool ok = true;
+    if constexpr (CH_ON == 2) {
+      const int lo = param_slot(c * VD), hi = param_slot(c * VD + 4);
+      const float4 s0 = *reinterpret_cast<const float4 *>(&s_scale[st][lo]);
+      const float4 s1 = *reinterpret_cast<const float4 *>(&s_scale[st][hi]);
+      ps[0] = s0.x, ps[1] = s0.y, ps[2] = s0.z, ps[3] = s0.w, ps[4] = s1.x, ps[5] = s1.y, ps[6] = s1.z, ps[7] = s1.w;
+      if (s.zp_mode == 2) {
+        const int4 z0 = *reinterpret_cast<const int4 *>(&s_zp[st][lo]);
+        const int4 z1 = *reinterpret_cast<const int4 *>(&s_zp[st][hi]);
+        const int z[VD] = {z0.x, z0.y, z0.z, z0.w, z1.x, z1.y, z1.z, z1.w};
+#pragma unroll
+        for (int j = 0; j < VD; ++j)
+          bias[j] = 8388736.0f + static_cast<float>(z[j]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < VD; ++j)
+          bias[j] = bias_all;
+      }
+      ok = d.box_lo[1] + static_cast<int64_t>(tb) * TB + (TB - 1) < s.channel_length;
+    }
+    const int64_t a0 = d.box_lo[0] + static_cast<int64_t>(ta) * TA;
+    const int64_t b0 = d.box_lo[1] + static_cast<int64_t>(tb) * TB;
+    const uint8_t *sp = stage0 + st * KTallTileBytes;
+    // bytes 8ag..8ag+7 of source rows 8c + j (slot 16j + c; slot mod 8 = c mod 8)
+    uint2 w[VD];
+    const int chunk = ((ag >> 1) ^ (c & 7)) << 4, half = (ag & 1) << 3;
+#pragma unroll
+    for (int j = 0; j < VD; ++j)
+      w[j] = *reinterpret_cast<const uint2 *>(sp + (16 * j + c) * 128 + chunk + half);
+    __syncwarp();
+    if (lane == 0)
+      mbar_arrive(&empty[st]); // this warp is done with the stage
+#pragma unroll
+    for (int j = 0; j < VD; ++j) {
+      w[j].x ^= 0x80808080u;
+      w[j].y ^= 0x80808080u;
+    }
+    uint8_t *dp = dst0 + (a0 * Da + b0) * 2 + static_cast<int64_t>(8 * ag) * DaB + c * 16;
+#pragma unroll
+    for (int i = 0; i < VD; ++i, dp += DaB) {
+      if constexpr (CH_ON == 1) {
+        int64_t ch = a0 + 8 * ag + i;
+        if (ch >= s.channel_length) {
+          ok = false;
+          ch = 0;
+        }
+        const float sc = s.param[ch], bi = 8388736.0f + static_cast<float>(zp_of(s, ch));
+#pragma unroll
+        for (int j = 0; j < VD; ++j) {
+          ps[j] = sc;
+          bias[j] = bi;
+        }
+      }
+      uint4 out;
+      uint32_t *u = reinterpret_cast<uint32_t *>(&out);
+#pragma unroll
+      for (int j = 0; j < VD; j += 2) {
+        const uint32_t wa = i < 4 ? w[j].x : w[j].y, wb = i < 4 ? w[j + 1].x : w[j + 1].y;
+        const float2 x = make_float2(__int_as_float(__byte_perm(wa, 0x4B000000u, 0x7650 + (i & 3))),
+                                     __int_as_float(__byte_perm(wb, 0x4B000000u, 0x7650 + (i & 3))));
+        const float2 f = __fmul2_rn(__fadd2_rn(x, make_float2(-bias[j], -bias[j + 1])),
+                                    make_float2(ps[j], ps[j + 1]));
+        if constexpr (CHAIN == CH_DQ_BF16) {
+          const __nv_bfloat162 h = __floats2bfloat162_rn(f.x, f.y);
+          u[j / 2] = *reinterpret_cast<const uint32_t *>(&h);
+        } else {
+          const __half2 h = __floats2half2_rn(f.x, f.y);
+          u[j / 2] = *reinterpret_cast<const uint32_t *>(&h);
+        }
+      }
+      tma_out_store(reinterpret_cast<uint4 *>(dp), out);
+    }
+    if (!ok)
+      flag(d);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Fill
 // ---------------------------------------------------------------------------
+
 
 template <int W>
 __global__ void __launch_bounds__(256) k_fill(void *dst, int64_t count, uint64_t bits) {
@@ -1802,6 +2017,19 @@ bool tma_enabled() {
   return on;
 }
 
+#ifndef SBC_TMA_TALL_DEFAULT
+#define SBC_TMA_TALL_DEFAULT 0
+#endif
+/// Whether int8 tiles of 128 source rows (k_tma_tall) are used where the
+/// shapes allow (SYM_B200_TMA_TALL=0/1; default SBC_TMA_TALL_DEFAULT).
+bool tma_tall_enabled() {
+  static const bool on = [] {
+    const char *v = std::getenv("SYM_B200_TMA_TALL");
+    return v ? v[0] != '0' : SBC_TMA_TALL_DEFAULT != 0;
+  }();
+  return on;
+}
+
 /// log2 of the column-block group of k_tma_tile's job order (SYM_B200_TMA_GROUP,
 /// 0..6; default 3).
 uint32_t tma_group_log2() {
@@ -1833,15 +2061,16 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 /// gr*pitch), z = row in group (stride pitch); box (128 / ws) x (64 / gr) x gr
 /// (64 rows) with the 128-byte swizzle. False when the driver rejects the
 /// description (the caller then uses a SIMT tile kernel).
-bool encode_rows3d(CUtensorMap *map, const void *base, int ws, int64_t cols, int64_t rows, int64_t pitch, int gr) {
+bool encode_rows3d(CUtensorMap *map, const void *base, int ws, int64_t cols, int64_t rows, int64_t pitch, int gr,
+                   int tile_rows = 64) {
   PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
   if (!enc || reinterpret_cast<uintptr_t>(base) % 16 || pitch % 16 || rows % gr || (ws != 1 && ws != 4) ||
-      (gr != 4 && gr != 8))
+      (gr != 4 && gr != 8) || (tile_rows != 64 && tile_rows != 128))
     return false;
   const cuuint64_t dims[3] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows / gr),
                               static_cast<cuuint64_t>(gr)};
   const cuuint64_t strides[2] = {static_cast<cuuint64_t>(pitch * gr), static_cast<cuuint64_t>(pitch)};
-  const cuuint32_t box[3] = {static_cast<cuuint32_t>(128 / ws), static_cast<cuuint32_t>(64 / gr),
+  const cuuint32_t box[3] = {static_cast<cuuint32_t>(128 / ws), static_cast<cuuint32_t>(tile_rows / gr),
                              static_cast<cuuint32_t>(gr)};
   const cuuint32_t estr[3] = {1, 1, 1};
   const CUresult r = enc(map, ws == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT32, 3,
@@ -2079,21 +2308,26 @@ int launch_tma(const sbc_relocate &d, int chain, int ch_on, const void *const *b
       (ext_a / tma_ta) * (ext_b / 64) >= (int64_t(1) << 31))
     return SBC_EUNSUPPORTED;
   const int group = tma_32 && chain == CH_COPY ? 4 : 8; // rows per view group, as the kernel's GR
+  // int8 sources whose blocks are all whole 128-row tiles take the tall tile
+  bool tall = tma_s8 && tma_tall_enabled() && ext_b % 128 == 0;
+  for (int j = 0; j < n && tall; ++j)
+    tall = rows[j] > 0 && rows[j] % 128 == 0;
+  const int64_t tb_rows = tall ? 128 : 64;
   TmaSources srcs{};
   srcs.n = n;
   int64_t covered = 0;
   for (int j = 0; j < n; ++j) {
     if (rows[j] <= 0 || rows[j] % 64)
       return SBC_EUNSUPPORTED;
-    srcs.tb_first[j] = static_cast<uint32_t>(covered / 64);
+    srcs.tb_first[j] = static_cast<uint32_t>(covered / tb_rows);
     if (!encode_rows3d(&srcs.map[j], bases[j], d.src_width, ext_a, rows[j], d.src_strides[1] * d.src_width,
-                       group))
+                       group, static_cast<int>(tb_rows)))
       return SBC_EUNSUPPORTED;
     covered += rows[j];
   }
   if (covered != ext_b)
     return SBC_EUNSUPPORTED;
-  const int64_t tiles_b = ext_b / 64, tiles = (ext_a / tma_ta) * tiles_b;
+  const int64_t tiles_b = ext_b / tb_rows, tiles = (ext_a / tma_ta) * tiles_b;
   srcs.tb_first[n] = static_cast<uint32_t>(tiles_b);
   const int64_t cap = static_cast<int64_t>(sm_count()) * SBC_TMA_CTAS_PER_SM;
   const unsigned blocks = static_cast<unsigned>(tiles < cap ? tiles : cap);
@@ -2102,7 +2336,7 @@ int launch_tma(const sbc_relocate &d, int chain, int ch_on, const void *const *b
   while (ord.lg > 0 && (ext_a / tma_ta) % (int64_t(1) << ord.lg))
     --ord.lg;
   ord.group = make_fastdiv(static_cast<uint32_t>(tiles_b << ord.lg));
-  const size_t smem = KStages * KTmaTileBytes + 1024;
+  const size_t smem = (tall ? KTallStages * KTallTileBytes : KStages * KTmaTileBytes) + 1024;
   const uint32_t nt = static_cast<uint32_t>(tiles);
   TmaCtl ctl;
   ctl.wait_ns = g_wait_ns.load(std::memory_order_relaxed);
@@ -2116,12 +2350,21 @@ int launch_tma(const sbc_relocate &d, int chain, int ch_on, const void *const *b
   (cudaFuncSetAttribute(k_tma_tile<WS_, CH_, ON_>, cudaFuncAttributeMaxDynamicSharedMemorySize,                    \
                         static_cast<int>(smem)),                                                                 \
    k_tma_tile<WS_, CH_, ON_><<<blocks, KTmaThreads, smem, st>>>(srcs, d, ord, nt, ctl))
-  if (tma_32)
+#define SBC_TALL(CH_, ON_)                                                                                     \
+  (cudaFuncSetAttribute(k_tma_tall<CH_, ON_>, cudaFuncAttributeMaxDynamicSharedMemorySize,                        \
+                        static_cast<int>(smem)),                                                                 \
+   k_tma_tall<CH_, ON_><<<blocks, KTmaThreads, smem, st>>>(srcs, d, ord, nt, ctl))
+  if (tall && chain == CH_DQ_F16)
+    ch_on == 0 ? SBC_TALL(CH_DQ_F16, 0) : ch_on == 1 ? SBC_TALL(CH_DQ_F16, 1) : SBC_TALL(CH_DQ_F16, 2);
+  else if (tall)
+    ch_on == 0 ? SBC_TALL(CH_DQ_BF16, 0) : ch_on == 1 ? SBC_TALL(CH_DQ_BF16, 1) : SBC_TALL(CH_DQ_BF16, 2);
+  else if (tma_32)
     chain == CH_COPY ? SBC_TMA(4, CH_COPY, 0) : chain == CH_F16 ? SBC_TMA(4, CH_F16, 0) : SBC_TMA(4, CH_BF16, 0);
   else if (chain == CH_DQ_F16)
     ch_on == 0 ? SBC_TMA(1, CH_DQ_F16, 0) : ch_on == 1 ? SBC_TMA(1, CH_DQ_F16, 1) : SBC_TMA(1, CH_DQ_F16, 2);
   else
     ch_on == 0 ? SBC_TMA(1, CH_DQ_BF16, 0) : ch_on == 1 ? SBC_TMA(1, CH_DQ_BF16, 1) : SBC_TMA(1, CH_DQ_BF16, 2);
+#undef SBC_TALL
 #undef SBC_TMA
   g_wait_launches.fetch_add(1, std::memory_order_relaxed);
   return launched(cudaSuccess);
