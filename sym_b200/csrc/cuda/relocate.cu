@@ -1646,8 +1646,11 @@ __global__ void __launch_bounds__(KTmaThreads, SBC_TMA_CTAS_PER_SM) k_tma_tile(c
 // fault word and the test hook are those of k_tma_tile.
 // ---------------------------------------------------------------------------
 
+// Ring depth of k_tma_tall (16 KB stages, 2 CTAs per SM). Gate matrix
+// [28672, 8192] per launch: 4 stages 0.1275 ms, 5 stages 0.1285 ms, 6 stages
+// 0.1292 ms; the 64-row k_tma_tile on the same box 0.1417-0.1434 ms.
 #ifndef SBC_TMA_TALL_STAGES
-#define SBC_TMA_TALL_STAGES 5
+#define SBC_TMA_TALL_STAGES 4
 #endif
 constexpr int KTallStages = SBC_TMA_TALL_STAGES;
 constexpr int KTallTileBytes = 128 * 128;
@@ -2018,7 +2021,7 @@ bool tma_enabled() {
 }
 
 #ifndef SBC_TMA_TALL_DEFAULT
-#define SBC_TMA_TALL_DEFAULT 0
+#define SBC_TMA_TALL_DEFAULT 1
 #endif
 /// Whether int8 tiles of 128 source rows (k_tma_tall) are used where the
 /// shapes allow (SYM_B200_TMA_TALL=0/1; default SBC_TMA_TALL_DEFAULT).

@@ -46,6 +46,16 @@ constexpr size_t kNone = SIZE_MAX;
 constexpr size_t kDefaultChunkBytes = size_t(8) << 20;
 constexpr size_t kMaxChunkBytes = size_t(64) << 20;
 
+/// Rows per chunk rounded down to whole tiles: multiples of 128 rows (the
+/// tall int8 tiles) when at least 128, else of 64, else unchanged.
+int64_t wholeTileRows(int64_t rows) {
+  if (rows >= 128)
+    return rows - rows % 128;
+  if (rows >= 64)
+    return rows - rows % 64;
+  return rows;
+}
+
 } // namespace
 
 namespace {
@@ -752,10 +762,10 @@ std::optional<TransferError> runH2D(const Lowered &l, CudaBackend &b, const void
       return *e;
     target = std::get<size_t>(t);
     rowsPer = std::max<int64_t>(1, static_cast<int64_t>(target) / rowBytes);
-    // Chunk boundaries on a multiple of 64 rows keep every chunk's
-    // destination box 16-byte aligned and made of whole kernel tiles.
-    if (rowsPer >= 64)
-      rowsPer -= rowsPer % 64;
+    // Chunk boundaries on a multiple of 128 (else 64) rows keep every
+    // chunk's destination box 16-byte aligned and made of whole kernel tiles
+    // (128 rows: the tall int8 tiles).
+    rowsPer = wholeTileRows(rowsPer);
     if (!b.ensureRing(slots, static_cast<size_t>(rowsPer * rowBytes)))
       return terr("backend_failure", b.error());
   }
@@ -882,8 +892,7 @@ std::optional<TransferError> runH2DStatic(const Lowered &l, const void *hsrc, vo
       return terr("invalid_options", "one source row of " + std::to_string(rowBytes) +
                                          " bytes exceeds the static scratch's " + std::to_string(slotBytes) +
                                          "-byte staging slot");
-    if (rowsPer >= 64)
-      rowsPer -= rowsPer % 64;
+    rowsPer = wholeTileRows(rowsPer);
     for (int64_t r0 = lo; r0 < lo + E; r0 += rowsPer) {
       const int64_t r1 = std::min(r0 + rowsPer, lo + E);
       const int64_t v0 = r0 - lo, v1 = r1 - lo;

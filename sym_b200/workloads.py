@@ -309,15 +309,18 @@ class ShardedLayerFetch:
         return handles
 
 
-def weighted_row_bounds(rows: int, weights, align: int = 64):
+def weighted_row_bounds(rows: int, weights, align=(128, 64)):
     """Split ``rows`` into contiguous per-rank ranges proportional to
     ``weights`` (e.g. each rank's measured concurrent host-to-device
-    bandwidth), on multiples of ``align`` rows where the extent allows.
-    Returns ``[b_0 = 0, b_1, ..., b_N = rows]``."""
+    bandwidth), on multiples of the first of ``align`` that the extent allows
+    (128-row shards let every shard use the tall int8 tiles; 64 rows is the
+    smaller tile), else of single rows. Returns ``[b_0 = 0, b_1, ..., b_N =
+    rows]``."""
     n = len(weights)
     if n == 0 or any(w <= 0 for w in weights):
         raise ValueError("weights must be positive")
-    unit = align if rows % align == 0 and rows // align >= n else 1
+    aligns = (align,) if isinstance(align, int) else tuple(align)
+    unit = next((a for a in aligns if rows % a == 0 and rows // a >= n), 1)
     units = rows // unit
     total = float(sum(weights))
     bounds, acc = [0], 0.0
