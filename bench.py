@@ -74,10 +74,16 @@ LLAMA7B = [("q", 4096, 4096), ("k", 4096, 4096), ("v", 4096, 4096), ("o", 4096, 
 # --config -> (matrix shapes, layers per step, workload name)
 MODELS = {"c5": (LLAMA70B, LAYERS, "llama70b_int8_fetch"), "c4": (LLAMA7B, 32, "llama7b_int8_fetch")}
 # DRAM bytes (read + write) per element of the gate launch, from one ncu
-# capture of `bench.py --kernel-case`: 235.3 MB + 412.7 MB over 28672 x 8192
-# elements. Writes sit below the algorithmic 2 B/element because the last
-# dirty lines are still in L2 when the kernel ends.
-GATE_DRAM_BYTES_PER_ELEM = (235.25888e6 + 412.66816e6) / (28672 * 8192)
+# capture of `bench.py --kernel-case` (k_tma_tall): 235.2 MB + 411.9 MB over
+# 28672 x 8192 elements. Writes sit below the algorithmic 2 B/element because
+# the last dirty lines are still in L2 when the kernel ends.
+GATE_DRAM_BYTES_PER_ELEM = (235.207168e6 + 411.922944e6) / (28672 * 8192)
+
+
+def int8_tile_kernel():
+    """Name of the TMA kernel that moves int8 weight matrices whose source
+    rows are whole 128-row tiles (the library's SYM_B200_TMA_TALL switch)."""
+    return "k_tma_tile" if os.environ.get("SYM_B200_TMA_TALL", "1")[:1] == "0" else "k_tma_tall"
 
 
 def _peaks():
@@ -240,27 +246,29 @@ def pinned_h2d_gbs(torch, device, nbytes=256 << 20, reps=10, d2h=False):
     return best
 
 
-def sustained_h2d_gbs(torch, device, barrier, nbytes=512 << 20, reps=4):
+def sustained_h2d_gbs(torch, device, barrier, hosts, reps=2):
     """Sustained pinned H2D GB/s of this GPU while every rank copies at once:
-    ``reps`` back-to-back copies of ``nbytes`` (2 GiB by default), started
-    together after a barrier. The job's host-to-device bound is the sum over
-    ranks."""
-    host = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
-    gpu = torch.empty(nbytes, dtype=torch.uint8, device=device)
+    the workload's own pinned host buffers (one layer's matrices, so the same
+    memory and NUMA placement as the timed copies) copied ``reps`` times back
+    to back into one device scratch buffer, started together after a
+    barrier. The job's host-to-device bound is the sum over ranks."""
+    flat = [h.reshape(-1).view(torch.uint8) for h in hosts]
+    gpu = torch.empty(max(f.numel() for f in flat), dtype=torch.uint8, device=device)
     s = torch.cuda.Stream(device)
     with torch.cuda.stream(s):
-        gpu.copy_(host, non_blocking=True)
+        gpu[:flat[0].numel()].copy_(flat[0], non_blocking=True)
     s.synchronize()
     barrier()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(s):
         a.record(s)
         for _ in range(reps):
-            gpu.copy_(host, non_blocking=True)
+            for f in flat:
+                gpu[:f.numel()].copy_(f, non_blocking=True)
         b.record(s)
     b.synchronize()
-    rate = nbytes * reps / (a.elapsed_time(b) * 1e-3) / 1e9
-    del host, gpu
+    rate = sum(f.numel() for f in flat) * reps / (a.elapsed_time(b) * 1e-3) / 1e9
+    del gpu
     return rate
 
 
@@ -347,9 +355,13 @@ def run_ours(args):
 
     sample = torch.empty(32, dtype=torch.float16).pin_memory()
     # Host-to-device bandwidth: this GPU alone (best of 10 256 MiB copies) and
-    # sustained while every rank copies 2 GiB at once (the job's bound).
+    # sustained while every rank copies one layer's host buffers twice at once
+    # (the job's bound; taken again after the timed regions, the higher of the
+    # two is the ceiling, since the box's host bandwidth is shared with other
+    # jobs and drifts).
     alone = pinned_h2d_gbs(torch, dev)
-    concurrent = sustained_h2d_gbs(torch, dev, barrier)
+    layer_hosts = [m["host"] for m in distinct[0]]
+    concurrent = sustained_h2d_gbs(torch, dev, barrier, layer_hosts)
     rates = gather(concurrent)
     peer = world > 1 and args.multi == "peer"
     weights = rates if (peer and args.balance) else None
@@ -439,6 +451,8 @@ def run_ours(args):
     ck = clocks.stop()
     launches_value = l1 - l0
     clock_records = gather(ck)
+    rates_pre = rates
+    rates = [max(x, y) for x, y in zip(rates_pre, gather(sustained_h2d_gbs(torch, dev, barrier, layer_hosts)))]
 
     # Output check: the last layer the e2e region assembled, on every rank.
     last = (n_layers - 1) % len(distinct)
@@ -537,7 +551,8 @@ def run_ours(args):
                    "l2": "inputs larger than L2 (855 MB int8 per layer)",
                    "value_timing": "CUDA events on the caller stream around the steps, max over ranks"},
         "gbs_per_gpu": gbs_job / world, "gbs_job": gbs_job,
-        "pinned_h2d_sustained_gbs_per_rank": rates, "pinned_h2d_aggregate_gbs": aggregate_ceiling,
+        "pinned_h2d_sustained_gbs_per_rank": rates, "pinned_h2d_sustained_gbs_per_rank_before": rates_pre,
+        "pinned_h2d_aggregate_gbs": aggregate_ceiling,
         "pinned_h2d_alone_gbs": alone,
         "pct_of_pinned_memcpy": 100.0 * gbs_job / aggregate_ceiling,
         "h2d_bound_layers_per_s": bound_layers,
@@ -553,7 +568,7 @@ def run_ours(args):
                                     + (" (peer shards read over NVLink)" if peer else "")},
         "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": hbm, "unit": "GB/s",
                      "frac": achieved_gbs / hbm, "traffic": traffic, "peak_source": peak_note,
-                     "kernel": f"k_tma_tile<int8, CH_DQ_F16, per-column scale> on gate [{gm['out']}, {gm['in']}]",
+                     "kernel": f"{int8_tile_kernel()}<int8, CH_DQ_F16, per-column scale> on gate [{gm['out']}, {gm['in']}]",
                      "bytes_per_launch": kernel_bytes, "launch_ms": kernel_s * 1e3,
                      "launch_ms_p95": kernel_p95_s * 1e3, "launches_timed": reps,
                      "bytes_per_launch_note": "int8 read + f16 write per element + 4 B per source-row scale",
@@ -703,11 +718,12 @@ def _dense(extents):
     return list(reversed(strides))
 
 
-def _config_case(name):
+def _config_case(name, c2_batch=64):
     """The plan, symbols, parameters, synthetic source (seed 0) and accounting
     of one config. `kernel_bytes` is the algorithmic HBM traffic of one
     device-resident execution; `unit_per_step` the amount of the config's
-    unit that one step moves."""
+    unit that one step moves. `c2_batch`: images of C2 (64 in the config;
+    other batches measure how the launch's fixed cost weighs with size)."""
     from helpers import encode, recipe_c1, recipe_c2, recipe_c3, recipe_tc
 
     rng = np.random.default_rng(0)
@@ -719,12 +735,13 @@ def _config_case(name):
                 "workload": "c1_transpose_f32", "shape": {"N": n}, "dtype": "f32",
                 "bytes_note": "4 B read + 4 B write per element"}
     if name == "c2":
-        src = rng.uniform(0.0, 1.0, (64, 3, 224, 224)).astype(np.float32)
-        px = 64 * 224 * 224
-        return {"blob": encode(recipe_c2()), "layout": False, "symbols": {}, "params": {}, "src": src,
-                "dst_bytes": px * 8, "kernel_bytes": 20 * px, "unit": "images/s", "unit_per_step": 64,
-                "workload": "c2_nchw_to_nhwc_pad4_f16", "shape": [64, 3, 224, 224], "dtype": "f32->f16",
-                "bytes_note": "12 B read + 8 B write per pixel"}
+        b = c2_batch
+        src = rng.uniform(0.0, 1.0, (b, 3, 224, 224)).astype(np.float32)
+        px = b * 224 * 224
+        return {"blob": encode(recipe_c2(b)), "layout": False, "symbols": {}, "params": {}, "src": src,
+                "dst_bytes": px * 8, "kernel_bytes": 20 * px, "unit": "images/s", "unit_per_step": b,
+                "workload": "c2_nchw_to_nhwc_pad4_f16" + ("" if b == 64 else f"_batch{b}"),
+                "shape": [b, 3, 224, 224], "dtype": "f32->f16", "bytes_note": "12 B read + 8 B write per pixel"}
     if name == "tc":  # the reference latency table's transpose + cast (rows of 1024 move intact)
         shape = (128, 128, 1024)
         n = 128 * 128 * 1024
@@ -777,7 +794,7 @@ def _cpu_config(case, threads, seconds=5.0):
     return case["unit_per_step"] / dt, dt, n
 
 
-def measure_config(name, steps, warmup, cpu_seconds=5.0, cpu_8_threads=True, device=0):
+def measure_config(name, steps, warmup, cpu_seconds=5.0, cpu_8_threads=True, device=0, c2_batch=64):
     """One config (C1, C2, C3q, C3d, tc, c3q_d2h) on one GPU: `value` with
     the source resident in HBM (the kernels alone, L2 flushed before each
     timed launch), `e2e` through the public dispatch API from pinned host
@@ -790,7 +807,7 @@ def measure_config(name, steps, warmup, cpu_seconds=5.0, cpu_8_threads=True, dev
     from sym_b200 import pyreloc
 
     threads = len(os.sched_getaffinity(0))
-    case = _config_case(name)
+    case = _config_case(name, c2_batch)
     dev = torch.device("cuda", device)
     torch.cuda.set_device(dev)
     res = pyreloc.DispatchResources()
@@ -836,6 +853,26 @@ def measure_config(name, steps, warmup, cpu_seconds=5.0, cpu_8_threads=True, dev
     launches = pyreloc.kernel_launches() - l0
     t_kernel = statistics.median(times)
     t_p95 = sorted(times)[int(0.95 * (len(times) - 1) + 0.5)]
+    # A plain device copy moving the same number of bytes (half read, half
+    # written), timed the same way: the fixed cost of a launch of this size
+    # (ramp-up, tail, events) that no transform kernel can beat.
+    half = max(16, case["kernel_bytes"] // 2 // 16 * 16)
+    cx = torch.empty(half, dtype=torch.uint8, device=dev).fill_(1)
+    cy = torch.empty_like(cx)
+    copy_times = []
+    for i in range(3 + steps):
+        flush.sum()
+        compute.wait_stream(torch.cuda.default_stream(dev))
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(compute):
+            a.record(compute)
+            cy.copy_(cx)
+            b.record(compute)
+        torch.cuda.synchronize(dev)
+        if i >= 3:
+            copy_times.append(a.elapsed_time(b) * 1e-3)
+    t_copy = statistics.median(copy_times)
+    del cx, cy
 
     # end to end through the public API: pinned host source -> device result
     # (d2h: device source -> pinned host result)
@@ -909,7 +946,10 @@ def measure_config(name, steps, warmup, cpu_seconds=5.0, cpu_8_threads=True, dev
                      "traffic": None, "peak_source": "measured" if peaks.get("hbm_gbs") else "fallback",
                      "kernel": desc.get("device_kernel"), "bytes_per_launch": case["kernel_bytes"],
                      "launches_per_execution": launches / max(1, steps),
-                     "bytes_per_launch_note": case["bytes_note"]},
+                     "bytes_per_launch_note": case["bytes_note"],
+                     "copy_same_bytes": {"ms": t_copy * 1e3, "frac": 2 * half / t_copy / 1e9 / hbm,
+                                         "note": "torch device copy of the same byte count (half read, half "
+                                                 "written), L2 flushed and event-timed the same way"}},
         "gpu_launches": int(launches), "clocks": ck,
     }
     if cpu_rate is not None:
@@ -930,7 +970,7 @@ def run_config(args):
 
     if args.impl == "reference":
         threads = len(os.sched_getaffinity(0))
-        case = _config_case(args.config)
+        case = _config_case(args.config, args.c2_batch)
         if not ref.available():
             print(json.dumps({"impl": "reference", "unavailable": "reference runtime (oracle/_ref) not built"}))
             return 0
@@ -945,7 +985,7 @@ def run_config(args):
                           "e2e": {"value": rate, "unit": case["unit"], "h2d_bytes_per_step": 0,
                                   "d2h_bytes_per_step": 0}}))
         return 0
-    print(json.dumps(measure_config(args.config, args.steps, args.warmup)))
+    print(json.dumps(measure_config(args.config, args.steps, args.warmup, c2_batch=args.c2_batch)))
     return 0
 
 
@@ -1015,7 +1055,7 @@ def measure_c4(steps=2, warmup=3, cpu_seconds=3.0):
     layer_bytes = sum(o * i for _, o, i in LLAMA7B)
     line = {"workload": "llama7b_int8_fetch", "value": 32 * steps / t, "unit": "layers/s",
             "gbs": layer_bytes * 32 * steps / t / 1e9,
-            "roofline": {"kernel": "k_tma_tile on gate [11008, 4096]", "achieved": kbytes / tk / 1e9, "peak": hbm,
+            "roofline": {"kernel": f"{int8_tile_kernel()} on gate [11008, 4096]", "achieved": kbytes / tk / 1e9, "peak": hbm,
                          "frac": kbytes / tk / 1e9 / hbm, "launch_ms": tk * 1e3, "unit": "GB/s"}}
     if ref.available():
         threads = len(os.sched_getaffinity(0))
@@ -1046,6 +1086,7 @@ def run_extras():
             line = measure_config(name, steps=10, warmup=3, cpu_seconds=2.0, cpu_8_threads=False)
             out[name] = {"workload": line["config"]["workload"], "value": line["value"], "unit": line["unit"],
                          "kernel_frac": line["roofline"]["frac"], "kernel": line["roofline"]["kernel"],
+                         "copy_frac_same_bytes": line["roofline"]["copy_same_bytes"]["frac"],
                          "e2e": line["e2e"]["value"],
                          "e2e_pct_of_pinned_memcpy": line["e2e"]["pct_of_pinned_memcpy"],
                          "cpu_baseline": (line.get("cpu_baseline") or {}).get("value"),
@@ -1175,6 +1216,8 @@ def run_latency(args):
 
 def main():
     parser = argparse.ArgumentParser()
+    parser.add_argument("--c2-batch", type=int, default=64,
+                        help="images of --config c2 (64 in the config; other sizes show the launch's fixed cost)")
     parser.add_argument("--config", default="c5",
                         choices=["c1", "c2", "c3q", "c3d", "c3q_d2h", "c4", "c5", "tc", "latency"],
                         help="c5 (default): the headline Llama-70B fetch; c4: Llama-7B, 32 layers; "

@@ -1847,162 +1847,6 @@ __global__ void __launch_bounds__(KTmaThreads, SBC_TMA_CTAS_PER_SM) k_tma_tall(c
 }
 
 // ---------------------------------------------------------------------------
-// Bulk-staged narrow planes (k_narrow_bulk): k_narrow's work, with the source
-// planes moved by the SM's bulk-copy unit instead of by thread loads. A chunk
-// is KNarrowItems consecutive items of one batch; each of its NB planes is one
-// contiguous run of KNarrowItems * 16 bytes, fetched by one 1-D
-// cp.async.bulk (no multicast) into a stage of a shared-memory ring (pad
-// planes are not read). The grid is persistent: CTA b takes chunks b, b + G,
-// b + 2G, ... Lane 0 of warp 8 produces; consumer thread i (warps 0-7) reads
-// item i of each chunk from shared memory (NB 16-byte reads; a warp's read is
-// 512 contiguous bytes) and stores its VA x NB result cells with k_narrow's
-// packed conversion and streaming stores. The bytes in flight per SM are the
-// ring's, not what the registers hold (k_narrow keeps its loads in registers
-// and runs out of them at two spans per lane). Barriers, bounded waits, the
-// fault word and the withheld-job test hook are those of k_tma_tile.
-// ---------------------------------------------------------------------------
-
-// Ring depth and resident CTAs per SM of k_narrow_bulk (compile-time tuning points).
-#ifndef SBC_NARROW_STAGES
-#define SBC_NARROW_STAGES 4
-#endif
-#ifndef SBC_NARROW_CTAS_PER_SM
-#define SBC_NARROW_CTAS_PER_SM 2
-#endif
-constexpr int KNarrowStages = SBC_NARROW_STAGES;
-constexpr int KNarrowItems = KTmaConsumers;              // items per chunk: one per consumer thread
-constexpr uint32_t KNarrowPlaneBytes = KNarrowItems * 16; // one plane of a chunk
-
-/// 1-D bulk copy global -> this CTA's shared memory, completing on `bar`
-/// (both addresses 16-byte aligned, `bytes` a multiple of 16).
-__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                   smem_addr(dst)),
-               "l"(__cvta_generic_to_global(src)), "r"(bytes), "r"(smem_addr(bar))
-               : "memory");
-}
-
-template <int WS, int WD, int CHAIN, int NB>
-__global__ void __launch_bounds__(KTmaThreads, SBC_NARROW_CTAS_PER_SM)
-    k_narrow_bulk(const __grid_constant__ sbc_relocate d, FastDiv chunks_per_batch, uint32_t chunks, TmaCtl ctl) {
-  constexpr int VA = 16 / WS;
-  constexpr uint32_t StageBytes = NB * KNarrowPlaneBytes;
-  extern __shared__ __align__(1024) uint8_t dyn[]; // the declaration the TMA kernels share
-  __shared__ __align__(8) uint64_t full[KNarrowStages], empty[KNarrowStages];
-  __shared__ int timed_out;
-  uint8_t *stage0 = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(dyn) + 127) & ~uintptr_t(127));
-  const int t = threadIdx.x;
-  const uint32_t G = gridDim.x;
-  const int ax_a = d.rank - 2, ax_b = d.rank - 1;
-  const int64_t Sb = d.src_strides[ax_b];
-  const int64_t lo_b = d.pad_lo[ax_b], hi_b = d.pad_lo[ax_b] + d.extents[ax_b];
-  const int64_t b0 = d.box_lo[ax_b];
-  bool valid[NB];
-  uint32_t bytes = 0; // per chunk: the valid planes
-#pragma unroll
-  for (int j = 0; j < NB; ++j) {
-    valid[j] = b0 + j >= lo_b && b0 + j < hi_b;
-    bytes += valid[j] ? KNarrowPlaneBytes : 0;
-  }
-  // element offsets of chunk q's first source cell (plane b0) and first destination cell
-  auto bases = [&](uint32_t q, int64_t &sbase, int64_t &dbase) {
-    const uint32_t n = d.rank == 3 ? fdiv(q, chunks_per_batch) : 0;
-    const int64_t a =
-        d.box_lo[ax_a] + static_cast<int64_t>(q - n * chunks_per_batch.d) * (KNarrowItems * VA);
-    sbase = (a - d.pad_lo[ax_a]) - d.src_offset + (b0 - lo_b) * Sb;
-    dbase = a * NB + b0 - d.dst_offset; // dst_strides[ax_a] == NB (host-checked)
-    if (d.rank == 3) {
-      sbase += (d.box_lo[0] + n - d.pad_lo[0]) * d.src_strides[0];
-      dbase += (d.box_lo[0] + n) * d.dst_strides[0];
-    }
-  };
-
-  if (t == 0) {
-    for (int i = 0; i < KNarrowStages; ++i) {
-      mbar_init(&full[i], 1);
-      mbar_init(&empty[i], KTmaConsumers / 32);
-    }
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    timed_out = 0;
-  }
-  __syncthreads(); // the only CTA-wide barrier
-  auto fail = [&]() {
-    if (atomicExch(&timed_out, 1) == 0 && d.fault) {
-      *reinterpret_cast<volatile int32_t *>(d.fault) = 2;
-      __threadfence_system();
-    }
-  };
-  // Bounded wait for the copies of local chunks [lo, hi) (issued, maybe in flight).
-  auto drain = [&](uint32_t lo, uint32_t hi) {
-    for (uint32_t k = lo; k < hi && blockIdx.x + k * G < chunks; ++k)
-      mbar_wait(&full[k % KNarrowStages], (k / KNarrowStages) & 1, ctl.wait_ns);
-  };
-
-  if (t >= KTmaConsumers) { // ---- producer: one thread
-    if (t != KTmaConsumers)
-      return;
-    const uint8_t *src = static_cast<const uint8_t *>(d.src);
-    for (uint32_t k = 0;; ++k) {
-      const uint32_t q = blockIdx.x + k * G;
-      if (q >= chunks)
-        break;
-      const int st = k % KNarrowStages;
-      if (k >= KNarrowStages && !mbar_wait(&empty[st], (k / KNarrowStages - 1) & 1, ctl.wait_ns)) {
-        fail();
-        drain(k - KNarrowStages, k);
-        return;
-      }
-      if (q == ctl.withhold_job)
-        continue; // test hook: no copy and no arrival, so this chunk's waits run out
-      int64_t sbase, dbase;
-      bases(q, sbase, dbase);
-      mbar_expect_tx(&full[st], bytes); // the one arrival, with the chunk's byte count
-      uint8_t *sp = stage0 + st * StageBytes;
-#pragma unroll
-      for (int j = 0; j < NB; ++j)
-        if (valid[j])
-          bulk_load(sp + j * KNarrowPlaneBytes, src + (sbase + j * Sb) * WS, KNarrowPlaneBytes, &full[st]);
-    }
-    return;
-  }
-
-  // ---- consumer warps
-  uint8_t *dst = static_cast<uint8_t *>(d.dst);
-  float p0 = 0.0f;
-  int32_t zp0 = 0;
-  if constexpr (CHAIN == CH_Q || CHAIN == CH_DQ) {
-    p0 = d.stages[0].param[0];
-    zp0 = zp_of(d.stages[0], 0);
-  }
-  const uint32_t fill = static_cast<uint32_t>(static_cast<typename Word<WD>::T>(d.fill_bits));
-  for (uint32_t k = 0;; ++k) {
-    const uint32_t q = blockIdx.x + k * G;
-    if (q >= chunks)
-      break;
-    const int st = k % KNarrowStages;
-    if (!mbar_wait(&full[st], (k / KNarrowStages) & 1, ctl.wait_ns)) {
-      fail();
-      if (t == 0) // the producer cannot pass chunk k + KNarrowStages - 1 before this warp releases chunk k
-        drain(k, k + KNarrowStages);
-      return;
-    }
-    const uint8_t *sp = stage0 + st * StageBytes + t * 16;
-    uint4 in[NB] = {};
-#pragma unroll
-    for (int j = 0; j < NB; ++j)
-      if (valid[j])
-        in[j] = *reinterpret_cast<const uint4 *>(sp + j * KNarrowPlaneBytes);
-    __syncwarp();
-    if ((t & 31) == 0)
-      mbar_arrive(&empty[st]); // this warp is done with the stage
-    int64_t sbase, dbase;
-    bases(q, sbase, dbase);
-    narrow_item<WS, WD, CHAIN, NB>(in, valid, dst + (dbase + static_cast<int64_t>(t) * VA * NB) * WD, fill, p0,
-                                   zp0);
-  }
-}
-
-// ---------------------------------------------------------------------------
 // Fill
 // ---------------------------------------------------------------------------
 
@@ -2189,19 +2033,6 @@ bool tma_tall_enabled() {
   return on;
 }
 
-#ifndef SBC_NARROW_BULK_DEFAULT
-#define SBC_NARROW_BULK_DEFAULT 1
-#endif
-/// Whether narrow-plane boxes whose batches hold whole chunks take the
-/// bulk-staged kernel (SYM_B200_NARROW_BULK=0/1; default SBC_NARROW_BULK_DEFAULT).
-bool narrow_bulk_enabled() {
-  static const bool on = [] {
-    const char *v = std::getenv("SYM_B200_NARROW_BULK");
-    return v ? v[0] != '0' : SBC_NARROW_BULK_DEFAULT != 0;
-  }();
-  return on;
-}
-
 /// Controls of one launch of a kernel with bounded waits: the current time
 /// limit, and the withheld job if the test hook armed one (it arms the next
 /// such launch only).
@@ -2354,28 +2185,6 @@ bool basic_ok(const sbc_relocate &d) {
 
 template <int WS, int WD, int CH>
 int launch_narrow(const sbc_relocate &d, int nb, int64_t per_batch, int64_t total, cudaStream_t s) {
-  if (narrow_bulk_enabled() && tma_enabled() && per_batch % KNarrowItems == 0) {
-    // bulk-staged chunks (every chunk lies in one batch)
-    const int64_t chunks = total / KNarrowItems;
-    const FastDiv cpb = make_fastdiv(static_cast<uint32_t>(per_batch / KNarrowItems));
-    const int64_t cap = static_cast<int64_t>(sm_count()) * SBC_NARROW_CTAS_PER_SM;
-    const unsigned blocks = static_cast<unsigned>(chunks < cap ? chunks : cap);
-    const size_t smem = static_cast<size_t>(nb) * KNarrowStages * KNarrowPlaneBytes + 128;
-    const TmaCtl ctl = bounded_ctl();
-    const uint32_t nc = static_cast<uint32_t>(chunks);
-#define SBC_NARROW_BULK(NB_)                                                                                   \
-  (cudaFuncSetAttribute(k_narrow_bulk<WS, WD, CH, NB_>, cudaFuncAttributeMaxDynamicSharedMemorySize,              \
-                        static_cast<int>(smem)),                                                                 \
-   k_narrow_bulk<WS, WD, CH, NB_><<<blocks, KTmaThreads, smem, s>>>(d, cpb, nc, ctl))
-    switch (nb) {
-    case 2: SBC_NARROW_BULK(2); break;
-    case 3: SBC_NARROW_BULK(3); break;
-    default: SBC_NARROW_BULK(4); break;
-    }
-#undef SBC_NARROW_BULK
-    g_wait_launches.fetch_add(1, std::memory_order_relaxed);
-    return launched(cudaSuccess);
-  }
   const FastDiv pb = make_fastdiv(static_cast<uint32_t>(per_batch));
   const uint32_t n = static_cast<uint32_t>(total);
   // Warp spans of 32 x V items when a batch holds whole spans (all of a

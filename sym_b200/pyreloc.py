@@ -597,8 +597,10 @@ class DispatchResources:
 
     def __del__(self):
         h = getattr(self, "handle", None)
-        if h and h.value and _native._lib is not None:
-            _native._lib.sb_resources_free(h)
+        native = globals().get("_native")  # None once the interpreter tears modules down
+        lib = getattr(native, "_lib", None)
+        if h and h.value and lib is not None:
+            lib.sb_resources_free(h)
             self.handle = ctypes.c_void_p()
 
 

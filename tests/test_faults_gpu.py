@@ -277,25 +277,3 @@ def test_bounded_wait_runs_out_in_the_allocation_free_entry_point(ref_lib):
     torch.cuda.synchronize()
     assert np.array_equal(out.cpu().numpy(), want)
 
-
-def test_bounded_wait_runs_out_in_the_narrow_plane_kernel(ref_lib):
-    """The bulk-staged narrow-plane kernel (NCHW f32 -> NHWC f16 with a pad
-    channel) has the same bounded waits: its second chunk is withheld."""
-    from helpers import recipe_c2
-    from sym_b200 import pyreloc
-
-    blob = encode(recipe_c2(2, 3, 32, 32))  # 1024 pixels per image: one chunk of 256 items each
-    x = np.random.default_rng(25).uniform(0, 1, 2 * 3 * 32 * 32).astype(np.float32)
-    bound = pyreloc.bind_typed(pyreloc.load_typed_plan(blob), {}, {})
-    want = ref_lib.TypedProgram(blob, {}, {}).execute(x.view(np.uint8))
-    res = pyreloc.DispatchResources()
-    call = _Call(bound, x)
-    req = call.request()
-    with pytest.raises(pyreloc.TransferError) as info:
-        _withheld(lambda: pyreloc.execute_dispatch(req, resources=res), job=1)
-    assert info.value.code == "backend_failure" and "bounded wait" in info.value.detail
-    assert not np.array_equal(call.result(), want)  # the withheld chunk was never written
-    call.out.fill_(0x5A)
-    pyreloc.execute_dispatch(call.request(), resources=res)
-    assert np.array_equal(call.result(), want)
-    res.close()

@@ -100,13 +100,12 @@ def _channels_last(batch, channels, hw, pad, op):
 
 @pytest.mark.parametrize("channels,pad", [(3, 1), (2, 0), (3, 0), (4, 0), (2, 2), (1, 1)])
 @pytest.mark.parametrize("op", ["copy", "f16", "bf16", "quantize"])
-@pytest.mark.parametrize("hw", [4096, 4352, 4093])
+@pytest.mark.parametrize("hw", [4096, 4093])
 def test_narrow_channels_last(channels, pad, op, hw):
     """Every narrow variant (2-4 destination channels, with and without pad
-    channels, copy / casts / per-tensor quantize) stays bit-identical to the
-    reference: 4096 pixels per image (whole chunks of 256 items: the
-    bulk-staged kernel), 4352 (warp spans of the register kernel) and 4093
-    (not a multiple of the vector width: the tiled fallback)."""
+    channels, copy / casts / per-tensor quantize) and a pixel count that is
+    not a multiple of the vector width (the tiled fallback) stay
+    bit-identical to the reference."""
     blob = encode(_channels_last(3, channels, hw, pad, op))
     x = _specials_f32(np.random.default_rng(5), 3 * channels * hw)
     for route in ("dma_ring", "zero_copy"):
