@@ -74,10 +74,11 @@ LLAMA7B = [("q", 4096, 4096), ("k", 4096, 4096), ("v", 4096, 4096), ("o", 4096, 
 # --config -> (matrix shapes, layers per step, workload name)
 MODELS = {"c5": (LLAMA70B, LAYERS, "llama70b_int8_fetch"), "c4": (LLAMA7B, 32, "llama7b_int8_fetch")}
 # DRAM bytes (read + write) per element of the gate launch, from one ncu
-# capture of `bench.py --kernel-case` (k_tma_tall): 235.2 MB + 411.9 MB over
-# 28672 x 8192 elements. Writes sit below the algorithmic 2 B/element because
-# the last dirty lines are still in L2 when the kernel ends.
-GATE_DRAM_BYTES_PER_ELEM = (235.207168e6 + 411.922944e6) / (28672 * 8192)
+# capture of `bench.py --kernel-case` (k_tma_tall, dynamic tile order):
+# 235.2 MB + 412.2 MB over 28672 x 8192 elements. Writes sit below the
+# algorithmic 2 B/element because the last dirty lines are still in L2 when
+# the kernel ends.
+GATE_DRAM_BYTES_PER_ELEM = (235.18976e6 + 412.207872e6) / (28672 * 8192)
 
 
 def int8_tile_kernel():

@@ -2301,7 +2301,8 @@ bool basic_ok(const sbc_relocate &d) {
 #define SBC_NARROW_BALANCED 0
 #endif
 // SBC_NARROW_CAP = 0: one span per warp (the hardware block scheduler hands
-// out the spans) instead of a grid capped at what stays resident.
+// out the spans) instead of a grid capped at what stays resident. Measured
+// on C2: capped 14.34 / 14.34 us, uncapped 14.34 / 14.83 us.
 #ifndef SBC_NARROW_CAP
 #define SBC_NARROW_CAP 1
 #endif
