@@ -63,3 +63,38 @@ def test_job_clock_record_is_the_slowest_gpu_with_every_reason():
                                   {"sm_mhz": 1800.0, "sm_max_mhz": 1965.0, "reasons": ["sw_power_cap"]}])
     assert merged["sm_mhz"] == 1800.0 and merged["sm_max_mhz"] == 1965.0
     assert merged["reasons"] == ["sw_power_cap"] and len(merged["per_gpu"]) == 2
+
+
+def _bench_module():
+    import importlib.util
+
+    spec = importlib.util.spec_from_file_location("bench_mod", ROOT / "bench.py")
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    return bench
+
+
+def test_c2_batch_scales_the_case_and_names_the_workload():
+    bench = _bench_module()
+    base = bench._config_case("c2")
+    small = bench._config_case("c2", c2_batch=4)
+    assert base["workload"] == "c2_nchw_to_nhwc_pad4_f16" and base["shape"] == [64, 3, 224, 224]
+    assert small["workload"] == "c2_nchw_to_nhwc_pad4_f16_batch4" and small["shape"] == [4, 3, 224, 224]
+    assert small["src"].shape == (4, 3, 224, 224) and small["unit_per_step"] == 4
+    assert small["kernel_bytes"] == 20 * 4 * 224 * 224 and small["dst_bytes"] == 8 * 4 * 224 * 224
+    assert base["kernel_bytes"] == 16 * small["kernel_bytes"]
+
+
+def test_reference_arm_takes_the_c2_batch():
+    line = _run("--impl", "reference", "--config", "c2", "--c2-batch", "2", "--steps", "3", "--warmup", "3")
+    if "unavailable" in line:
+        return
+    assert line["config"]["workload"].endswith("_batch2") and line["config"]["shape"][0] == 2
+
+
+def test_int8_tile_kernel_name_follows_the_library_switch(monkeypatch):
+    bench = _bench_module()
+    monkeypatch.delenv("SYM_B200_TMA_TALL", raising=False)
+    assert bench.int8_tile_kernel() == "k_tma_tall"
+    monkeypatch.setenv("SYM_B200_TMA_TALL", "0")
+    assert bench.int8_tile_kernel() == "k_tma_tile"
