@@ -364,11 +364,11 @@ def run_ours(args):
     layer_hosts = [m["host"] for m in distinct[0]]
     concurrent = sustained_h2d_gbs(torch, dev, barrier, layer_hosts)
     rates = gather(concurrent)
-    peer = world > 1 and args.multi == "peer"
+    peer = args.multi == "peer" and (world > 1 or args.n1_path == "peer")
     weights = rates if (peer and args.balance) else None
     if peer:
         fetcher = PeerShardedFetch(res, gpu_index, world, rank, [(m["out"], m["in"]) for m in distinct[0]],
-                                   weights=weights, buffers=len(distinct))
+                                   weights=weights, buffers=len(distinct), copy_chunk_bytes=args.peer_copy_chunk)
         for d, mats in enumerate(distinct):
             fetcher.preload(d, [m["host"] for m in mats])
         torch.cuda.synchronize(dev)
@@ -533,7 +533,9 @@ def run_ours(args):
     check["status"] = "match" if ok else "mismatch"
     extras = run_extras() if (world == 1 and args.extras) else None
     gbs_job = layer_src_bytes * layers_value / 1e9
-    if peer:
+    if peer and world == 1:
+        shard = "one shard per matrix: one DMA per matrix into HBM, then one tile launch (the N>1 fetch path)"
+    elif peer:
         shard = ("int8 source rows per rank (weighted by sustained concurrent H2D bandwidth)" if args.balance
                  else "int8 source rows per rank, equal") + "; every rank's kernels read all shards (peers' over " \
                                                            "NVLink, CUDA IPC)"
@@ -1238,6 +1240,12 @@ def main():
     parser.add_argument("--multi", default="peer", choices=["peer", "allgather"],
                         help="N>1: peer (int8 shards read over NVLink by every rank's kernel) or allgather "
                              "(f16 result rows all-gathered by NCCL)")
+    parser.add_argument("--peer-copy-chunk", type=int, default=0,
+                        help="peer fetch: copy each shard in pieces of about this many bytes (0: one copy per shard)")
+    parser.add_argument("--n1-path", default="peer", choices=["peer", "dispatch"],
+                        help="N=1 `value` path: peer (the same shard fetch as N>1, one shard per matrix: one DMA "
+                             "per matrix, then one tile launch) or dispatch (the chunked HBM ring of "
+                             "sb_execute_rows); `e2e` is the C-ABI dispatch call either way")
     parser.add_argument("--balance", type=int, default=1,
                         help="N>1 peer: size shards by each rank's sustained concurrent H2D bandwidth (1) or "
                              "equally (0)")

@@ -355,12 +355,14 @@ class PeerShardedFetch:
     on another GPU.
     """
 
-    def __init__(self, resources, device_index, world, rank, shapes, *, weights=None, group=None, buffers=2):
+    def __init__(self, resources, device_index, world, rank, shapes, *, weights=None, group=None, buffers=2,
+                 copy_chunk_bytes=0):
         import torch
         import torch.distributed as dist
 
         self.res, self.device, self.world, self.rank = resources, device_index, world, rank
         self.group, self.buffers = group, buffers
+        self.copy_chunk_bytes = int(copy_chunk_bytes)  # > 0: each shard copy in pieces of about this size
         weights = list(weights) if weights is not None else [1.0] * world
         self.bounds = [weighted_row_bounds(out_f, weights) for out_f, _ in shapes]  # per matrix
         self.shapes = list(shapes)
@@ -379,9 +381,12 @@ class PeerShardedFetch:
             sizes.append(max(off, 256))
         dev = torch.device("cuda", device_index)
         self.arena = torch.empty(sizes[rank], dtype=torch.uint8, device=dev)
-        handle = pyreloc.ipc_handle(self.arena.data_ptr())
-        handles = [None] * world
-        dist.all_gather_object(handles, handle, group=group)
+        if world > 1:
+            handle = pyreloc.ipc_handle(self.arena.data_ptr())
+            handles = [None] * world
+            dist.all_gather_object(handles, handle, group=group)
+        else:  # one rank (no process group needed): only its own arena
+            handles = [(None, 0)]
         self.bases = []
         self._mapped = []
         for j, (h, offset) in enumerate(handles):
@@ -407,9 +412,11 @@ class PeerShardedFetch:
 
     def preload(self, parity, host_mats):
         """Device-resident mode: copy this rank's rows of every matrix once."""
+        import torch
+
         for m, q in enumerate(host_mats):
             b0, b1, view = self.shard(parity, m)
-            view.copy_(q.reshape(-1)[b0 * self.shapes[m][1]:b1 * self.shapes[m][1]])
+            view.copy_(q.reshape(-1).view(torch.uint8)[b0 * self.shapes[m][1]:b1 * self.shapes[m][1]])
 
     def fetch(self, templates, outputs, parity, host_mats=None):
         """Enqueue one layer: ``templates[m]`` maps int8 ``[out, in]`` to the
@@ -440,8 +447,13 @@ class PeerShardedFetch:
             in_f = self.shapes[m][1]
             if host_mats is not None:
                 b0, b1, view = self.shard(parity, m)
+                # the bytes as they are (the arena is uint8): a same-dtype copy is one
+                # DMA, where int8 -> uint8 would add a conversion on the copy stream
+                src = host_mats[m].reshape(-1).view(torch.uint8)[b0 * in_f:b1 * in_f]
+                step = max(in_f, self.copy_chunk_bytes // in_f * in_f) if self.copy_chunk_bytes > 0 else src.numel()
                 with torch.cuda.stream(self.copy_stream):
-                    view.copy_(host_mats[m].reshape(-1)[b0 * in_f:b1 * in_f], non_blocking=True)
+                    for c0 in range(0, src.numel(), max(step, 1)):
+                        view[c0:c0 + step].copy_(src[c0:c0 + step], non_blocking=True)
                     self._landed[parity][m].record(self.copy_stream)
                 caller.wait_event(self._landed[parity][m])
                 if self.world > 1:
