@@ -400,13 +400,31 @@ def run_ours(args):
     def public_step():
         """One step through the public API, with the result read back."""
         if world == 1:
+            pending = []  # submitted layers, at most two in flight
             for l in range(n_layers):
+                views = []
                 for m, out in zip(distinct[l % len(distinct)], outs[l % 2]):
                     dv = pyreloc.BufferView(out.data_ptr(), out.numel() * 2, 0, [m["in"], m["out"]],
                                             [m["out"], 1], 2, "cuda", gpu_index)
+                    views.append((m, dv))
+                if args.e2e_api in ("submit", "group"):  # one transfer group per layer, one completion
+                    group = pyreloc.prepare_dispatch_group([(m["tmpl"], m["sv"], dv, "h2d") for m, dv in views])
+                    if args.e2e_api == "group":
+                        pyreloc.execute_dispatch_group(group, resources=res, caller_stream=cur.cuda_stream,
+                                                       chunk_size=args.chunk_bytes, n_buffers=args.ring_slots)
+                        continue
+                    if len(pending) == 2:
+                        pending.pop(0).wait()
+                    pending.append(pyreloc.submit_dispatch_group(group, resources=res, caller_stream=cur.cuda_stream,
+                                                                 chunk_size=args.chunk_bytes,
+                                                                 n_buffers=args.ring_slots))
+                    continue
+                for m, dv in views:  # one blocking dispatch per matrix
                     req = pyreloc.prepare_dispatch_from_template(m["tmpl"], m["sv"], dv)
                     pyreloc.execute_dispatch(req, resources=res, caller_stream=cur.cuda_stream,
                                              chunk_size=args.chunk_bytes, n_buffers=args.ring_slots)
+            for c in pending:
+                c.wait()
         else:
             step(True)
         sample.copy_(outs[(n_layers - 1) % 2][-1].view(-1)[:32], non_blocking=True)
@@ -562,7 +580,11 @@ def run_ours(args):
         "e2e": {"value": layers_e2e, "unit": "layers/s", "ms_per_step": 1e3 * t_e2e / args.steps,
                 "h2d_bytes_per_step": int(layer_src_bytes / world * n_layers),
                 "d2h_bytes_per_step": int(sample.numel() * 2),
-                "api": "pyreloc.execute_dispatch per matrix (sb_execute_dispatch)" if world == 1 else
+                "api": ({"submit": "pyreloc.submit_dispatch_group per layer (sb_submit_dispatch_group, two layers "
+                                   "in flight, each completion waited)",
+                         "group": "pyreloc.execute_dispatch_group per layer (sb_execute_dispatch_group)",
+                         "dispatch": "pyreloc.execute_dispatch per matrix (sb_execute_dispatch)"}[args.e2e_api])
+                       if world == 1 else
                        "workloads.PeerShardedFetch.fetch" if peer else "workloads.ShardedLayerFetch.fetch",
                 "timing": "host wall clock between synchronizations, max over ranks",
                 "pct_of_pinned_memcpy": 100.0 * layer_src_bytes * layers_e2e / 1e9 / aggregate_ceiling},
@@ -1242,6 +1264,9 @@ def main():
                              "(f16 result rows all-gathered by NCCL)")
     parser.add_argument("--peer-copy-chunk", type=int, default=0,
                         help="peer fetch: copy each shard in pieces of about this many bytes (0: one copy per shard)")
+    parser.add_argument("--e2e-api", default="submit", choices=["submit", "group", "dispatch"],
+                        help="N=1 e2e: one dispatch group per layer (7 matrices, one completion) submitted with two "
+                             "layers in flight, or executed blocking, or one blocking dispatch per matrix")
     parser.add_argument("--n1-path", default="peer", choices=["peer", "dispatch"],
                         help="N=1 `value` path: peer (the same shard fetch as N>1, one shard per matrix: one DMA "
                              "per matrix, then one tile launch) or dispatch (the chunked HBM ring of "
