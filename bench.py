@@ -931,7 +931,12 @@ def measure_config(name, steps, warmup, cpu_seconds=5.0, cpu_8_threads=True, dev
             return pyreloc.prepare_dispatch_from_template(tmpl, sv, dv)
 
     def e2e_step():
-        rep = pyreloc.execute_dispatch(request(), resources=res, caller_stream=cur.cuda_stream)
+        # host -> device: returns once enqueued (the caller stream is ordered
+        # after the work, so the readback below follows it), letting the host
+        # prepare the next call while this one runs; device -> host: blocking,
+        # the result is in host memory when it returns
+        rep = pyreloc.execute_dispatch(request(), resources=res, caller_stream=cur.cuda_stream,
+                                       async_completion=not d2h)
         if not d2h:
             sample.copy_(out[:4096], non_blocking=True)
         return rep
