@@ -931,12 +931,9 @@ def measure_config(name, steps, warmup, cpu_seconds=5.0, cpu_8_threads=True, dev
             return pyreloc.prepare_dispatch_from_template(tmpl, sv, dv)
 
     def e2e_step():
-        # host -> device: returns once enqueued (the caller stream is ordered
-        # after the work, so the readback below follows it), letting the host
-        # prepare the next call while this one runs; device -> host: blocking,
-        # the result is in host memory when it returns
-        rep = pyreloc.execute_dispatch(request(), resources=res, caller_stream=cur.cuda_stream,
-                                       async_completion=not d2h)
+        # one blocking call per step (returning asynchronously measured 1-2 %
+        # better on C1 / C2 and 3-4 % worse on C3q / C3d)
+        rep = pyreloc.execute_dispatch(request(), resources=res, caller_stream=cur.cuda_stream)
         if not d2h:
             sample.copy_(out[:4096], non_blocking=True)
         return rep
